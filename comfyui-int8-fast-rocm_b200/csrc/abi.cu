@@ -1,0 +1,339 @@
+// extern "C" entry points of libqlinear_b200.so: argument validation, error
+// reporting and dispatch to the kernel launchers.  Nothing here throws.
+#include <cstdint>
+#include <string>
+
+#include "../../include/qlinear_b200.h"
+#include "common.cuh"
+#include "internal.h"
+#include "rowquant.cuh"
+
+namespace qlin {
+
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return QLIN_ERR_CUDA;
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sms[kMaxDevices] = {0};
+int g_cc[kMaxDevices] = {0};
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return (d >= 0 && d < kMaxDevices) ? d : -1;
+}
+}  // namespace
+
+int device_sm_count() {
+  const int d = current_device();
+  if (d < 0) return 0;
+  if (!g_sms[d]) cudaDeviceGetAttribute(&g_sms[d], cudaDevAttrMultiProcessorCount, d);
+  return g_sms[d];
+}
+int device_cc() {
+  const int d = current_device();
+  if (d < 0) return 0;
+  if (!g_cc[d]) {
+    int ma = 0, mi = 0;
+    cudaDeviceGetAttribute(&ma, cudaDevAttrComputeCapabilityMajor, d);
+    cudaDeviceGetAttribute(&mi, cudaDevAttrComputeCapabilityMinor, d);
+    g_cc[d] = ma * 10 + mi;
+  }
+  return g_cc[d];
+}
+
+}  // namespace qlin
+
+using namespace qlin;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+int esize(int dt) { return dt == QLIN_F32 ? 4 : (dt == QLIN_I8 ? 1 : 2); }
+bool float_dt(int dt) { return dt == QLIN_BF16 || dt == QLIN_F16 || dt == QLIN_F32; }
+
+// ``clamp(min=1e-10)`` on a tensor of dtype dt compares with 1e-10 in dt.
+float clamp_min_for(int dt) {
+  if (dt == QLIN_BF16) return __bfloat162float(__float2bfloat16_rn(1e-10f));
+  if (dt == QLIN_F16) return __half2float(__float2half_rn(1e-10f));
+  return 1e-10f;
+}
+
+int check_device() {
+  const int cc = device_cc();
+  if (cc == 0) return fail(QLIN_ERR_NO_DEVICE, "no current CUDA device");
+  if (cc != 100)
+    return fail(QLIN_ERR_NO_DEVICE,
+                "kernels are built for sm_100a (B200); device has compute capability " + std::to_string(cc));
+  return QLIN_OK;
+}
+
+int check_rot(int kind, int group, int64_t K) {
+  if (kind == QLIN_ROT_NONE) return QLIN_OK;
+  if (kind != QLIN_ROT_REGULAR && kind != QLIN_ROT_SYLVESTER) return fail(QLIN_ERR_INVALID_ARG, "bad rot_kind");
+  if (group <= 0 || K % group != 0)
+    return fail(QLIN_ERR_INVALID_ARG,
+                "features " + std::to_string(K) + " not divisible by group_size " + std::to_string(group));
+  return QLIN_OK;
+}
+
+// Rows usable by the vectorised kernels: 16-element multiples, 16-byte aligned.
+bool rows_vec_ok(const void* x, int64_t K, int64_t ldx, int dt) {
+  return (K % 16 == 0) && aligned16(x) && ((ldx * esize(dt)) % 16 == 0);
+}
+
+int gemm_common_checks(const int8_t* a, const void* w, int64_t M, int64_t N, int64_t K, int kmul) {
+  if (M < 0 || N < 0 || K <= 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(QLIN_ERR_UNSUPPORTED, "dimension too large");
+  if (K % kmul) return fail(QLIN_ERR_ALIGNMENT, "K must be a multiple of " + std::to_string(kmul));
+  if (M == 0 || N == 0) return QLIN_OK;
+  if (!a || !w) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(a) || !aligned16(w)) return fail(QLIN_ERR_ALIGNMENT, "operands must be 16-byte aligned");
+  return check_device();
+}
+
+}  // namespace
+
+extern "C" {
+
+QLIN_API int qlin_version(void) { return 10000; }
+
+QLIN_API int qlin_set_device(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return QLIN_OK;
+}
+
+QLIN_API const char* qlin_last_error(void) { return t_last_error.c_str(); }
+
+QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits) {
+  if (!error_bits) return fail(QLIN_ERR_INVALID_ARG, "error_bits is null");
+  int rc = check_device();
+  if (rc) return rc;
+  return read_device_error(static_cast<cudaStream_t>(stream), error_bits);
+}
+
+QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
+                                 int rot_group, float rot_c, int8_t* q, float* scale, void* stream) {
+  if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = rows_vec_ok(x, K, ldx, x_dtype) && aligned16(q);
+  if (!vec) {
+    if (rot_kind != QLIN_ROT_NONE)
+      return fail(QLIN_ERR_ALIGNMENT, "rotation needs K % 16 == 0 and 16-byte aligned rows");
+    return launch_rowquant_generic(x_dtype, MODE_INT8, x, ldx, M, K, 0.0f, q, scale, s);
+  }
+  RowQuantLaunch L{x_dtype, x_dtype, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, MODE_INT8};
+  return launch_rowquant(L, x, ldx, M, K, rot_c, 0.0f, nullptr, 0, q, scale, nullptr, 0, s);
+}
+
+QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
+                                 int rot_group, float rot_c, int group, float clamp_min, int8_t* q, float* scale,
+                                 void* stream) {
+  if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
+  if (group != 0 && group != 128) return fail(QLIN_ERR_UNSUPPORTED, "int4 group must be 0 (per row) or 128");
+  if (group == 128 && K % 128) return fail(QLIN_ERR_INVALID_ARG, "K must be a multiple of 128 for group-128 int4");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = rows_vec_ok(x, K, ldx, x_dtype) && aligned16(q);
+  if (!vec) {
+    if (rot_kind != QLIN_ROT_NONE || group)
+      return fail(QLIN_ERR_ALIGNMENT, "rotation / grouping needs K % 16 == 0 and 16-byte aligned rows");
+    return launch_rowquant_generic(x_dtype, MODE_INT4_ROW, x, ldx, M, K, clamp_min, q, scale, s);
+  }
+  RowQuantLaunch L{x_dtype, x_dtype, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group,
+                   group ? MODE_INT4_G128 : MODE_INT4_ROW};
+  return launch_rowquant(L, x, ldx, M, K, rot_c, clamp_min, nullptr, 0, q, scale, nullptr, 0, s);
+}
+
+QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
+                         int rot_group, float rot_c, void* out, void* stream) {
+  if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
+  if (rot_kind == QLIN_ROT_NONE) return fail(QLIN_ERR_INVALID_ARG, "qlin_rotate needs a rotation");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (!rows_vec_ok(x, K, ldx, x_dtype) || !aligned16(out))
+    return fail(QLIN_ERR_ALIGNMENT, "rotation needs K % 16 == 0 and 16-byte aligned rows");
+  RowQuantLaunch L{x_dtype, x_dtype, rot_kind, rot_group, MODE_ROTATE};
+  return launch_rowquant(L, x, ldx, M, K, rot_c, 0.0f, nullptr, 0, nullptr, nullptr, out, 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                            int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
+                            int64_t K, void* stream) {
+  int rc = gemm_common_checks(a, w, M, N, K, 16);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_scale || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (wscale_mode != QLIN_WSCALE_ROW && wscale_mode != QLIN_WSCALE_TENSOR)
+    return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
+  return launch_gemm(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, false, a, w, a_scale,
+                     w_scale, bias, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c, int64_t M, int64_t N, int64_t K,
+                         void* stream) {
+  int rc = gemm_common_checks(a, w, M, N, K, 16);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!c) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  return launch_gemm(GEMM_I32, false, a, w, nullptr, nullptr, nullptr, c, QLIN_F32, M, N, K,
+                     static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_int4_mm(const int8_t* a, const int8_t* w_packed, int32_t* c, int64_t M, int64_t N, int64_t K,
+                          void* stream) {
+  int rc = gemm_common_checks(a, w_packed, M, N, K, 32);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!c) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  return launch_gemm(GEMM_I32, true, a, w_packed, nullptr, nullptr, nullptr, c, QLIN_F32, M, N, K,
+                     static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_gemm_w4a4(const int8_t* a, const float* a_scale, const int8_t* w_packed, const float* w_scale,
+                            const void* bias, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                            void* stream) {
+  int rc = gemm_common_checks(a, w_packed, M, N, K, 32);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_scale || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  return launch_gemm(GEMM_W4A4_ROW, true, a, w_packed, a_scale, w_scale, bias, out, out_dtype, M, N, K,
+                     static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_gemm_w4a8_g128(const int8_t* a, const float* a_scale, const int8_t* w_packed,
+                                 const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
+                                 int64_t M, int64_t N, int64_t K, void* stream) {
+  int rc = gemm_common_checks(a, w_packed, M, N, K, 128);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_scale || !w_gscale_bf16 || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  return launch_gemm_g128(false, a, a_scale, w_packed, w_gscale_bf16, bias, out, out_dtype, M, N, K,
+                          static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_gemm_w4a4_g128(const int8_t* a, const float* a_gscale, const int8_t* w_packed,
+                                 const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
+                                 int64_t M, int64_t N, int64_t K, void* stream) {
+  int rc = gemm_common_checks(a, w_packed, M, N, K, 128);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_gscale || !w_gscale_bf16 || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  return launch_gemm_g128(true, a, a_gscale, w_packed, w_gscale_bf16, bias, out, out_dtype, M, N, K,
+                          static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_quant_weight_int8(const void* w, int w_dtype, int64_t N, int64_t K, int rot_kind, int rot_group,
+                                    float rot_c, int8_t* q, float* scale, void* stream) {
+  if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(w_dtype)) return fail(QLIN_ERR_INVALID_ARG, "w_dtype must be BF16, F16 or F32");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!w || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (!rows_vec_ok(w, K, K, w_dtype) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "weights need K % 16 == 0 and 16-byte alignment");
+  RowQuantLaunch L{w_dtype, QLIN_F32, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, MODE_INT8};
+  return launch_rowquant(L, w, K, N, K, rot_c, 0.0f, nullptr, 0, q, scale, nullptr, 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_quant_weight_int4(const void* w, int w_dtype, int64_t N, int64_t K, int rot_kind, int rot_group,
+                                    float rot_c, int group, int8_t* packed, float* scale, void* stream) {
+  if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(w_dtype)) return fail(QLIN_ERR_INVALID_ARG, "w_dtype must be BF16, F16 or F32");
+  if (group != 0 && group != 128) return fail(QLIN_ERR_UNSUPPORTED, "int4 group must be 0 or 128");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!w || !packed || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (!rows_vec_ok(w, K, K, w_dtype) || (K % 32) || !aligned16(packed) || (group && K % 128))
+    return fail(QLIN_ERR_ALIGNMENT, "int4 weights need K % 32 == 0 (K % 128 for groups) and 16-byte alignment");
+  // group == 0: float32 math (quantize_convrot_w4a4_weight on a .float() weight);
+  // group == 128: the compute dtype is the weight dtype.
+  const int dt_q = group ? w_dtype : QLIN_F32;
+  const float cmin = group ? clamp_min_for(w_dtype) : 1e-10f;
+  RowQuantLaunch L{w_dtype, dt_q, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group,
+                   group ? MODE_INT4_G128 : MODE_INT4_ROW};
+  return launch_rowquant(L, w, K, N, K, rot_c, cmin, nullptr, 0, nullptr, scale, packed, 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
+                                    const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K, int8_t* q,
+                                    float* scale, void* stream) {
+  if (N < 0 || K < 0 || group_size <= 0 || K % group_size)
+    return fail(QLIN_ERR_INVALID_ARG, "bad shape / group_size");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!packed || !codebook || !s_channel || !s_rel_fp8 || !q || !scale)
+    return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if (K % 32 || !aligned16(packed) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "need K % 32 == 0 and 16-byte alignment");
+  return launch_requant_asym_w4a8(packed, codebook, s_channel, s_rel_fp8, group_size, N, K, q, scale,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_dequant_int8(const int8_t* q, const float* scale, int scale_mode, int64_t N, int64_t K,
+                               int rot_kind, int rot_group, float rot_c, float* out, void* stream) {
+  if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!q || !scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (K % 16 || !aligned16(q) || !aligned16(out))
+    return fail(QLIN_ERR_ALIGNMENT, "need K % 16 == 0 and 16-byte alignment");
+  RowQuantLaunch L{DT_I8, QLIN_F32, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, MODE_ROTATE};
+  return launch_rowquant(L, q, K, N, K, rot_c, 0.0f, scale, scale_mode == QLIN_WSCALE_ROW, nullptr, nullptr, out, 0,
+                         static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_requant_int8(const float* w, const float* scale, int scale_mode, int64_t N, int64_t K,
+                               int rot_kind, int rot_group, float rot_c, int round_mode, uint64_t seed, int8_t* q,
+                               void* stream) {
+  if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (round_mode != QLIN_ROUND_NEAREST && round_mode != QLIN_ROUND_STOCHASTIC)
+    return fail(QLIN_ERR_INVALID_ARG, "bad round_mode");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!w || !scale || !q) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (K % 16 || !aligned16(w) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "need K % 16 == 0 and 16-byte alignment");
+  RowQuantLaunch L{QLIN_F32, QLIN_F32, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group,
+                   round_mode == QLIN_ROUND_NEAREST ? MODE_REQUANT : MODE_REQUANT_SR};
+  return launch_rowquant(L, w, K, N, K, rot_c, 0.0f, scale, scale_mode == QLIN_WSCALE_ROW, q, nullptr, nullptr, seed,
+                         static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+// Host side of the tcgen05 GEMMs: TMA descriptors, tile configuration, launch.
+#include <mutex>
+
+#include "../../include/qlinear_b200.h"
+#include "gemm_i8.cuh"
+#include "internal.h"
+
+namespace qlin {
+namespace {
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled_t get_encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(ptr);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor map: `outer` rows of `inner` bytes, row pitch `pitch` bytes.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_inner,
+              uint32_t box_outer, CUtensorMapSwizzle swz) {
+  PFN_encodeTiled_t enc = get_encode_fn();
+  if (!enc) return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
+  return QLIN_OK;
+}
+
+template <int BN, int EPI, int OUT_DT, bool B_INT4>
+int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, B_INT4>;
+  auto kern = gemm_i8_kernel<BN, EPI, OUT_DT, B_INT4>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+  const int num_tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + BN - 1) / BN);
+  const int grid = num_tiles < p.num_sms ? num_tiles : p.num_sms;
+  kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return QLIN_OK;
+}
+
+template <int BN, bool B_INT4>
+int dispatch_epi(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                 cudaStream_t s) {
+  if (kind == GEMM_I32) return launch_cfg<BN, EPI_I32, DT_F32, B_INT4>(ta, tb, p, s);
+  if constexpr (!B_INT4) {
+    if (kind == GEMM_W8A8_ROW) {
+      if (out_dt == DT_BF16) return launch_cfg<BN, EPI_W8A8_ROW, DT_BF16, false>(ta, tb, p, s);
+      if (out_dt == DT_F16) return launch_cfg<BN, EPI_W8A8_ROW, DT_F16, false>(ta, tb, p, s);
+      if (out_dt == DT_F32) return launch_cfg<BN, EPI_W8A8_ROW, DT_F32, false>(ta, tb, p, s);
+    }
+    if (kind == GEMM_W8A8_TENSOR) {
+      if (out_dt == DT_BF16) return launch_cfg<BN, EPI_W8A8_TENSOR, DT_BF16, false>(ta, tb, p, s);
+      if (out_dt == DT_F16) return launch_cfg<BN, EPI_W8A8_TENSOR, DT_F16, false>(ta, tb, p, s);
+      if (out_dt == DT_F32) return launch_cfg<BN, EPI_W8A8_TENSOR, DT_F32, false>(ta, tb, p, s);
+    }
+  } else {
+    if (kind == GEMM_W4A4_ROW) {
+      if (out_dt == DT_BF16) return launch_cfg<BN, EPI_W4A4_ROW, DT_BF16, true>(ta, tb, p, s);
+      if (out_dt == DT_F16) return launch_cfg<BN, EPI_W4A4_ROW, DT_F16, true>(ta, tb, p, s);
+      if (out_dt == DT_F32) return launch_cfg<BN, EPI_W4A4_ROW, DT_F32, true>(ta, tb, p, s);
+    }
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported GEMM epilogue / output dtype");
+}
+
+}  // namespace
+
+int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
+                const float* w_scale, const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K,
+                cudaStream_t stream) {
+  if (M == 0 || N == 0) return QLIN_OK;
+  const int sms = device_sm_count();
+  if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  // Narrow outputs waste half a 256-wide tile; use 128 columns there.
+  const int BN = (N <= 128) ? 128 : 256;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (b_int4) {
+    rc = make_tmap(&tb, b, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), GEMM_BK / 2, (uint32_t)BN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (rc) return rc;
+  GemmParams p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.a_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = out;
+  p.ldo = N;
+  p.num_sms = sms;
+  if (b_int4) {
+    if (BN == 128) return dispatch_epi<128, true>(kind, out_dt, ta, tb, p, stream);
+    return dispatch_epi<256, true>(kind, out_dt, ta, tb, p, stream);
+  }
+  if (BN == 128) return dispatch_epi<128, false>(kind, out_dt, ta, tb, p, stream);
+  return dispatch_epi<256, false>(kind, out_dt, ta, tb, p, stream);
+}
+
+int read_device_error(cudaStream_t stream, uint32_t* bits) {
+  uint32_t h = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_error_bits, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "read error word");
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "sync");
+  const uint32_t zero = 0;
+  e = cudaMemcpyToSymbolAsync(g_error_bits, &zero, sizeof(uint32_t), 0, cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clear error word");
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "sync");
+  *bits = h;
+  return QLIN_OK;
+}
+
+}  // namespace qlin

@@ -1,0 +1,367 @@
+// Persistent warp-specialised int8 GEMM on the sm_100a 5th-generation tensor
+// cores: C[M,N] = A[M,K] . B[N,K]^T, int32 accumulation in tensor memory.
+//
+//   warp 0      TMA producer: A and B K-slabs (128 bytes of K per stage,
+//               128B-swizzled) into a STAGES-deep shared-memory ring;
+//               for packed-int4 B it loads the packed slab instead.
+//   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.kind::i8 (M=128,
+//               N=BN, K=32) x 4 per stage, commits free the ring slot and,
+//               at tile end, hand the accumulator to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld of the int32 tile (each warp owns one
+//               32-lane TMEM quarter), the reference's scale/bias/rounding
+//               sequence, stores to HBM.  Two TMEM accumulators let the
+//               epilogue of tile i overlap the MMAs of tile i+1.
+//   warps 6-9   (packed-int4 B only) nibble -> int8 unpack of the B slab
+//               into the swizzled operand layout the MMA reads.
+//
+// No TMA multicast is used anywhere (the same kernel runs in multi-GPU jobs).
+// Every pipeline wait is bounded: on timeout the kernel sets a device error
+// word, all roles leave their loops, TMEM is released and the kernel exits.
+#pragma once
+
+#include "common.cuh"
+
+namespace qlin {
+
+// Device error word (bit 0: a pipeline wait timed out).  Read and cleared by
+// qlin_device_error().  Defined here: gemm.cu is the only translation unit
+// that includes this header.
+__device__ uint32_t g_error_bits = 0;
+
+// Pipeline waits give up after this long and flag the failure.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Bounded wait on an mbarrier phase.  Returns false (and sets the device
+// error word and *abort) if the phase did not complete within the limit or
+// another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t iter = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++iter & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&g_error_bits, 1u);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+enum : int {
+  EPI_W8A8_ROW = 0,     // dt(dt(float(acc)*xs[m]*ws[n]) + bias[n])
+  EPI_W8A8_TENSOR = 1,  // dt(dt(float(acc)*(ws*xs[m])) + bias[n])
+  EPI_W4A4_ROW = 2,     // dt(float(acc)*xs[m]*ws[n] + float(bias[n]))
+  EPI_I32 = 3,          // raw int32
+};
+
+struct GemmParams {
+  int M, N, K;
+  const float* a_scale;  // [M]
+  const float* w_scale;  // [N] or [1]
+  const void* bias;      // [N] in the output dtype, or null
+  void* out;             // [M, N]
+  int64_t ldo;           // output row stride (elements)
+  int num_sms;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 128;  // bytes (= int8 elements) of K per stage
+
+template <int BN, bool B_INT4>
+struct GemmCfg {
+  static constexpr int STAGES = B_INT4 ? 3 : 4;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK;
+  static constexpr int B_BYTES = BN * GEMM_BK;
+  static constexpr int BP_BYTES = B_INT4 ? BN * (GEMM_BK / 2) : 0;  // packed staging
+  static constexpr int NUM_THREADS = B_INT4 ? 320 : 192;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  constexpr int GROUP_M = 8;
+  const int per_group = GROUP_M * num_n;
+  const int gid = tile / per_group;
+  const int first_m = gid * GROUP_M;
+  const int gsz = min(num_m - first_m, GROUP_M);
+  const int in_g = tile % per_group;
+  mb = first_m + in_g % gsz;
+  nb = in_g / gsz;
+}
+
+template <int DT>
+__device__ __forceinline__ void store_out_chunk(typename Elem<DT>::T* dst, const float (&y)[32], bool vec, int ncols) {
+  if (vec) {
+    if constexpr (DT == DT_F32) {
+      float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+    } else {
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        // values are already representable in DT: conversion is exact
+        if constexpr (DT == DT_BF16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols) dst[j] = Elem<DT>::from_f(y[j]);
+  }
+}
+
+// Unpack one packed-int4 K-slab (BN rows x 64 bytes, row-major, unswizzled)
+// into the 128B-swizzled int8 layout TMA would have produced for an int8
+// slab (16-byte chunk c of row r lands at chunk c ^ (r & 7)).
+template <int BN>
+__device__ __forceinline__ void unpack_int4_slab(const uint8_t* src, uint8_t* dst, int tid, int nthr) {
+  // each work item: one row, one 16-byte output chunk (= 8 packed bytes)
+  for (int item = tid; item < BN * 8; item += nthr) {
+    const int r = item >> 3;
+    const int c = item & 7;
+    const uint2 pk = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+    const uint32_t pw[2] = {pk.x, pk.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t v = pw[h];
+#pragma unroll
+      for (int b2 = 0; b2 < 2; ++b2) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const uint32_t nib = (v >> (4 * (4 * b2 + n))) & 0xFu;
+          const uint32_t sx = (nib ^ 0x8u) - 0x8u;  // sign-extend 4 -> 32 bits
+          word |= (sx & 0xFFu) << (8 * n);
+        }
+        o[2 * h + b2] = word;
+      }
+    }
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int BN, int EPI, int OUT_DT, bool B_INT4>
+__global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmParams p) {
+  using Cfg = GemmCfg<BN, B_INT4>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
+  uint8_t* sBP = sB + STAGES * Cfg::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBP + STAGES * Cfg::BP_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* conv = empty + STAGES;      // B unpacked and ready (B_INT4)
+  uint64_t* tfull = conv + STAGES;      // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 4);  // 4 converter warps
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // 4 epilogue warps
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + GEMM_BM - 1) / GEMM_BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
+          if constexpr (B_INT4) {
+            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::BP_BYTES);
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+            tma_load_2d(sBP + stage * Cfg::BP_BYTES, &tmB, &full[stage], kb * (GEMM_BK / 2), nb * BN);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) goto mma_done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if constexpr (B_INT4) {
+            if (!mbar_wait_bounded(&conv[stage], phase, abort_flag)) goto mma_done;
+          } else {
+            if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) goto mma_done;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 32; ++k) {
+            // advance 32 bytes of K inside the 128-byte swizzle atom
+            umma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  mma_done:;
+  } else if (warp < 6) {
+    // ---------------- epilogue ----------------
+    using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+    const int vec_n = out16 ? 8 : 4;
+    const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * GEMM_BM + row_in_tile;
+      const bool row_ok = row < p.M;
+      float xs = 0.0f;
+      if constexpr (EPI != EPI_I32) xs = row_ok ? __ldg(p.a_scale + row) : 0.0f;
+      float s_tensor = 0.0f;
+      if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + acc * BN + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        const int ncols = min(32, p.N - col0);
+        const bool full_chunk = (ncols == 32) && vec_ok;
+        if constexpr (EPI == EPI_I32) {
+          int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+          if (full_chunk) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              reinterpret_cast<int4*>(dst)[i] = make_int4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) dst[j] = (int32_t)r[j];
+          }
+        } else {
+          float y[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float f = __int2float_rn((int32_t)r[j]);  // res.float()
+            const int col = col0 + j;
+            const bool ok = j < ncols;
+            float v;
+            if constexpr (EPI == EPI_W8A8_TENSOR) {
+              v = EO::round(__fmul_rn(f, s_tensor));
+            } else {
+              const float ws = ok ? __ldg(p.w_scale + col) : 0.0f;
+              v = __fmul_rn(__fmul_rn(f, xs), ws);
+              if constexpr (EPI == EPI_W8A8_ROW) v = EO::round(v);
+            }
+            if (p.bias != nullptr) {
+              const float b = ok ? EO::to_f(reinterpret_cast<const typename EO::T*>(p.bias)[col]) : 0.0f;
+              v = __fadd_rn(v, b);
+            }
+            y[j] = EO::round(v);
+          }
+          auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
+          store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  } else if constexpr (B_INT4) {
+    // ---------------- int4 -> int8 converters (warps 6..9) ----------------
+    const int ctid = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
+        unpack_int4_slab<BN>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid, 128);
+        fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace qlin

@@ -1,0 +1,54 @@
+// Host-side declarations shared by the translation units of libqlinear_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace qlin {
+
+// thread-local last-error message behind qlin_last_error()
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Number of SMs of the current device (cached per device); 0 on failure.
+int device_sm_count();
+// Major*10+minor of the current device (cached); 0 on failure.
+int device_cc();
+
+struct RowQuantLaunch {
+  int dt_in;       // DT_BF16/F16/F32/I8
+  int dt_q;        // compute dtype of rotation + quantisation
+  int rot_kind;    // ROT_*
+  int rot_group;   // 0 when rot_kind == ROT_NONE
+  int mode;        // MODE_*
+};
+
+// Launch the row kernel family; returns a QLIN_* status.
+int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t M, int64_t K, float rot_c,
+                    float clamp_min, const float* in_scale, int in_scale_per_row, int8_t* q, float* scale,
+                    void* out, uint64_t seed, cudaStream_t stream);
+
+int launch_rowquant_generic(int dt, int mode, const void* x, int64_t ldx, int64_t M, int64_t K, float clamp_min,
+                            int8_t* q, float* scale, cudaStream_t stream);
+
+enum GemmKind { GEMM_W8A8_ROW = 0, GEMM_W8A8_TENSOR = 1, GEMM_W4A4_ROW = 2, GEMM_I32 = 3 };
+
+// Launch the tcgen05 GEMM; b_int4 selects packed-int4 B.
+int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
+                const float* w_scale, const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K,
+                cudaStream_t stream);
+
+int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
+                     const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
+                     int64_t K, cudaStream_t stream);
+
+int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
+                             const uint8_t* s_rel, int group_size, int64_t N, int64_t K, int8_t* q, float* scale,
+                             cudaStream_t stream);
+
+int read_device_error(cudaStream_t stream, uint32_t* bits);
+
+}  // namespace qlin

@@ -1,0 +1,178 @@
+// Instantiation and launch of the row-wise rotate/quantise kernel family.
+#include "../../include/qlinear_b200.h"
+#include "internal.h"
+#include "rowquant.cuh"
+
+namespace qlin {
+namespace {
+
+// Rotation shapes this build instantiates: none, regular 16/64/256,
+// Sylvester 32/128 (the sizes that are not powers of 4).
+enum RotCode { RC_NONE, RC_REG16, RC_REG64, RC_REG256, RC_SYL32, RC_SYL128, RC_BAD };
+
+RotCode rot_code(int kind, int group) {
+  if (kind == ROT_NONE) return RC_NONE;
+  if (kind == ROT_REGULAR) {
+    if (group == 16) return RC_REG16;
+    if (group == 64) return RC_REG64;
+    if (group == 256) return RC_REG256;
+  }
+  if (kind == ROT_SYLVESTER) {
+    if (group == 32) return RC_SYL32;
+    if (group == 128) return RC_SYL128;
+  }
+  return RC_BAD;
+}
+
+struct LaunchShape {
+  int chunks, tpr, rpc;
+  size_t smem;
+};
+
+template <int DT_IN, int DT_Q, int KIND, int R, int CHUNKS, int MODE>
+int launch_one(const RowQuantParams& p, const LaunchShape& s, cudaStream_t stream) {
+  auto kern = rowquant_kernel<DT_IN, DT_Q, KIND, R, CHUNKS, MODE>;
+  if (s.smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant)");
+  }
+  dim3 block(s.tpr, s.rpc);
+  dim3 grid((unsigned)((p.M + s.rpc - 1) / s.rpc));
+  kern<<<grid, block, s.smem, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rowquant launch");
+  return QLIN_OK;
+}
+
+template <int DT_IN, int DT_Q, int KIND, int R, int MODE>
+int by_chunks(const RowQuantParams& p, const LaunchShape& s, cudaStream_t stream) {
+  if (s.chunks == 1) return launch_one<DT_IN, DT_Q, KIND, R, 1, MODE>(p, s, stream);
+  if constexpr (DT_IN == DT_Q) {
+    if (s.chunks == 2) return launch_one<DT_IN, DT_Q, KIND, R, 2, MODE>(p, s, stream);
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "row length too large for this kernel configuration");
+}
+
+template <int DT_IN, int DT_Q, int MODE>
+int by_rot(RotCode rc, const RowQuantParams& p, const LaunchShape& s, cudaStream_t stream) {
+  switch (rc) {
+    case RC_NONE: return by_chunks<DT_IN, DT_Q, ROT_NONE, 1, MODE>(p, s, stream);
+    case RC_REG16: return by_chunks<DT_IN, DT_Q, ROT_REGULAR, 1, MODE>(p, s, stream);
+    case RC_REG64: return by_chunks<DT_IN, DT_Q, ROT_REGULAR, 4, MODE>(p, s, stream);
+    case RC_REG256: return by_chunks<DT_IN, DT_Q, ROT_REGULAR, 16, MODE>(p, s, stream);
+    case RC_SYL32: return by_chunks<DT_IN, DT_Q, ROT_SYLVESTER, 2, MODE>(p, s, stream);
+    case RC_SYL128: return by_chunks<DT_IN, DT_Q, ROT_SYLVESTER, 8, MODE>(p, s, stream);
+    default: return fail(QLIN_ERR_UNSUPPORTED, "unsupported rotation");
+  }
+}
+
+template <int DT_IN, int DT_Q>
+int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s, cudaStream_t stream) {
+  if constexpr (DT_IN == DT_Q) {
+    // activation modes (the compute dtype is the input dtype)
+    switch (mode) {
+      case MODE_INT8: return by_rot<DT_IN, DT_Q, MODE_INT8>(rc, p, s, stream);
+      case MODE_INT4_ROW: return by_rot<DT_IN, DT_Q, MODE_INT4_ROW>(rc, p, s, stream);
+      case MODE_INT4_G128: return by_rot<DT_IN, DT_Q, MODE_INT4_G128>(rc, p, s, stream);
+      case MODE_ROTATE: return by_rot<DT_IN, DT_Q, MODE_ROTATE>(rc, p, s, stream);
+      default: break;
+    }
+    if constexpr (DT_Q == DT_F32) {
+      if (mode == MODE_REQUANT) return by_rot<DT_IN, DT_Q, MODE_REQUANT>(rc, p, s, stream);
+      if (mode == MODE_REQUANT_SR) return by_rot<DT_IN, DT_Q, MODE_REQUANT_SR>(rc, p, s, stream);
+    }
+  } else if constexpr (DT_IN == DT_I8) {
+    if (mode == MODE_ROTATE) return by_rot<DT_IN, DT_Q, MODE_ROTATE>(rc, p, s, stream);
+  } else {
+    // weights held in bf16/f16, computed in float32 (w.float() first)
+    if (mode == MODE_INT8) return by_rot<DT_IN, DT_Q, MODE_INT8>(rc, p, s, stream);
+    if (mode == MODE_INT4_ROW) return by_rot<DT_IN, DT_Q, MODE_INT4_ROW>(rc, p, s, stream);
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported dtype/mode combination");
+}
+
+}  // namespace
+
+int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t M, int64_t K, float rot_c,
+                    float clamp_min, const float* in_scale, int in_scale_per_row, int8_t* q, float* scale,
+                    void* out, uint64_t seed, cudaStream_t stream) {
+  if (M == 0 || K == 0) return QLIN_OK;
+  RowQuantParams p;
+  p.x = x;
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.K = (int)K;
+  p.rot_c = rot_c;
+  p.clamp_min = clamp_min;
+  p.in_scale = in_scale;
+  p.in_scale_per_row = in_scale_per_row;
+  p.q = q;
+  p.scale = scale;
+  p.out = out;
+  p.seed = seed;
+
+  const RotCode rc = rot_code(L.rot_kind, L.rot_group);
+  if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
+
+  const int64_t nchunks = K / 16;
+  if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  LaunchShape s;
+  s.chunks = nchunks <= 1024 ? 1 : 2;
+  const int64_t per = (nchunks + s.chunks - 1) / s.chunks;
+  s.tpr = (int)(((per + 31) / 32) * 32);
+  s.rpc = 256 / s.tpr;
+  if (s.rpc < 1) s.rpc = 1;
+  if (s.rpc > 32) s.rpc = 32;
+  const bool staged = (rc == RC_REG64 || rc == RC_REG256 || rc == RC_SYL32 || rc == RC_SYL128);
+  s.smem = staged ? (size_t)(s.rpc * s.tpr / 32) * 512 * sizeof(float) : 0;
+
+  switch (L.dt_in) {
+    case DT_BF16:
+      if (L.dt_q == DT_BF16) return by_mode<DT_BF16, DT_BF16>(L.mode, rc, p, s, stream);
+      if (L.dt_q == DT_F32) return by_mode<DT_BF16, DT_F32>(L.mode, rc, p, s, stream);
+      break;
+    case DT_F16:
+      if (L.dt_q == DT_F16) return by_mode<DT_F16, DT_F16>(L.mode, rc, p, s, stream);
+      if (L.dt_q == DT_F32) return by_mode<DT_F16, DT_F32>(L.mode, rc, p, s, stream);
+      break;
+    case DT_F32:
+      if (L.dt_q == DT_F32) return by_mode<DT_F32, DT_F32>(L.mode, rc, p, s, stream);
+      break;
+    case DT_I8:
+      if (L.dt_q == DT_F32) return by_mode<DT_I8, DT_F32>(L.mode, rc, p, s, stream);
+      break;
+    default: break;
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported input/compute dtype pair");
+}
+
+// Unaligned rows (no rotation): generic kernel.
+int launch_rowquant_generic(int dt, int mode, const void* x, int64_t ldx, int64_t M, int64_t K, float clamp_min,
+                            int8_t* q, float* scale, cudaStream_t stream) {
+  if (M == 0) return QLIN_OK;
+  RowQuantParams p{};
+  p.x = x;
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.K = (int)K;
+  p.clamp_min = clamp_min;
+  p.q = q;
+  p.scale = scale;
+  dim3 grid((unsigned)M), block(256);
+#define QLIN_GEN(DTV, MV) rowquant_generic_kernel<DTV, MV><<<grid, block, 0, stream>>>(p)
+  if (mode == MODE_INT8) {
+    if (dt == DT_BF16) QLIN_GEN(DT_BF16, MODE_INT8);
+    else if (dt == DT_F16) QLIN_GEN(DT_F16, MODE_INT8);
+    else QLIN_GEN(DT_F32, MODE_INT8);
+  } else {
+    if (dt == DT_BF16) QLIN_GEN(DT_BF16, MODE_INT4_ROW);
+    else if (dt == DT_F16) QLIN_GEN(DT_F16, MODE_INT4_ROW);
+    else QLIN_GEN(DT_F32, MODE_INT4_ROW);
+  }
+#undef QLIN_GEN
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rowquant_generic launch");
+  return QLIN_OK;
+}
+
+}  // namespace qlin

@@ -1,0 +1,325 @@
+// Row-wise rotate + quantise kernels (bandwidth bound).
+//
+// One warp covers 32 consecutive 16-element chunks of a row; a row is covered
+// by TPR threads (a multiple of 32), a CTA holds RPC rows.  Every thread
+// keeps its CHUNKS x 16 elements in registers from the single HBM read to
+// the single HBM write:
+//   1. 128-bit loads, convert to float32 (int8 input: times its row scale);
+//   2. ConvRot stage 1: Hadamard digits inside the 16-element chunk;
+//   3. ConvRot stage 2 (group > 16): the chunk-index digits, through a
+//      per-warp swizzled shared-memory transpose (only __syncwarp needed:
+//      a rotation group never leaves its warp);
+//   4. times the normalisation constant, rounded to the compute dtype;
+//   5. absmax (row: warp shuffles + one CTA exchange; group of 128: 8 lanes),
+//      scale and codes with the reference's exact rounding sequence;
+//   6. one 128-bit (or 64-bit packed-int4) store per chunk.
+#pragma once
+
+#include "common.cuh"
+
+namespace qlin {
+
+enum : int {
+  MODE_INT8 = 0,        // quantize_int8_axiswise(dim=-1): absmax/127, rint(x * (1/s))
+  MODE_INT4_ROW = 1,    // quantize_signed_int4_rowwise: dtype math, codes in [-7, 7]
+  MODE_INT4_G128 = 2,   // same conventions per 128-element group
+  MODE_ROTATE = 3,      // rotated values only, in the compute dtype
+  MODE_REQUANT = 4,     // quantize_int8(x, given scale), round-half-even
+  MODE_REQUANT_SR = 5,  // stochastic rounding with a given scale
+};
+enum : int { DT_I8 = 3 };  // extra input type for dequantisation
+
+struct RowQuantParams {
+  const void* x;
+  int64_t ldx;           // input row stride, elements
+  int M, K;
+  float rot_c;           // normalised Hadamard entry in the compute dtype
+  float clamp_min;       // int4: 1e-10 in the compute dtype
+  const float* in_scale; // int8 input (dequant) or given requant scale
+  int in_scale_per_row;  // 1: in_scale[M], 0: in_scale[0]
+  int8_t* q;             // codes: [M, K] int8
+  float* scale;          // per-row [M] or per-group [M, K/128]
+  void* out;             // MODE_ROTATE output [M, K] in the compute dtype,
+                         // or packed int4 codes [M, K/2] for the int4 modes
+  uint64_t seed;         // MODE_REQUANT_SR
+};
+
+template <int DT_IN>
+__device__ __forceinline__ void load_chunk(const void* base, int64_t off, float (&v)[16], float s) {
+  if constexpr (DT_IN == DT_I8) {
+    const int4 t = __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const int8_t*>(base) + off));
+    const uint32_t w[4] = {(uint32_t)t.x, (uint32_t)t.y, (uint32_t)t.z, (uint32_t)t.w};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int b = (int)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFF);
+      v[j] = __fmul_rn((float)b, s);  // dequantize: q.float() * scale
+    }
+  } else {
+    load16<DT_IN>(reinterpret_cast<const typename Elem<DT_IN>::T*>(base) + off, v);
+  }
+}
+
+// Swizzled float index inside a warp's 512-float staging buffer.  XORs the
+// low three bits of the 16-byte chunk index with bits of the chunk index
+// above them, so both the natural-order float4 accesses and the transposed
+// stage-2 accesses of each rotation size are (nearly) bank-conflict free.
+template <int R>
+__device__ __forceinline__ int swz(int e) {
+  constexpr int S = (R >= 16) ? 6 : (R == 8) ? 5 : (R == 4) ? 4 : 3;
+  const int c = e >> 2;
+  const int p = c ^ ((c >> 3) & 3) ^ (((c >> S) & 1) << 2);
+  return (p << 2) | (e & 3);
+}
+
+// Counter-based uniform random in [0, 1) (SplitMix64 finaliser of
+// seed + element index); 24 random bits.
+__device__ __forceinline__ float uniform01(uint64_t seed, uint64_t idx) {
+  uint64_t z = seed + 0x9E3779B97F4A7C15ull * (idx + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(uint32_t)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  const uint32_t ab = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
+  const uint32_t cd = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
+}
+
+template <int DT_IN, int DT_Q, int KIND, int R, int CHUNKS, int MODE>
+__global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
+  using EQ = Elem<DT_Q>;
+  extern __shared__ float stage_smem[];  // [warps][512] when R > 1
+  __shared__ float red[32][33];          // per row, per warp partial absmax
+
+  const int tpr = blockDim.x;
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp_in_row = t >> 5;
+  const int row = blockIdx.x * blockDim.y + threadIdx.y;
+  const bool row_ok = row < p.M;
+  const int nchunks = p.K >> 4;
+  const int warp_lin = threadIdx.y * (tpr >> 5) + warp_in_row;
+  float* wbuf = stage_smem + warp_lin * 512;
+  (void)wbuf;
+
+  float in_s = 1.0f;
+  if constexpr (DT_IN == DT_I8) {
+    if (row_ok) in_s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
+  }
+
+  float v[CHUNKS][16];
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    const int ci = t + i * tpr;
+    if (row_ok && ci < nchunks) {
+      load_chunk<DT_IN>(p.x, (int64_t)row * p.ldx + (int64_t)ci * 16, v[i], in_s);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
+    }
+  }
+
+  if constexpr (KIND != ROT_NONE) {
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      xform_regs<KIND, 16>(v[i]);
+      if constexpr (R > 1) {
+        // stage 2: Hadamard over the chunk index within each group of R chunks
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float4 f = make_float4(v[i][4 * q4], v[i][4 * q4 + 1], v[i][4 * q4 + 2], v[i][4 * q4 + 3]);
+          *reinterpret_cast<float4*>(wbuf + swz<R>(lane * 16 + 4 * q4)) = f;
+        }
+        __syncwarp();
+        constexpr int J = 16 / R;  // columns handled per thread
+        const int g0 = (lane / R) * (16 * R);
+        const int rp = lane % R;
+        float w[J][R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int jj = 0; jj < J; ++jj) w[jj][r] = wbuf[swz<R>(g0 + 16 * r + rp * J + jj)];
+        }
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) xform_regs<KIND, R>(w[jj]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int jj = 0; jj < J; ++jj) wbuf[swz<R>(g0 + 16 * r + rp * J + jj)] = w[jj][r];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 f = *reinterpret_cast<const float4*>(wbuf + swz<R>(lane * 16 + 4 * q4));
+          v[i][4 * q4] = f.x; v[i][4 * q4 + 1] = f.y; v[i][4 * q4 + 2] = f.z; v[i][4 * q4 + 3] = f.w;
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[i][j] = EQ::round(__fmul_rn(v[i][j], p.rot_c));
+    }
+  }
+
+  if constexpr (MODE == MODE_ROTATE) {
+    if (row_ok) {
+      auto* out = reinterpret_cast<typename EQ::T*>(p.out) + (int64_t)row * p.K;
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        const int ci = t + i * tpr;
+        if (ci < nchunks) store16<DT_Q>(out + (int64_t)ci * 16, v[i]);
+      }
+    }
+    return;
+  } else if constexpr (MODE == MODE_REQUANT || MODE == MODE_REQUANT_SR) {
+    if (!row_ok) return;
+    const float s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
+    const float inv = __frcp_rn(s);
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int ci = t + i * tpr;
+      if (ci >= nchunks) continue;
+      int qv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float y;
+        if constexpr (MODE == MODE_REQUANT) {
+          y = __fmul_rn(v[i][j], inv);                       // x * (1/scale)
+          y = fminf(fmaxf(y, -128.0f), 127.0f);
+          qv[j] = rint_to_int(y);
+        } else {
+          const float xs = __fdiv_rn(v[i][j], s);            // x / scale
+          const float fl = floorf(xs);
+          const float frac = __fsub_rn(xs, fl);
+          const float u = uniform01(p.seed, (uint64_t)row * p.K + ci * 16 + j);
+          y = (u < frac) ? __fadd_rn(fl, 1.0f) : fl;
+          y = fminf(fmaxf(y, -128.0f), 127.0f);
+          qv[j] = (int)y;
+        }
+      }
+      int4 o;
+      o.x = (int)pack4(qv[0], qv[1], qv[2], qv[3]);
+      o.y = (int)pack4(qv[4], qv[5], qv[6], qv[7]);
+      o.z = (int)pack4(qv[8], qv[9], qv[10], qv[11]);
+      o.w = (int)pack4(qv[12], qv[13], qv[14], qv[15]);
+      *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+    }
+    return;
+  } else {
+    // ---- absmax ----
+    float amax_row = 0.0f;
+    float amax_grp[CHUNKS];
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      float a = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a = fmaxf(a, fabsf(v[i][j]));
+      amax_grp[i] = a;
+      amax_row = fmaxf(amax_row, a);
+    }
+    if constexpr (MODE == MODE_INT4_G128) {
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) amax_grp[i] = fmaxf(amax_grp[i], __shfl_xor_sync(0xffffffffu, amax_grp[i], o));
+      }
+    } else {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax_row = fmaxf(amax_row, __shfl_xor_sync(0xffffffffu, amax_row, o));
+      const int nw = tpr >> 5;
+      if (lane == 0) red[threadIdx.y][warp_in_row] = amax_row;
+      __syncthreads();
+      amax_row = 0.0f;
+      for (int w2 = 0; w2 < nw; ++w2) amax_row = fmaxf(amax_row, red[threadIdx.y][w2]);
+    }
+    if (!row_ok) return;
+
+    float s_row = 0.0f, inv_row = 0.0f;
+    if constexpr (MODE == MODE_INT8) {
+      s_row = fmaxf(__fdiv_rn(amax_row, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
+      inv_row = __frcp_rn(s_row);                           // 1.0 / scale
+      if (t == 0) p.scale[row] = s_row;
+    } else if constexpr (MODE == MODE_INT4_ROW) {
+      s_row = EQ::round(__fdiv_rn(fmaxf(amax_row, p.clamp_min), 7.0f));
+      if (t == 0) p.scale[row] = s_row;
+    }
+
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int ci = t + i * tpr;
+      if (ci >= nchunks) continue;
+      float s = s_row;
+      if constexpr (MODE == MODE_INT4_G128) {
+        s = EQ::round(__fdiv_rn(fmaxf(amax_grp[i], p.clamp_min), 7.0f));
+        if ((ci & 7) == 0) p.scale[(int64_t)row * (p.K >> 7) + (ci >> 3)] = s;
+      }
+      int qv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float y;
+        if constexpr (MODE == MODE_INT8) {
+          y = __fmul_rn(v[i][j], inv_row);
+          y = fminf(fmaxf(y, -128.0f), 127.0f);
+        } else {
+          y = EQ::round(__fdiv_rn(v[i][j], s));  // (x / scale) in the compute dtype
+          y = fminf(fmaxf(y, -7.0f), 7.0f);
+        }
+        qv[j] = rint_to_int(y);
+      }
+      if (MODE != MODE_INT8 && p.out != nullptr) {
+        // packed int4 output [M, K/2]: low nibble = even k
+        uint32_t w2[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w2[j >> 3] |= ((uint32_t)qv[j] & 0xFu) << (4 * (j & 7));
+        *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(p.out) + (int64_t)row * (p.K >> 1) + (int64_t)ci * 8) =
+            make_uint2(w2[0], w2[1]);
+      } else {
+        int4 o;
+        o.x = (int)pack4(qv[0], qv[1], qv[2], qv[3]);
+        o.y = (int)pack4(qv[4], qv[5], qv[6], qv[7]);
+        o.z = (int)pack4(qv[8], qv[9], qv[10], qv[11]);
+        o.w = (int)pack4(qv[12], qv[13], qv[14], qv[15]);
+        *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+      }
+    }
+  }
+}
+
+// Generic fallback for rows that are not 16-element aligned (no rotation):
+// one CTA per row, strided scalar loop, two passes over the row.
+template <int DT_IN, int MODE>
+__global__ void __launch_bounds__(256) rowquant_generic_kernel(RowQuantParams p) {
+  using EQ = Elem<DT_IN>;
+  using T = typename Elem<DT_IN>::T;
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const T* x = reinterpret_cast<const T*>(p.x) + (int64_t)row * p.ldx;
+  float a = 0.0f;
+  for (int k = threadIdx.x; k < p.K; k += blockDim.x) a = fmaxf(a, fabsf(EQ::to_f(x[k])));
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+  __syncthreads();
+  a = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a = fmaxf(a, red[w]);
+  float s, inv = 0.0f;
+  if constexpr (MODE == MODE_INT8) {
+    s = fmaxf(__fdiv_rn(a, 127.0f), 1e-30f);
+    inv = __frcp_rn(s);
+  } else {
+    s = EQ::round(__fdiv_rn(fmaxf(a, p.clamp_min), 7.0f));
+  }
+  if (threadIdx.x == 0) p.scale[row] = s;
+  for (int k = threadIdx.x; k < p.K; k += blockDim.x) {
+    const float xv = EQ::to_f(x[k]);
+    float y;
+    if constexpr (MODE == MODE_INT8) {
+      y = fminf(fmaxf(__fmul_rn(xv, inv), -128.0f), 127.0f);
+    } else {
+      y = fminf(fmaxf(EQ::round(__fdiv_rn(xv, s)), -7.0f), 7.0f);
+    }
+    p.q[(int64_t)row * p.K + k] = (int8_t)rint_to_int(y);
+  }
+}
+
+}  // namespace qlin

@@ -1,0 +1,193 @@
+/*
+ * qlinear_b200.h -- C ABI of the B200 (sm_100a) quantized-linear kernels.
+ *
+ * Drop-in boundary for the quantized-linear hot path of the ComfyUI
+ * INT8-Fast node pack (reference v1.3.4).  The reference is pure Python: its
+ * kernels are Triton functions called from PyTorch.  Each entry point below
+ * replaces one of them (or one PyTorch expression on the hot path); the
+ * comment on each cites the reference interface it replaces.  The Python
+ * package binds these with ctypes (INTEGRATION.md shows the binding).
+ *
+ * Conventions
+ *  - All pointers are device pointers unless stated otherwise; matrices are
+ *    row-major with the given leading dimension (in elements).
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream); work is
+ *    enqueued asynchronously on it, nothing synchronises the host.
+ *  - The device is the calling thread's current CUDA device.
+ *  - Every function returns QLIN_OK (0) or a QLIN_ERR_* code and never throws;
+ *    qlin_last_error() returns a thread-local message for the last failure.
+ *  - Numerics follow the reference's PyTorch CPU path bit for bit (see
+ *    DESIGN.md for the exact rounding order of every epilogue).
+ */
+#ifndef QLINEAR_B200_H
+#define QLINEAR_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QLIN_API __attribute__((visibility("default")))
+#else
+#define QLIN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define QLIN_OK 0
+#define QLIN_ERR_INVALID_ARG 1   /* bad shape / null pointer / enum value      */
+#define QLIN_ERR_UNSUPPORTED 2   /* valid request this build does not handle   */
+#define QLIN_ERR_ALIGNMENT 3     /* pointer or leading dimension misaligned    */
+#define QLIN_ERR_CUDA 4          /* a CUDA runtime/driver call failed          */
+#define QLIN_ERR_NO_DEVICE 5     /* current device is not an sm_100 GPU        */
+
+/* element types */
+#define QLIN_BF16 0
+#define QLIN_F16 1
+#define QLIN_F32 2
+#define QLIN_I8 3
+#define QLIN_I32 4
+
+/* Hadamard families for ConvRot */
+#define QLIN_ROT_NONE 0
+#define QLIN_ROT_REGULAR 1   /* H4 (x) ... (x) H4, sizes 16, 64, 256 (convrot.py:18-55)        */
+#define QLIN_ROT_SYLVESTER 2 /* Sylvester H2^(x)k, sizes 32 and 128 (scipy.linalg.hadamard)  */
+
+/* weight-scale layouts for the W8A8 epilogue */
+#define QLIN_WSCALE_TENSOR 0 /* one float: int8_quant.py:113-133 order (ws*xs) */
+#define QLIN_WSCALE_ROW 1    /* float[N]:  int8_quant.py:137-164 order (xs then ws) */
+
+/* rounding modes for weight requantisation */
+#define QLIN_ROUND_NEAREST 0    /* quantize_int8 (int8_quant.py:41-42)             */
+#define QLIN_ROUND_STOCHASTIC 1 /* stochastic_round_int8_delta (int8_quant.py:80-106) */
+
+/* Library identification and diagnostics. */
+QLIN_API int qlin_version(void);
+/* Makes `device` current for the calling thread (the entry points below run
+ * on the current device; callers that switch devices call this first). */
+QLIN_API int qlin_set_device(int device);
+QLIN_API const char* qlin_last_error(void);
+/* Reads and clears the device-side error word of the current device (bit 0:
+ * a pipeline wait inside a GEMM kernel timed out).  Synchronises `stream`. */
+QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits);
+
+/* ---- (a) activation quantisation, fused with the ConvRot rotation -------- */
+
+/* Per-token int8 quantisation of x[M,K] (dtype x_dtype in {BF16,F16,F32}),
+ * optionally preceded by the block-diagonal Hadamard rotation of group
+ * `rot_group` (rot_kind != QLIN_ROT_NONE), rounded to x_dtype before
+ * quantising.  Writes q[M,K] int8 (row stride K) and scale[M] float.
+ * rot_c is the +-entry of the normalised Hadamard in x_dtype.
+ * Replaces: triton_quantize_rowwise (int8_fused_kernel.py:67-85) and the
+ * PyTorch quantize_int8_axiswise(x, dim=-1) (int8_quant.py:49-52), fused
+ * with rotate_activation (convrot.py:89-118, called at int8_quant.py:702-706). */
+QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                                 int rot_kind, int rot_group, float rot_c,
+                                 int8_t* q, float* scale, void* stream);
+
+/* Signed int4-range quantisation (codes in [-7,7], one per int8 byte) with
+ * the int4_quant.py conventions computed in x_dtype: absmax clamped at
+ * clamp_min (1e-10 in x_dtype), scale = absmax/7, round(x/scale).
+ * group == 0: per row, scale[M]   (quantize_signed_int4_rowwise, int4_quant.py:65-73)
+ * group == 128: per row and K-group, scale[M, K/128] (group-128 scheme).
+ * Optional fused rotation as above (prepare_rotated_activation, int4_quant.py:255-289). */
+QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                                 int rot_kind, int rot_group, float rot_c, int group, float clamp_min,
+                                 int8_t* q, float* scale, void* stream);
+
+/* Rotation only: out[M,K] (x_dtype, row stride K) = rotate_activation(x)
+ * (convrot.py:89-118); for float32 input this is rotate_weight (convrot.py:58-86). */
+QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                         int rot_kind, int rot_group, float rot_c, void* out, void* stream);
+
+/* ---- (b) W8A8 GEMM on tcgen05 kind::i8 ------------------------------------ */
+
+/* out[M,N] = epilogue( a[M,K] int8 . w[N,K]^T int8 ) with int32 accumulation.
+ * wscale_mode QLIN_WSCALE_ROW:    out = dt(dt(float(acc)*a_scale[m]*w_scale[n]) + bias[n])
+ * wscale_mode QLIN_WSCALE_TENSOR: out = dt(dt(float(acc)*(w_scale[0]*a_scale[m])) + bias[n])
+ * (dt = out_dtype rounding; bias has out_dtype, may be NULL.)
+ * K % 16 == 0; a, w 16-byte aligned.
+ * Replaces: triton_int8_linear_per_row / triton_int8_linear
+ * (int8_fused_kernel.py:332-377, 184-244) with the epilogue order of the
+ * PyTorch path int8_forward_dynamic_per_row / int8_forward_dynamic
+ * (int8_quant.py:137-164, 113-133). */
+QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                            int wscale_mode, const void* bias, void* out, int out_dtype,
+                            int64_t M, int64_t N, int64_t K, void* stream);
+
+/* c[M,N] int32 = a[M,K] . w[N,K]^T (torch._int_mm(a, w.T), int8_quant.py:124,152). */
+QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c,
+                         int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- (c) packed-INT4 GEMMs (nibbles unpacked in shared memory) ------------ */
+
+/* c[M,N] int32 = a[M,K] . unpack(w_packed[N,K/2])^T, signed nibbles, low
+ * nibble = even k.  Replaces triton_int4_mm (triton_int4_mm.py:123-170). */
+QLIN_API int qlin_int4_mm(const int8_t* a, const int8_t* w_packed, int32_t* c,
+                          int64_t M, int64_t N, int64_t K, void* stream);
+
+/* W4A4 per-row linear: out = dt(float(acc)*a_scale[m]*w_scale[n] + bias[n])
+ * in float32 with one rounding (convrot_w4a4_forward, int4_quant.py:325-353);
+ * bias has out_dtype (converted to float32), may be NULL. */
+QLIN_API int qlin_gemm_w4a4(const int8_t* a, const float* a_scale, const int8_t* w_packed,
+                            const float* w_scale, const void* bias, void* out, int out_dtype,
+                            int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Group-128 W4A8 (int8 activations, per-token scale a_scale[M]; weights
+ * packed int4 with bf16 scales w_gscale[N, K/128]):
+ *   acc = 0; for g: acc = fmaf(float(P_g[m,n]), w_gscale[n,g], acc)
+ *   out = dt(acc * a_scale[m] + bias[n])
+ * Group-128 W4A4 (int4 activations with float scales a_gscale[M, K/128]):
+ *   acc = fmaf(float(P_g), a_gscale[m,g]*w_gscale[n,g], acc); out = dt(acc + bias[n]).
+ * No counterpart in the reference (it has per-row int4 only); these follow
+ * the int4_quant.py conventions. */
+QLIN_API int qlin_gemm_w4a8_g128(const int8_t* a, const float* a_scale, const int8_t* w_packed,
+                                 const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
+                                 int64_t M, int64_t N, int64_t K, void* stream);
+QLIN_API int qlin_gemm_w4a4_g128(const int8_t* a, const float* a_gscale, const int8_t* w_packed,
+                                 const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
+                                 int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- (d) weight-side kernels for loaders and LoRA ------------------------- */
+
+/* On-the-fly weight quantisation: w[N,K] (BF16/F16/F32) -> float32 ->
+ * optional rotate_weight -> quantize_int8_axiswise(dim=1): q[N,K], scale[N].
+ * Replaces int8_quant.py:527-554 (and 276-326). */
+QLIN_API int qlin_quant_weight_int8(const void* w, int w_dtype, int64_t N, int64_t K,
+                                    int rot_kind, int rot_group, float rot_c,
+                                    int8_t* q, float* scale, void* stream);
+
+/* ConvRot W4A4 weight quantisation, packed[N,K/2] (low nibble = even k):
+ * group == 0: float32 -> rotate_weight -> quantize_signed_int4_rowwise_packed,
+ *             scale[N] (quantize_convrot_w4a4_weight, int4_quant.py:121-134);
+ * group == 128: the same conventions per 128-wide K group, computed in the
+ *             weight's dtype, scale[N, K/128] (group-128 scheme). */
+QLIN_API int qlin_quant_weight_int4(const void* w, int w_dtype, int64_t N, int64_t K,
+                                    int rot_kind, int rot_group, float rot_c, int group,
+                                    int8_t* packed, float* scale, void* stream);
+
+/* Asymmetric W4A8 -> int8 per-channel: codebook[code]*s_channel[n]*s_rel[n,k/gs]
+ * (w4a8_int8.py:46-75) followed by quantize_int8_axiswise(dim=1)
+ * (int8_quant.py:679-687), in one pass.  s_rel is float8_e4m3fn bytes. */
+QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
+                                    const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K,
+                                    int8_t* q, float* scale, void* stream);
+
+/* LoRA bake helpers (int8_quant.py:809-843, 881-941).
+ * dequant: out[N,K] float32 = rotate_weight(q * scale)   (rotation optional)
+ * requant: q[N,K] = round(rotate_weight(w) * (1/scale)) with the ORIGINAL
+ *          scale; QLIN_ROUND_STOCHASTIC uses a counter-based RNG seeded by
+ *          `seed` (same distribution as the reference, not the same stream).
+ * scale_mode: QLIN_WSCALE_TENSOR (one float) or QLIN_WSCALE_ROW (float[N]). */
+QLIN_API int qlin_dequant_int8(const int8_t* q, const float* scale, int scale_mode, int64_t N, int64_t K,
+                               int rot_kind, int rot_group, float rot_c, float* out, void* stream);
+QLIN_API int qlin_requant_int8(const float* w, const float* scale, int scale_mode, int64_t N, int64_t K,
+                               int rot_kind, int rot_group, float rot_c, int round_mode, uint64_t seed,
+                               int8_t* q, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLINEAR_B200_H */
