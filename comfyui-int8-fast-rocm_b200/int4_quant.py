@@ -1,0 +1,349 @@
+"""INT4 ConvRot W4A4 math and the ``Int4ConvRotOps`` ComfyUI custom
+operations (reference: int4_quant.py).
+
+The forward is two launches: the fused rotate + int4 activation quantiser
+(codes in int8 storage, as the reference's ``quantize_signed_int4_rowwise``)
+and the tcgen05 GEMM that unpacks the packed weight nibbles in shared memory
+(``triton_int4_mm`` + the float32 epilogue of ``convrot_w4a4_forward``).
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+from torch import Tensor, nn
+import torch.nn.functional as F
+
+from . import ops
+from .int8_quant import (_normalize_lora_key, _parse_comfy_quant, _pop_metadata, int8_forward_dynamic,
+                         int8_forward_dynamic_per_row, rot_for_group)
+
+CONVROT_W4A4_GROUP_SIZE = 256
+_INT4_MAX = 7
+
+
+def pack_int4_row_major(values: Tensor) -> Tensor:
+    """(..., K) nibbles -> (..., K//2) int8; low nibble = even column
+    (int4_quant.py:36-47)."""
+    if values.shape[-1] % 2 != 0:
+        raise ValueError(f"last dim must be even, got {values.shape[-1]}")
+    lo = values[..., 0::2].to(torch.int32) & 0x0F
+    hi = values[..., 1::2].to(torch.int32) & 0x0F
+    return (lo | (hi << 4)).to(torch.uint8).view(torch.int8)
+
+
+def unpack_int4_row_major(packed: Tensor) -> Tensor:
+    """Inverse of pack_int4_row_major, signed nibbles (int4_quant.py:50-58)."""
+    x32 = packed.to(torch.int32)
+    lo = x32 & 0x0F
+    hi = (x32 >> 4) & 0x0F
+    lo = torch.where(lo >= 8, lo - 16, lo)
+    hi = torch.where(hi >= 8, hi - 16, hi)
+    return torch.stack([lo, hi], dim=-1).reshape(*packed.shape[:-1], -1).to(torch.int8)
+
+
+def quantize_signed_int4_rowwise(x: Tensor):
+    """Per-row symmetric int4 in x.dtype, int8 storage (int4_quant.py:65-73):
+    (q [R,K] int8 in [-7,7], scales float32 [R])."""
+    return ops.quant_act_int4(x.reshape(x.shape[0], -1))
+
+
+def quantize_signed_int4_rowwise_packed(x: Tensor):
+    """Same, packed two per byte (int4_quant.py:76-83)."""
+    if x.dtype == torch.float32:
+        return ops.quant_weight_int4(x)
+    q, s = ops.quant_act_int4(x)
+    return pack_int4_row_major(q), s
+
+
+def quantize_convrot_w4a4_weight(weight: Tensor, convrot_groupsize: int = CONVROT_W4A4_GROUP_SIZE):
+    """rotate_weight + packed signed int4 per row (int4_quant.py:121-134)."""
+    if weight.dim() != 2:
+        raise ValueError(f"ConvRot W4A4 expects a 2D weight, got shape {tuple(weight.shape)}")
+    if weight.shape[-1] % convrot_groupsize != 0:
+        raise ValueError(f"in_features {weight.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
+    return ops.quant_weight_int4(weight.float(), rot_for_group(convrot_groupsize))
+
+
+def quantize_int4_g128(x: Tensor, rot=None):
+    """Group-128 int4 (per row and 128-wide K group) in x.dtype:
+    (q int8 [R,K], scales float32 [R, K/128])."""
+    return ops.quant_act_int4(x, rot, group=128)
+
+
+def dequantize_convrot_w4a4_weight_full(qweight: Tensor, wscales: Tensor, convrot_groupsize: int,
+                                        dtype: torch.dtype = torch.float32) -> Tensor:
+    """Unpack, rescale, un-rotate (int4_quant.py:217-231)."""
+    w = unpack_int4_row_major(qweight).to(torch.float32) * wscales.reshape(-1, 1).to(torch.float32)
+    return ops.rotate(w, *rot_for_group(convrot_groupsize)).to(dtype)
+
+
+def prepare_rotated_activation(x: Tensor, convrot_groupsize: int, compute_dtype: torch.dtype,
+                               skip_rotation: bool = False):
+    """Flatten + cast + rotate (int4_quant.py:255-289)."""
+    orig_shape = x.shape
+    if orig_shape[-1] % convrot_groupsize != 0:
+        raise ValueError(f"Input K={orig_shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
+    x2d = x.reshape(-1, orig_shape[-1]).to(compute_dtype).contiguous()
+    if skip_rotation:
+        return x2d, orig_shape
+    return ops.rotate(x2d, *rot_for_group(convrot_groupsize)), orig_shape
+
+
+def convrot_w4a4_forward(x: Tensor, qweight: Tensor, wscales: Tensor, bias, convrot_groupsize: int,
+                         compute_dtype: torch.dtype, skip_rotation: bool = False, qweight_unpacked=None,
+                         x_rot=None, orig_shape=None) -> Tensor:
+    """W4A4 ConvRot linear (int4_quant.py:292-353): fused rotate + int4
+    activation quant, then the packed-int4 tcgen05 GEMM with the float32
+    epilogue ``acc * x_scale * w_scale + bias`` rounded once."""
+    if x_rot is None:
+        orig_shape = x.shape
+        if orig_shape[-1] % convrot_groupsize != 0:
+            raise ValueError(f"Input K={orig_shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
+        x2d = x.reshape(-1, orig_shape[-1]).to(compute_dtype)
+        rot = None if skip_rotation else rot_for_group(convrot_groupsize)
+        qact, x_scale = ops.quant_act_int4(x2d, rot)
+    else:
+        qact, x_scale = ops.quant_act_int4(x_rot)
+    in_f = orig_shape[-1]
+    if in_f != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={in_f} does not match packed qweight K={qweight.shape[-1] * 2}")
+    out = ops.gemm_w4a4(qact, x_scale, qweight, wscales, bias, compute_dtype)
+    return out.reshape(*orig_shape[:-1], wscales.shape[0])
+
+
+try:
+    from comfy.ops import manual_cast, cast_bias_weight, uncast_bias_weight
+    _COMFY_OPS_AVAILABLE = True
+except ImportError:
+    _COMFY_OPS_AVAILABLE = False
+
+
+if _COMFY_OPS_AVAILABLE:
+
+    class Int4ConvRotOps(manual_cast):
+        """ComfyUI custom operations for INT4 ConvRot W4A4 (int4_quant.py:394-976)."""
+
+        excluded_names: list = []
+        dynamic_quantize = False
+        compute_dtype = None
+        convrot_groupsize = CONVROT_W4A4_GROUP_SIZE
+        _is_prequantized = False
+        _logged_otf = False
+        debug_nan_check = False
+        debug_skip_rotation = False
+        debug_weight_only_reference = False
+        lora_mode = "None"
+        dynamic_lora = False
+        lora_patches: dict = {}
+        lora_strength = 1.0
+        skeleton_meta_init = False
+
+        @staticmethod
+        def _default_compute_dtype(x: Tensor) -> torch.dtype:
+            if x.dtype in (torch.float16, torch.bfloat16):
+                return x.dtype
+            return torch.float16
+
+        class Linear(manual_cast.Linear):
+            def __init__(self, in_features, out_features, bias=True, device=None, dtype=None):
+                if getattr(Int4ConvRotOps, "skeleton_meta_init", False):
+                    nn.Module.__init__(self)
+                    self.in_features = in_features
+                    self.out_features = out_features
+                    kw = {"device": "meta"}
+                    if dtype is not None:
+                        kw["dtype"] = dtype
+                    self.weight = nn.Parameter(torch.empty((out_features, in_features), **kw), requires_grad=False)
+                    self.bias = nn.Parameter(torch.empty((out_features,), **kw), requires_grad=False) if bias else None
+                else:
+                    super().__init__(in_features, out_features, bias, device, dtype)
+                self.register_buffer("weight_scale", None)
+                self._is_quantized = False
+                self._convrot_groupsize = Int4ConvRotOps.convrot_groupsize
+                self._linear_dtype = "int4"
+                self._use_convrot = False
+                self._is_per_row = True
+                self.comfy_cast_weights = False
+                self._debug_name = "<unnamed>"
+                self.lora_patches = []
+
+            def reset_parameters(self):
+                return None
+
+            _normalize_lora_key = staticmethod(_normalize_lora_key)
+
+            def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                                      unexpected_keys, error_msgs):
+                self._debug_name = prefix
+                weight_key = prefix + "weight"
+                weight_tensor = state_dict.pop(weight_key, None)
+                bias_tensor = state_dict.pop(prefix + "bias", None)
+                weight_scale = _pop_metadata(state_dict, prefix, "weight_scale")
+                conf = _parse_comfy_quant(_pop_metadata(state_dict, prefix, "comfy_quant"))
+                state_dict.pop(prefix + "input_scale", None)
+                is_w4a4 = isinstance(conf, dict) and conf.get("format") == "convrot_w4a4"
+                is_other = isinstance(conf, dict) and conf.get("format") not in (None, "convrot_w4a4")
+
+                if weight_tensor is not None and weight_tensor.dtype == torch.int8 and is_w4a4:
+                    if weight_scale is None:
+                        error_msgs.append(f"{weight_key}: convrot_w4a4 weight found but weight_scale is missing")
+                    else:
+                        if weight_tensor.shape[-1] * 2 != self.in_features:
+                            error_msgs.append(
+                                f"{weight_key}: int4 weight implies in_features={weight_tensor.shape[-1] * 2}, "
+                                f"but this Linear expects {self.in_features}")
+                        self._is_quantized = True
+                        self._convrot_groupsize = int(conf.get("convrot_groupsize", CONVROT_W4A4_GROUP_SIZE))
+                        self._linear_dtype = conf.get("linear_dtype", "int4")
+                        self.weight = nn.Parameter(weight_tensor, requires_grad=False)
+                        self.register_buffer("weight_scale", weight_scale.float())
+                        Int4ConvRotOps._is_prequantized = True
+                elif weight_tensor is not None and weight_tensor.dtype == torch.int8 and is_other:
+                    if conf.get("format") == "int8_tensorwise" and weight_scale is not None:
+                        per_row = bool(conf.get("per_row", weight_scale.numel() > 1))
+                        self._is_quantized = True
+                        self._linear_dtype = "int8_tensorwise"
+                        self._use_convrot = bool(conf.get("convrot", False))
+                        self._convrot_groupsize = int(conf.get("convrot_groupsize", CONVROT_W4A4_GROUP_SIZE))
+                        self._is_per_row = per_row
+                        self.weight = nn.Parameter(weight_tensor.contiguous(), requires_grad=False)
+                        self.register_buffer("weight_scale", weight_scale.float().reshape(-1) if per_row
+                                             else weight_scale.float().reshape(()))
+                    else:
+                        error_msgs.append(f"{weight_key}: unsupported quantisation format {conf.get('format')!r}")
+                elif weight_tensor is not None and weight_tensor.dtype in (torch.float16, torch.bfloat16, torch.float32):
+                    is_excluded = any(ex in prefix for ex in Int4ConvRotOps.excluded_names)
+                    is_dim1 = self.in_features == 1 or self.out_features == 1 or weight_tensor.ndim == 1
+                    fits = weight_tensor.shape[-1] % Int4ConvRotOps.convrot_groupsize == 0
+                    if Int4ConvRotOps.dynamic_quantize and not is_excluded and not is_dim1 and fits:
+                        w = weight_tensor.to("cuda", non_blocking=True).float()
+                        q, s = quantize_convrot_w4a4_weight(w, Int4ConvRotOps.convrot_groupsize)
+                        self.weight = nn.Parameter(q.cpu(), requires_grad=False)
+                        self.register_buffer("weight_scale", s.cpu())
+                        self._is_quantized = True
+                        self._convrot_groupsize = Int4ConvRotOps.convrot_groupsize
+                        self._linear_dtype = "int4"
+                    else:
+                        self._is_quantized = False
+                        self.weight = nn.Parameter(weight_tensor, requires_grad=False)
+                else:
+                    self._is_quantized = False
+                    if weight_tensor is not None:
+                        self.weight = nn.Parameter(weight_tensor, requires_grad=False)
+                    else:
+                        missing_keys.append(weight_key)
+                self.bias = nn.Parameter(bias_tensor, requires_grad=False) if bias_tensor is not None else None
+
+            def convert_weight(self, _weight, inplace=False):
+                return self.weight if self._is_quantized else _weight
+
+            def set_weight(self, out_weight, inplace_update=False, seed=0, return_weight=False, **kwargs):
+                if not self._is_quantized:
+                    new_weight = out_weight.to(self.weight.dtype)
+                elif out_weight.dtype == torch.int8:
+                    new_weight = out_weight
+                else:
+                    q, s = quantize_convrot_w4a4_weight(out_weight.float(), self._convrot_groupsize)
+                    new_weight = q
+                    self.register_buffer("weight_scale", s.to(self.weight_scale.device))
+                if return_weight:
+                    return new_weight
+                if inplace_update:
+                    self.weight.data.copy_(new_weight)
+                else:
+                    self.weight = nn.Parameter(new_weight, requires_grad=False)
+
+            def set_bias(self, out_bias, inplace_update=False, seed=0, return_weight=False, **kwargs):
+                if out_bias is None:
+                    return None
+                if return_weight:
+                    return out_bias
+                if inplace_update and self.bias is not None:
+                    self.bias.data.copy_(out_bias)
+                else:
+                    self.bias = nn.Parameter(out_bias, requires_grad=False)
+
+            def forward(self, x: Tensor) -> Tensor:
+                need_cast = self.comfy_cast_weights or len(self.weight_function) > 0 or len(self.bias_function) > 0
+                if not self._is_quantized:
+                    if need_cast:
+                        weight, bias, offload_stream = cast_bias_weight(self, x, offloadable=True)
+                        out = F.linear(x, weight, bias)
+                        uncast_bias_weight(self, weight, bias, offload_stream)
+                        return out
+                    weight = self.weight.to(device=x.device, dtype=x.dtype)
+                    bias = self.bias.to(device=x.device, dtype=x.dtype) if self.bias is not None else None
+                    return F.linear(x, weight, bias)
+
+                if need_cast:
+                    weight, bias, offload_stream = cast_bias_weight(
+                        self, input=None, dtype=torch.int8, device=x.device, bias_dtype=x.dtype, offloadable=True)
+                else:
+                    weight, bias, offload_stream = self.weight, self.bias, None
+                if weight.device != x.device:
+                    weight = weight.to(x.device, non_blocking=True)
+                if bias is not None and bias.device != x.device:
+                    bias = bias.to(x.device, non_blocking=True)
+                w_scale = self.weight_scale.to(x.device, non_blocking=True)
+                compute_dtype = Int4ConvRotOps.compute_dtype or Int4ConvRotOps._default_compute_dtype(x)
+
+                if self._linear_dtype == "int8_tensorwise":
+                    x2d = x.reshape(-1, x.shape[-1]).to(compute_dtype)
+                    rot = rot_for_group(self._convrot_groupsize) if self._use_convrot else None
+                    if self._is_per_row:
+                        y = int8_forward_dynamic_per_row(x2d, weight, w_scale, bias, compute_dtype, rot)
+                    else:
+                        y = int8_forward_dynamic(x2d, weight, w_scale, bias, compute_dtype, rot)
+                    y = y.reshape(*x.shape[:-1], weight.shape[0])
+                    x_l = ops.rotate(x2d, *rot) if (self.lora_patches and rot is not None) else x2d
+                else:
+                    y = convrot_w4a4_forward(x, weight, w_scale, bias, self._convrot_groupsize, compute_dtype,
+                                             skip_rotation=Int4ConvRotOps.debug_skip_rotation)
+                    x_l = None
+                    if self.lora_patches:
+                        x_l, _ = prepare_rotated_activation(x, self._convrot_groupsize, compute_dtype,
+                                                            Int4ConvRotOps.debug_skip_rotation)
+                if self.lora_patches:
+                    y2 = y.reshape(-1, y.shape[-1])
+                    for lora_down, lora_up, lora_start, lora_size in self.lora_patches:
+                        lD = lora_down.to(x.device, non_blocking=True)
+                        lU = lora_up.to(x.device, non_blocking=True)
+                        ly = F.linear(F.linear(x_l.to(lD.dtype), lD), lU)
+                        if lora_start is not None:
+                            y2[:, lora_start:lora_start + lora_size] = (
+                                y2[:, lora_start:lora_start + lora_size] + ly.to(y2.dtype))
+                        else:
+                            y2 = y2 + ly.to(y2.dtype)
+                    y = y2.reshape(y.shape)
+                if Int4ConvRotOps.debug_nan_check and not torch.isfinite(y).all():
+                    logging.error(f"INT4 ConvRot DEBUG: NaN/Inf output at layer '{self._debug_name}'")
+                if need_cast:
+                    uncast_bias_weight(self, weight, bias, offload_stream)
+                return y
+
+        class GroupNorm(manual_cast.GroupNorm):
+            pass
+
+        class LayerNorm(manual_cast.LayerNorm):
+            pass
+
+        class Conv2d(manual_cast.Conv2d):
+            pass
+
+        class Conv3d(manual_cast.Conv3d):
+            pass
+
+        class ConvTranspose2d(manual_cast.ConvTranspose2d):
+            pass
+
+        class Embedding(manual_cast.Embedding):
+            pass
+
+        @classmethod
+        def conv_nd(cls, dims, *args, **kwargs):
+            if dims == 2:
+                return cls.Conv2d(*args, **kwargs)
+            if dims == 3:
+                return cls.Conv3d(*args, **kwargs)
+            raise ValueError(f"unsupported dimensions: {dims}")

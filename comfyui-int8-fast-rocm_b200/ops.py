@@ -1,0 +1,357 @@
+"""Torch-facing wrappers of the sm_100a kernels.
+
+Each function validates/normalises its tensors, allocates the outputs with
+``torch.empty`` on the input's device, and calls one C-ABI entry point of
+libqlinear_b200 on torch's current CUDA stream.  CUDA tensors only: there is
+no CPU path (a CPU tensor raises).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn.functional as F
+
+from . import _native as N
+
+_DT = {torch.bfloat16: N.BF16, torch.float16: N.F16, torch.float32: N.F32}
+_ROT = {None: N.ROT_NONE, "none": N.ROT_NONE, "regular": N.ROT_REGULAR, "sylvester": N.ROT_SYLVESTER}
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor):
+    if not t.is_cuda:
+        raise RuntimeError(
+            "comfyui-int8-fast-rocm_b200 kernels run on CUDA (sm_100a) tensors only; got a tensor on " + str(t.device))
+    N.call("qlin_set_device", t.device.index)
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous with a 16-byte aligned base (copies only when needed)."""
+    if not t.is_contiguous():
+        t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _rows(x: torch.Tensor):
+    """2-D view with unit inner stride; returns (x2d, ldx)."""
+    if x.dim() != 2:
+        raise ValueError(f"expected a 2-D tensor, got shape {tuple(x.shape)}")
+    if x.stride(1) != 1 or x.stride(0) < x.shape[1]:
+        x = x.contiguous()
+    return x, x.stride(0)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}; expected bfloat16, float16 or float32") from None
+
+
+def hadamard_scale(group: int, dtype: torch.dtype) -> float:
+    """The +-entry of the normalised Hadamard ``H / group**0.5`` (built in
+    float32, convrot.py:54) after the cast to the operand dtype
+    (``H.to(dtype=x.dtype)``, convrot.py:116)."""
+    c = torch.ones((), dtype=torch.float32) / (group ** 0.5)
+    return float(c.to(dtype).float().item())
+
+
+def _rot_args(rot, dtype):
+    """rot: None or (kind, group) with kind in {"regular", "sylvester"}."""
+    if rot is None:
+        return N.ROT_NONE, 0, 0.0
+    kind, group = rot
+    return _ROT[kind], int(group), hadamard_scale(int(group), dtype)
+
+
+def int4_clamp_min(dtype: torch.dtype) -> float:
+    """``clamp(min=1e-10)`` on a ``dtype`` tensor (int4_quant.py:70)."""
+    return float(torch.tensor(1e-10, dtype=dtype).float().item())
+
+
+# ---------------------------------------------------------------------------
+# (a) activations
+# ---------------------------------------------------------------------------
+
+
+def quant_act_int8(x: torch.Tensor, rot=None):
+    """Per-token int8: (q int8 [M,K], scale float32 [M,1])."""
+    x, ldx = _rows(x)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    if M and K:
+        st = _stream(x)
+        kind, g, c = _rot_args(rot, x.dtype)
+        if kind != N.ROT_NONE and x.data_ptr() % 16:
+            x, ldx = x.clone(), K
+        N.call("qlin_quant_act_int8", x.data_ptr(), dtype_code(x.dtype), M, K, ldx, kind, g, c,
+               q.data_ptr(), s.data_ptr(), st)
+    return q, s
+
+
+def quant_act_int4(x: torch.Tensor, rot=None, group: int = 0):
+    """Signed int4-range codes in int8 storage: (q [M,K], scale float32
+    [M] (group 0) or [M, K/128] (group 128))."""
+    x, ldx = _rows(x)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,) if group == 0 else (M, K // 128), dtype=torch.float32, device=x.device)
+    if M and K:
+        st = _stream(x)
+        kind, g, c = _rot_args(rot, x.dtype)
+        if (kind != N.ROT_NONE or group) and x.data_ptr() % 16:
+            x, ldx = x.clone(), K
+        N.call("qlin_quant_act_int4", x.data_ptr(), dtype_code(x.dtype), M, K, ldx, kind, g, c, int(group),
+               int4_clamp_min(x.dtype), q.data_ptr(), s.data_ptr(), st)
+    return q, s
+
+
+def rotate(x: torch.Tensor, kind: str, group: int) -> torch.Tensor:
+    """Block-diagonal Hadamard rotation of the last dim (rotate_activation /
+    rotate_weight semantics), result in x.dtype."""
+    shape = x.shape
+    x2, ldx = _rows(x.reshape(-1, shape[-1]))
+    M, K = x2.shape
+    out = torch.empty((M, K), dtype=x.dtype, device=x.device)
+    if M and K:
+        st = _stream(x2)
+        if x2.data_ptr() % 16:
+            x2, ldx = x2.clone(), K
+        k, g, c = _rot_args((kind, group), x.dtype)
+        N.call("qlin_rotate", x2.data_ptr(), dtype_code(x.dtype), M, K, ldx, k, g, c, out.data_ptr(), st)
+    return out.reshape(shape)
+
+
+# ---------------------------------------------------------------------------
+# (b) / (c) GEMMs
+# ---------------------------------------------------------------------------
+
+
+def _check_gemm(a, w, k_factor=1):
+    if a.dtype != torch.int8 or w.dtype != torch.int8:
+        raise TypeError("int8 operands expected")
+    if a.dim() != 2 or w.dim() != 2:
+        raise ValueError("2-D operands expected")
+    if a.shape[1] != w.shape[1] * k_factor:
+        raise ValueError(f"K mismatch: activation K={a.shape[1]}, weight represents {w.shape[1] * k_factor}")
+    if a.device != w.device:
+        raise ValueError("operands on different devices")
+
+
+def _pad_k(a_q, w, mult, w_factor=1):
+    """Zero-pad K to a multiple of ``mult`` (zero columns add nothing to the
+    int32 sums)."""
+    K = a_q.shape[1]
+    if K % mult:
+        pad = mult - K % mult
+        a_q = F.pad(a_q, (0, pad))
+        w = F.pad(w, (0, pad // w_factor))
+    return a_q, w
+
+
+def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, per_row=True):
+    """W8A8 linear on int8 operands (int8_forward_dynamic(_per_row) epilogue)."""
+    _check_gemm(a_q, w_q)
+    a_q, w_q = _pad_k(_aligned(a_q), _aligned(w_q), 16)
+    M, K = a_q.shape
+    Nn = w_q.shape[0]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return out
+    a_scale = a_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    w_scale = w_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    if per_row and w_scale.numel() != Nn:
+        raise ValueError(f"per-row weight scale must have {Nn} entries, got {w_scale.numel()}")
+    if not per_row and w_scale.numel() != 1:
+        raise ValueError("tensorwise weight scale must be a scalar")
+    if bias is not None:
+        bias = bias.reshape(-1).to(device=a_q.device, dtype=out_dtype).contiguous()
+    st = _stream(a_q)
+    N.call("qlin_gemm_w8a8", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
+           N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
+           M, Nn, K, st)
+    return out
+
+
+def int_mm(a_q, w_q):
+    """int32 [M,N] = a_q [M,K] . w_q[N,K]^T (``torch._int_mm(a, w.T)``)."""
+    _check_gemm(a_q, w_q)
+    a_q, w_q = _pad_k(_aligned(a_q), _aligned(w_q), 16)
+    M, K = a_q.shape
+    Nn = w_q.shape[0]
+    c = torch.empty((M, Nn), dtype=torch.int32, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return c
+    if K == 0:
+        return c.zero_()
+    st = _stream(a_q)
+    N.call("qlin_int_mm", a_q.data_ptr(), w_q.data_ptr(), c.data_ptr(), M, Nn, K, st)
+    return c
+
+
+def int4_mm(a_q, w_packed):
+    """int32 [M,N] = a_q [M,K] . unpack(w_packed [N,K/2])^T (triton_int4_mm)."""
+    _check_gemm(a_q, w_packed, 2)
+    a_q, w_packed = _pad_k(_aligned(a_q), _aligned(w_packed), 32, 2)
+    M, K = a_q.shape
+    Nn = w_packed.shape[0]
+    c = torch.empty((M, Nn), dtype=torch.int32, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return c
+    st = _stream(a_q)
+    N.call("qlin_int4_mm", a_q.data_ptr(), w_packed.data_ptr(), c.data_ptr(), M, Nn, K, st)
+    return c
+
+
+def gemm_w4a4(a_q, a_scale, w_packed, w_scale, bias=None, out_dtype=torch.bfloat16):
+    """W4A4 per-row linear with the convrot_w4a4_forward epilogue."""
+    _check_gemm(a_q, w_packed, 2)
+    a_q, w_packed = _pad_k(_aligned(a_q), _aligned(w_packed), 32, 2)
+    M, K = a_q.shape
+    Nn = w_packed.shape[0]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return out
+    a_scale = a_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    w_scale = w_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(device=a_q.device, dtype=out_dtype).contiguous()
+    st = _stream(a_q)
+    N.call("qlin_gemm_w4a4", a_q.data_ptr(), a_scale.data_ptr(), w_packed.data_ptr(), w_scale.data_ptr(),
+           _ptr(bias), out.data_ptr(), dtype_code(out_dtype), M, Nn, K, st)
+    return out
+
+
+def gemm_w4_g128(a_q, a_scale, w_packed, w_gscale, bias=None, out_dtype=torch.bfloat16, a_int4_groups=False):
+    """Group-128 W4A8 (a_scale [M]) or W4A4 (a_scale [M, K/128]) linear;
+    w_gscale [N, K/128] (bf16 values)."""
+    _check_gemm(a_q, w_packed, 2)
+    a_q, w_packed = _aligned(a_q), _aligned(w_packed)
+    M, K = a_q.shape
+    Nn = w_packed.shape[0]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return out
+    a_scale = a_scale.to(device=a_q.device, dtype=torch.float32).contiguous()
+    ws = w_gscale.to(device=a_q.device, dtype=torch.bfloat16).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(device=a_q.device, dtype=out_dtype).contiguous()
+    st = _stream(a_q)
+    fn = "qlin_gemm_w4a4_g128" if a_int4_groups else "qlin_gemm_w4a8_g128"
+    N.call(fn, a_q.data_ptr(), a_scale.data_ptr(), w_packed.data_ptr(), ws.data_ptr(), _ptr(bias),
+           out.data_ptr(), dtype_code(out_dtype), M, Nn, K, st)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (d) weights
+# ---------------------------------------------------------------------------
+
+
+def quant_weight_int8(w: torch.Tensor, rot=None):
+    """w [N,K] (bf16/f16/f32) -> .float() -> optional rotate_weight ->
+    quantize_int8_axiswise(dim=1): (q int8 [N,K], scale float32 [N,1])."""
+    w = _aligned(w)
+    Nn, K = w.shape
+    q = torch.empty((Nn, K), dtype=torch.int8, device=w.device)
+    s = torch.empty((Nn, 1), dtype=torch.float32, device=w.device)
+    if Nn and K:
+        st = _stream(w)
+        kind, g, c = _rot_args(rot, torch.float32)
+        N.call("qlin_quant_weight_int8", w.data_ptr(), dtype_code(w.dtype), Nn, K, kind, g, c, q.data_ptr(),
+               s.data_ptr(), st)
+    return q, s
+
+
+def quant_weight_int4(w: torch.Tensor, rot=None, group: int = 0):
+    """Packed signed int4 [N,K/2] + scales: float32 [N] (group 0, float32
+    math as quantize_convrot_w4a4_weight) or [N, K/128] (group 128, math in
+    w.dtype)."""
+    w = _aligned(w)
+    Nn, K = w.shape
+    p = torch.empty((Nn, K // 2), dtype=torch.int8, device=w.device)
+    s = torch.empty((Nn,) if group == 0 else (Nn, K // 128), dtype=torch.float32, device=w.device)
+    if Nn and K:
+        st = _stream(w)
+        kind, g, c = _rot_args(rot, torch.float32 if group == 0 else w.dtype)
+        N.call("qlin_quant_weight_int4", w.data_ptr(), dtype_code(w.dtype), Nn, K, kind, g, c, int(group),
+               p.data_ptr(), s.data_ptr(), st)
+    return p, s
+
+
+def requant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size: int):
+    """asym_w4a8_int8 -> int8 per-channel (q [N,K], scale float32 [N,1])."""
+    packed = _aligned(packed)
+    Nn, Kp = packed.shape
+    K = Kp * 2
+    dev = packed.device
+    codebook = codebook.to(device=dev, dtype=torch.float32).contiguous()
+    s_channel = s_channel.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    if s_rel.dtype != torch.uint8:
+        s_rel = s_rel.view(torch.uint8)
+    s_rel = s_rel.to(dev).contiguous()
+    if s_rel.shape[1] * group_size != K:
+        raise ValueError(f"W4A8: group mismatch, num_groups({s_rel.shape[1]}) * group_size({group_size}) != K({K})")
+    q = torch.empty((Nn, K), dtype=torch.int8, device=dev)
+    s = torch.empty((Nn, 1), dtype=torch.float32, device=dev)
+    if Nn and K:
+        st = _stream(packed)
+        N.call("qlin_requant_asym_w4a8", packed.data_ptr(), codebook.data_ptr(), s_channel.data_ptr(),
+               s_rel.data_ptr(), int(group_size), Nn, K, q.data_ptr(), s.data_ptr(), st)
+    return q, s
+
+
+def _scale_arg(scale, n, device):
+    s = scale.reshape(-1).to(device=device, dtype=torch.float32).contiguous() if torch.is_tensor(scale) \
+        else torch.tensor([float(scale)], dtype=torch.float32, device=device)
+    if s.numel() == 1:
+        return s, N.WSCALE_TENSOR
+    if s.numel() != n:
+        raise ValueError(f"scale must have 1 or {n} entries, got {s.numel()}")
+    return s, N.WSCALE_ROW
+
+
+def dequant_int8(q: torch.Tensor, scale, rot=None) -> torch.Tensor:
+    """float32 ``rotate_weight(q.float() * scale)`` (rotation optional)."""
+    q = _aligned(q)
+    Nn, K = q.shape
+    out = torch.empty((Nn, K), dtype=torch.float32, device=q.device)
+    if Nn and K:
+        st = _stream(q)
+        s, mode = _scale_arg(scale, Nn, q.device)
+        kind, g, c = _rot_args(rot, torch.float32)
+        N.call("qlin_dequant_int8", q.data_ptr(), s.data_ptr(), mode, Nn, K, kind, g, c, out.data_ptr(), st)
+    return out
+
+
+def requant_int8(w: torch.Tensor, scale, rot=None, stochastic=False, seed=0) -> torch.Tensor:
+    """int8 ``quantize_int8(rotate_weight(w), scale)`` with the given (original)
+    scale; stochastic=True follows stochastic_round_int8_delta's rule."""
+    w = _aligned(w.to(torch.float32))
+    Nn, K = w.shape
+    q = torch.empty((Nn, K), dtype=torch.int8, device=w.device)
+    if Nn and K:
+        st = _stream(w)
+        s, mode = _scale_arg(scale, Nn, w.device)
+        kind, g, c = _rot_args(rot, torch.float32)
+        N.call("qlin_requant_int8", w.data_ptr(), s.data_ptr(), mode, Nn, K, kind, g, c,
+               N.ROUND_STOCHASTIC if stochastic else N.ROUND_NEAREST, int(seed) & (2 ** 64 - 1), q.data_ptr(), st)
+    return q
+
+
+def device_error(device=None) -> int:
+    """Read and clear the device-side error word (nonzero: a GEMM pipeline
+    wait timed out)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    N.call("qlin_set_device", dev.index)
+    bits = ctypes.c_uint32(0)
+    N.call("qlin_device_error", torch.cuda.current_stream(dev).cuda_stream, ctypes.addressof(bits))
+    return bits.value
