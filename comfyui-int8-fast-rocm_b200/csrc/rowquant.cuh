@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
           y = fminf(fmaxf(y, -128.0f), 127.0f);
         } else {
           y = EQ::round(__fdiv_rn(v[i][j], s));  // (x / scale) in the compute dtype
-          y = fminf(fmaxf(y, -7.0f), 7.0f);
+          // NaN (0/0 on an all-zero row in f16, where the 1e-10 clamp
+          // underflows) converts to code 0, as torch's float->int8 cast does
+          y = (y != y) ? 0.0f : fminf(fmaxf(y, -7.0f), 7.0f);
         }
         qv[j] = rint_to_int(y);
       }
@@ -316,7 +318,8 @@ __global__ void __launch_bounds__(256) rowquant_generic_kernel(RowQuantParams p)
     if constexpr (MODE == MODE_INT8) {
       y = fminf(fmaxf(__fmul_rn(xv, inv), -128.0f), 127.0f);
     } else {
-      y = fminf(fmaxf(EQ::round(__fdiv_rn(xv, s)), -7.0f), 7.0f);
+      y = EQ::round(__fdiv_rn(xv, s));
+      y = (y != y) ? 0.0f : fminf(fmaxf(y, -7.0f), 7.0f);
     }
     p.q[(int64_t)row * p.K + k] = (int8_t)rint_to_int(y);
   }

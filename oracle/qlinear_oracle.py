@@ -327,7 +327,11 @@ def quantize_signed_int4(x: np.ndarray, dtype: str, axis: int = -1):
     amax = np.abs(x).max(axis=axis, keepdims=True)
     amax = np.maximum(amax, F32(int4_clamp_min(dtype)))
     s = rnd(dtype, amax / F32(INT4_MAX))
-    q = np.rint(rnd(dtype, x / s))
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = np.rint(rnd(dtype, x / s))
+    # an all-zero f16 row divides 0/0 (the 1e-10 clamp underflows in f16);
+    # torch casts the NaN to int8 code 0
+    q = np.where(np.isnan(q), 0, q)
     return np.clip(q, -INT4_MAX, INT4_MAX).astype(np.int8), s.astype(F32)
 
 

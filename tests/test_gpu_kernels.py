@@ -1,0 +1,376 @@
+"""Parity of the sm_100a kernels (through the C-ABI) with the numpy oracle
+and the reference's golden vectors.
+
+Integer work (codes, scales, int32 accumulators) and every bf16/f16/f32
+output is compared bit for bit: the kernels evaluate the same float32
+expression sequence as the oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+from conftest import cuda_ok
+from oracle import qlinear_oracle as O
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+TDT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
+
+@pytest.fixture(scope="module")
+def P(pkg):
+    return pkg
+
+
+def dev(a, dt=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dt is not None:
+        t = t.to(TDT[dt])
+    return t.cuda()
+
+
+def host_f32(t):
+    return t.float().cpu().numpy()
+
+
+def bits(dt, v):
+    v = np.asarray(v, np.float32)
+    if dt == "bf16":
+        return O.f32_to_bf16_bits(v)
+    if dt == "f16":
+        return v.astype(np.float16).view(np.uint16)
+    return v.view(np.uint32)
+
+
+def tbits(t):
+    if t.dtype == torch.float32:
+        return t.cpu().numpy().view(np.uint32)
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+# ---------------------------------------------------------------------------
+# (a) activation quantisation
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+def test_quant_int8_golden(P, golden, dt):
+    x = gi.activation(0, 37, 256, dt, zero_row=5)
+    q, s = P.ops.quant_act_int8(dev(x, dt))
+    np.testing.assert_array_equal(q.cpu().numpy(), golden[f"q8_{dt}_q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), golden[f"q8_{dt}_s"])
+
+
+def test_quant_int8_configs0_scale(P, golden):
+    x = gi.activation(0, 4096, 3072, "bf16")
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
+    import hashlib
+    assert hashlib.sha256(q.cpu().numpy().tobytes()).hexdigest() == str(golden["q8_c0_q_sha"])
+    np.testing.assert_array_equal(s.cpu().numpy(), golden["q8_c0_s"])
+
+
+@pytest.mark.parametrize("K", [100, 250, 7])
+def test_quant_int8_unaligned_rows(P, K):
+    x = gi.activation(11, 19, K, "bf16")
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
+    qo, so = O.quantize_int8_axiswise(x, -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_quant_int8_strided_rows(P):
+    x = gi.activation(12, 40, 512, "bf16")
+    xt = dev(x, "bf16")[:, :384]  # row stride 512, 16-byte aligned rows
+    q, s = P.ops.quant_act_int8(xt)
+    qo, so = O.quantize_int8_axiswise(x[:, :384], -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_quant_int8_long_rows(P):
+    x = gi.activation(13, 8, 24576, "bf16")  # two chunks per thread
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
+    qo, so = O.quantize_int8_axiswise(x, -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+ROTS = [("regular", 16), ("regular", 64), ("regular", 256), ("sylvester", 32), ("sylvester", 128)]
+
+
+@pytest.mark.parametrize("kind,g", ROTS)
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_rotate_matches_oracle(P, kind, g, dt):
+    x = gi.activation(14, 33, 1024, dt)
+    y = P.ops.rotate(dev(x, dt), kind, g)
+    yo = O.rotate(x, g, kind, dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+
+
+@pytest.mark.parametrize("kind,g", ROTS)
+def test_fused_rotate_quant_int8(P, kind, g):
+    x = gi.activation(15, 64, 3072, "bf16")
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"), (kind, g))
+    qo, so = O.quantize_int8_axiswise(O.rotate(x, g, kind, "bf16"), -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_fused_rotate_quant_long_rows(P):
+    x = gi.activation(16, 4, 24576, "bf16")
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"), ("regular", 256))
+    qo, so = O.quantize_int8_axiswise(O.rotate(x, 256, "regular", "bf16"), -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_rotate_vs_reference_golden(P, golden):
+    # the reference's own bf16 matmul rotation: within 1 bf16 ulp
+    x = gi.activation(4, 32, 1024, "bf16")
+    for name, g, kind in [("rot_reg256", 256, "regular"), ("rot_syl128", 128, "sylvester")]:
+        y = tbits(P.ops.rotate(dev(x, "bf16"), kind, g)).astype(np.int32)
+        d = np.abs(y - golden[f"{name}_y"].astype(np.int32))
+        assert d.max() <= 1
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_quant_int4_rowwise(P, golden, dt):
+    x = gi.activation(6, 37, 512, dt, zero_row=3)
+    q, s = P.ops.quant_act_int4(dev(x, dt))
+    qo, so = O.quantize_signed_int4_rowwise(x, dt)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+    if dt == "f16":
+        np.testing.assert_array_equal(q.cpu().numpy()[np.arange(37) != 3], golden["i4_f16_q"][np.arange(37) != 3])
+
+
+def test_quant_int4_rowwise_reference_rotated_input(P, golden):
+    xr = O.bf16_bits_to_f32(golden["i4_xrot"]).reshape(37, 512)
+    q, s = P.ops.quant_act_int4(dev(xr, "bf16"))
+    np.testing.assert_array_equal(q.cpu().numpy(), golden["i4_q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), golden["i4_s"])
+
+
+@pytest.mark.parametrize("kind,g", [("regular", 256), ("sylvester", 128)])
+def test_fused_rotate_quant_int4(P, kind, g):
+    x = gi.activation(17, 48, 3072, "bf16")
+    q, s = P.ops.quant_act_int4(dev(x, "bf16"), (kind, g))
+    qo, so = O.quantize_signed_int4_rowwise(O.rotate(x, g, kind, "bf16"), "bf16")
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_quant_int4_group128(P):
+    x = gi.activation(18, 40, 3072, "bf16")
+    q, s = P.ops.quant_act_int4(dev(x, "bf16"), ("sylvester", 128), group=128)
+    qo, so = O.quantize_signed_int4_grouped(O.rotate(x, 128, "sylvester", "bf16"), "bf16")
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+# ---------------------------------------------------------------------------
+# (b) W8A8 GEMM
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("M,N,K", [(37, 512, 256), (256, 384, 3072), (200, 300, 160), (129, 136, 96),
+                                   (1, 8, 16), (513, 1024, 1024)])
+def test_int_mm(P, M, N, K):
+    rng = np.random.default_rng(M * 7 + N)
+    a = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    c = P.ops.int_mm(dev(a), dev(w))
+    np.testing.assert_array_equal(c.cpu().numpy(), O.int_mm(a, w))
+
+
+def test_int_mm_k_padding(P):
+    rng = np.random.default_rng(5)
+    a = rng.integers(-128, 128, (33, 100), dtype=np.int8)
+    w = rng.integers(-128, 128, (70, 100), dtype=np.int8)
+    np.testing.assert_array_equal(P.ops.int_mm(dev(a), dev(w)).cpu().numpy(), O.int_mm(a, w))
+
+
+def test_int_mm_extremes(P):
+    # all -128 * -128 over K = 8192: 134217728 fits int32 exactly
+    a = np.full((128, 8192), -128, np.int8)
+    w = np.full((256, 8192), -128, np.int8)
+    c = P.ops.int_mm(dev(a), dev(w)).cpu().numpy()
+    assert (c == 128 * 128 * 8192).all()
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_w8a8_golden(P, golden, dt):
+    x = gi.activation(1, 37, 256, dt)
+    wq, ws = golden[f"w8_{dt}_wq"], golden[f"w8_{dt}_ws"]
+    b = gi.bias(1, 512, dt)
+    xq, xs = P.ops.quant_act_int8(dev(x, dt))
+    y = P.ops.gemm_w8a8(xq, xs, dev(wq), dev(ws), dev(b, dt), TDT[dt], per_row=True)
+    np.testing.assert_array_equal(tbits(y), golden[f"w8_{dt}_y"])
+    y0 = P.ops.gemm_w8a8(xq, xs, dev(wq), dev(ws), None, TDT[dt], per_row=True)
+    np.testing.assert_array_equal(tbits(y0), golden[f"w8_{dt}_y_nobias"])
+
+
+def test_w8a8_medium_golden(P, golden):
+    x = gi.activation(2, 256, 3072, "bf16")
+    w = gi.weight(2, 384, 3072)
+    wq, ws = P.ops.quant_weight_int8(dev(w))
+    np.testing.assert_array_equal(ws.cpu().numpy(), golden["w8m_ws"])
+    xq, xs = P.ops.quant_act_int8(dev(x, "bf16"))
+    y = P.ops.gemm_w8a8(xq, xs, wq, ws, dev(gi.bias(2, 384, "bf16"), "bf16"), torch.bfloat16)
+    np.testing.assert_array_equal(tbits(y), golden["w8m_y"])
+
+
+def test_w8a8_tensorwise_golden(P, golden):
+    x = gi.activation(3, 37, 256, "f16")
+    wq = gi.int8_weight(3, 512, 256)
+    xq, xs = P.ops.quant_act_int8(dev(x, "f16"))
+    y = P.ops.gemm_w8a8(xq, xs, dev(wq), torch.tensor([0.01]), dev(gi.bias(3, 512, "f16"), "f16"),
+                        torch.float16, per_row=False)
+    np.testing.assert_array_equal(tbits(y), golden["w8t_y"])
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 512), (1024, 3072, 3072)])
+def test_w8a8_vs_oracle(P, dt, M, N, K):
+    x = gi.activation(20, M, K, dt)
+    w = gi.weight(20, N, K)
+    b = gi.bias(20, N, dt)
+    wq, ws = O.quantize_int8_axiswise(w, 1)
+    xq, xs = P.ops.quant_act_int8(dev(x, dt))
+    y = P.ops.gemm_w8a8(xq, xs, dev(wq), dev(ws), dev(b, dt), TDT[dt])
+    yo = O.int8_forward_dynamic_per_row(x, wq, ws, b, dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+
+
+@pytest.mark.parametrize("g,kind", [(256, "regular"), (128, "sylvester")])
+def test_convrot_w8a8_linear_configs1_shape(P, g, kind):
+    """ConvRot W8A8 at M=1024, N=3072, K=3072 (outlier activations)."""
+    M, N, K = 1024, 3072, 3072
+    x = gi.activation(1, M, K, "bf16")
+    w = gi.weight(1, N, K)
+    b = gi.bias(1, N, "bf16")
+    wq, ws = O.quantize_weight_int8(w, g, kind)
+    gq, gs = P.ops.quant_weight_int8(dev(w), (kind, g))
+    np.testing.assert_array_equal(gq.cpu().numpy(), wq)
+    np.testing.assert_array_equal(gs.cpu().numpy(), ws)
+    xq, xs = P.ops.quant_act_int8(dev(x, "bf16"), (kind, g))
+    y = P.ops.gemm_w8a8(xq, xs, gq, gs, dev(b, "bf16"), torch.bfloat16)
+    xo = O.rotate(x, g, kind, "bf16")
+    yo = O.int8_forward_dynamic_per_row(xo, wq, ws, b, "bf16")
+    np.testing.assert_array_equal(tbits(y), bits("bf16", yo))
+
+
+# ---------------------------------------------------------------------------
+# (c) packed-INT4 GEMMs
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("M,N,K", [(37, 128, 512), (256, 384, 3072), (130, 264, 160)])
+def test_int4_mm(P, M, N, K):
+    rng = np.random.default_rng(N)
+    a = rng.integers(-7, 8, (M, K), dtype=np.int8)
+    wn = rng.integers(-8, 8, (N, K), dtype=np.int8)
+    wp = O.pack_int4_row_major(wn)
+    c = P.ops.int4_mm(dev(a), dev(wp))
+    np.testing.assert_array_equal(c.cpu().numpy(), O.int_mm(a, wn))
+
+
+def test_w4a4_forward_golden(P, golden):
+    x = gi.activation(9, 37, 512, "bf16")
+    b = gi.bias(9, 128, "bf16")
+    pw, ps = golden["i4w_packed"], golden["i4w_scale"]
+    qa, sa = P.ops.quant_act_int4(dev(x, "bf16"), ("regular", 256))
+    acc = P.ops.int4_mm(qa, dev(pw))
+    np.testing.assert_array_equal(acc.cpu().numpy(), golden["i4fwd_acc"])
+    y = P.ops.gemm_w4a4(qa, sa, dev(pw), dev(ps), dev(b, "bf16"), torch.bfloat16)
+    np.testing.assert_array_equal(tbits(y), golden["i4fwd_y"])
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_w4a4_vs_oracle(P, dt):
+    M, N, K = 300, 640, 3072
+    x = gi.activation(21, M, K, dt)
+    w = gi.weight(21, N, K)
+    b = gi.bias(21, N, dt)
+    pw, ps = O.quantize_convrot_w4a4_weight(w, 256, "regular")
+    gp, gs = P.ops.quant_weight_int4(dev(w), ("regular", 256))
+    np.testing.assert_array_equal(gp.cpu().numpy(), pw)
+    np.testing.assert_array_equal(gs.cpu().numpy(), ps)
+    qa, sa = P.ops.quant_act_int4(dev(x, dt), ("regular", 256))
+    y = P.ops.gemm_w4a4(qa, sa, gp, gs, dev(b, dt), TDT[dt])
+    yo = O.convrot_w4a4_forward(x, pw, ps, b, 256, "regular", dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+
+
+# ---------------------------------------------------------------------------
+# (d) weight-side kernels
+# ---------------------------------------------------------------------------
+
+
+def test_requant_asym_w4a8_golden(P, golden):
+    packed, cb, sch, srel = gi.asym_w4a8(10, 96, 256, 16)
+    q, s = P.ops.requant_asym_w4a8(dev(packed), dev(cb), dev(sch), dev(srel), 16)
+    np.testing.assert_array_equal(q.cpu().numpy(), golden["w4a8_q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), golden["w4a8_s"])
+
+
+@pytest.mark.parametrize("wdt", ["bf16", "f16", "f32"])
+def test_quant_weight_int8_dtypes(P, wdt):
+    w = O.rnd(wdt, gi.weight(22, 96, 1024))
+    q, s = P.ops.quant_weight_int8(dev(w, wdt), ("regular", 256))
+    qo, so = O.quantize_weight_int8(w, 256, "regular")
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+def test_lora_dequant_requant(P, golden):
+    oq, os_ = golden["otf_q"], golden["otf_s"]
+    wf = P.ops.dequant_int8(dev(oq), dev(os_), ("regular", 256))
+    wo = O.dequant_unrotate_int8(oq, os_, 256, "regular")
+    np.testing.assert_array_equal(host_f32(wf), wo)
+    delta = gi.weight(12, 48, 512) * np.float32(0.05)
+    patched = wo + delta
+    q = P.ops.requant_int8(dev(patched), dev(os_), ("regular", 256))
+    np.testing.assert_array_equal(q.cpu().numpy(), O.rotate_requant_int8(patched, os_, 256, "regular"))
+    # no rotation, tensor-wide scale
+    q2 = P.ops.requant_int8(dev(patched), 0.003)
+    np.testing.assert_array_equal(q2.cpu().numpy(), O.quantize_int8(patched, np.float32(0.003)))
+
+
+def test_stochastic_requant_distribution(P):
+    x = np.full((64, 4096), 0.3, np.float32)
+    q = P.ops.requant_int8(dev(x), 1.0, stochastic=True, seed=7).cpu().numpy()
+    assert set(np.unique(q)) <= {0, 1}
+    assert abs(q.mean() - 0.3) < 0.01
+    q2 = P.ops.requant_int8(dev(x), 1.0, stochastic=True, seed=7).cpu().numpy()
+    np.testing.assert_array_equal(q, q2)
+
+
+# ---------------------------------------------------------------------------
+# errors
+# ---------------------------------------------------------------------------
+
+
+def test_cpu_tensor_rejected(P):
+    with pytest.raises(RuntimeError):
+        P.ops.quant_act_int8(torch.zeros(4, 16, dtype=torch.bfloat16))
+
+
+def test_bad_group_rejected(P):
+    from comfyui_int8_fast_rocm_b200._native import NativeError
+    with pytest.raises(NativeError):
+        P.ops.quant_act_int8(torch.zeros(4, 96, dtype=torch.bfloat16, device="cuda"), ("regular", 64))
+
+
+def test_empty_inputs(P):
+    q, s = P.ops.quant_act_int8(torch.zeros(0, 256, dtype=torch.bfloat16, device="cuda"))
+    assert q.shape == (0, 256) and s.shape == (0, 1)
+    y = P.ops.gemm_w8a8(q, s, torch.zeros(64, 256, dtype=torch.int8, device="cuda"),
+                        torch.ones(64, 1, device="cuda"), None, torch.bfloat16)
+    assert y.shape == (0, 64)
+
+
+def test_no_device_error_flag(P):
+    torch.cuda.synchronize()
+    assert P.ops.device_error() == 0
