@@ -1,4 +1,5 @@
 // Host side of the tcgen05 GEMMs: TMA descriptors, tile configuration, launch.
+#include <atomic>
 #include <mutex>
 
 #include "../../include/qlinear_b200.h"
@@ -47,8 +48,16 @@ template <int BN, int EPI, int OUT_DT, bool B_INT4>
 int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, B_INT4>;
   auto kern = gemm_i8_kernel<BN, EPI, OUT_DT, B_INT4>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+  static std::atomic<uint64_t> attr_devices{0};  // smem limit raised once per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  cudaError_t e;
+  if (!(attr_devices.load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+    attr_devices.fetch_or(bit);
+  }
   const int num_tiles = ((p.M + GEMM_BM - 1) / GEMM_BM) * ((p.N + BN - 1) / BN);
   const int grid = num_tiles < p.num_sms ? num_tiles : p.num_sms;
   kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);

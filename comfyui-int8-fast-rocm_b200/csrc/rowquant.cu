@@ -1,4 +1,6 @@
 // Instantiation and launch of the row-wise rotate/quantise kernel family.
+#include <atomic>
+
 #include "../../include/qlinear_b200.h"
 #include "internal.h"
 #include "rowquant.cuh"
@@ -32,9 +34,18 @@ struct LaunchShape {
 template <int DT_IN, int DT_Q, int KIND, int R, int CHUNKS, int MODE>
 int launch_one(const RowQuantParams& p, const LaunchShape& s, cudaStream_t stream) {
   auto kern = rowquant_kernel<DT_IN, DT_Q, KIND, R, CHUNKS, MODE>;
-  if (s.smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant)");
+  // Staged kernels can exceed the default 48 KB once the static reduction
+  // array is added; raise the limit once per device for this instantiation.
+  static std::atomic<uint64_t> attr_devices{0};
+  if (s.smem > 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_devices.load() & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant)");
+      attr_devices.fetch_or(bit);
+    }
   }
   dim3 block(s.tpr, s.rpc);
   dim3 grid((unsigned)((p.M + s.rpc - 1) / s.rpc));
