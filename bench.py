@@ -20,12 +20,9 @@ JSON line with the whole-job throughput (max step time over ranks).
 from __future__ import annotations
 
 import argparse
-import csv
-import io
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -75,47 +72,56 @@ def make_inputs(rows, device, seed=SEED):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML in a
+    background thread while the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, gpu_index, period_s=0.005):
+        self.gpu, self.period = gpu_index, period_s
+        self.samples, self.max_mhz, self.err = [], None, None
+
+    def _run(self):
+        import pynvml
+        while not self._stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((sm, rs))
+            except Exception as e:  # pragma: no cover
+                self.err = str(e)
+                return
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
+        self.thread = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.gpu]) if vis and vis.split(",")[0].isdigit() else self.gpu
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception as e:
+            self.err = str(e)
         return self
 
     def __exit__(self, *a):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for r in csv.reader(io.StringIO(getattr(self, "out", "") or "")):
-            if len(r) >= 9:
-                rows.append([c.strip() for c in r])
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "error": self.err}
+        reasons = sorted({k for _, rs in self.samples for k, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 def cpu_baseline(min_seconds=10.0, max_runs=60):
@@ -206,6 +212,9 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             flush.zero_()
+            # keep the GPU busy while the host enqueues the step, so the
+            # events time kernels, not host launch latency
+            torch.cuda._sleep(200_000)
             ev[i][0].record(s)
             xq, xs = ops.quant_act_int8(x, rot)
             ev[i][1].record(s)

@@ -107,11 +107,13 @@ __device__ __forceinline__ int rint_to_int(float v) {
 // Regular H4 (convrot.py:40-43): every column sums the 4 inputs and flips the
 // sign of exactly one (anti-diagonal), so y_k = S - 2*a_{3-k}.
 __device__ __forceinline__ void h4_regular(float& a0, float& a1, float& a2, float& a3) {
+  // fma(-2, a, s) == RN(s - 2a): 2a is exact, so this is the same single
+  // rounding as a subtraction of the doubled value.
   const float s = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-  const float y0 = __fsub_rn(s, __fmul_rn(2.0f, a3));
-  const float y1 = __fsub_rn(s, __fmul_rn(2.0f, a2));
-  const float y2 = __fsub_rn(s, __fmul_rn(2.0f, a1));
-  const float y3 = __fsub_rn(s, __fmul_rn(2.0f, a0));
+  const float y0 = __fmaf_rn(-2.0f, a3, s);
+  const float y1 = __fmaf_rn(-2.0f, a2, s);
+  const float y2 = __fmaf_rn(-2.0f, a1, s);
+  const float y3 = __fmaf_rn(-2.0f, a0, s);
   a0 = y0; a1 = y1; a2 = y2; a3 = y3;
 }
 __device__ __forceinline__ void h2_sylvester(float& a0, float& a1) {

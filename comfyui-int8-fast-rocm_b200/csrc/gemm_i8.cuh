@@ -7,11 +7,12 @@
 //   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.kind::i8 (M=128,
 //               N=BN, K=32) x 4 per stage, commits free the ring slot and,
 //               at tile end, hand the accumulator to the epilogue.
-//   warps 2-5   epilogue: tcgen05.ld of the int32 tile (each warp owns one
-//               32-lane TMEM quarter), the reference's scale/bias/rounding
-//               sequence, stores to HBM.  Two TMEM accumulators let the
-//               epilogue of tile i overlap the MMAs of tile i+1.
-//   warps 6-9   (packed-int4 B only) nibble -> int8 unpack of the B slab
+//   warps 2-9   epilogue: tcgen05.ld of the int32 tile (two warps per
+//               32-lane TMEM quarter, each converting half of the columns),
+//               the reference's scale/bias/rounding sequence, stores to HBM.
+//               Two TMEM accumulators let the epilogue of tile i overlap the
+//               MMAs of tile i+1.
+//   warps 10-13 (packed-int4 B only) nibble -> int8 unpack of the B slab
 //               into the swizzled operand layout the MMA reads.
 //
 // No TMA multicast is used anywhere (the same kernel runs in multi-GPU jobs).
@@ -70,6 +71,7 @@ struct GemmParams {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 128;  // bytes (= int8 elements) of K per stage
+constexpr int EPI_WARPS = 8;  // epilogue warps (2 per TMEM lane quarter)
 
 template <int BN, bool B_INT4>
 struct GemmCfg {
@@ -77,7 +79,7 @@ struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;
   static constexpr int B_BYTES = BN * GEMM_BK;
   static constexpr int BP_BYTES = B_INT4 ? BN * (GEMM_BK / 2) : 0;  // packed staging
-  static constexpr int NUM_THREADS = B_INT4 ? 320 : 192;
+  static constexpr int NUM_THREADS = B_INT4 ? 448 : 320;
   static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // 4 epilogue warps
+      mbar_init(&tempty[b], EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -265,16 +267,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       }
     }
   mma_done:;
-  } else if (warp < 6) {
+  } else if (warp < 2 + EPI_WARPS) {
     // ---------------- epilogue ----------------
+    // 8 warps: warp & 3 selects the 32-lane TMEM quarter (rows), the warp's
+    // half selects which half of the tile's 32-column chunks it converts.
     using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
+    constexpr int CHUNKS = BN / 32;
+    constexpr int CPW = CHUNKS / 2;  // chunks per warp
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
     const int vec_n = out16 ? 8 : 4;
-    const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
+    const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
+                        ((reinterpret_cast<uintptr_t>(p.w_scale) & 15) == 0) &&
+                        ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+    const bool has_bias = p.bias != nullptr;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
@@ -287,14 +297,57 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       float s_tensor = 0.0f;
       if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int c = half * CPW + cc;
+        const int col0 = nb * BN + c * 32;
+        const int ncols = min(32, p.N - col0);
+        const bool full_chunk = (ncols == 32) && vec_ok;
+        // per-column parameters first, so their latency overlaps the TMEM load
+        float wsv[32];
+        float bv[32];
+        if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) {
+          if (full_chunk) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0) + i);
+              wsv[4 * i] = t.x; wsv[4 * i + 1] = t.y; wsv[4 * i + 2] = t.z; wsv[4 * i + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) wsv[j] = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.0f;
+          }
+        }
+        if constexpr (EPI != EPI_I32) {
+          if (has_bias) {
+            using BT = typename EO::T;
+            const BT* bp = reinterpret_cast<const BT*>(p.bias) + col0;
+            if (full_chunk && OUT_DT != DT_F32) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 t = __ldg(reinterpret_cast<const uint4*>(bp) + i);
+                const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  if constexpr (OUT_DT == DT_BF16) {
+                    bv[8 * i + 2 * k] = __uint_as_float(w4[k] << 16);
+                    bv[8 * i + 2 * k + 1] = __uint_as_float(w4[k] & 0xFFFF0000u);
+                  } else {
+                    const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+                    bv[8 * i + 2 * k] = f2.x;
+                    bv[8 * i + 2 * k + 1] = f2.y;
+                  }
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) bv[j] = (j < ncols) ? EO::to_f(bp[j]) : 0.0f;
+            }
+          }
+        }
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + acc * BN + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
         tmem_ld_wait();
-        const int col0 = nb * BN + c * 32;
         if (!row_ok || col0 >= p.N) continue;
-        const int ncols = min(32, p.N - col0);
-        const bool full_chunk = (ncols == 32) && vec_ok;
         if constexpr (EPI == EPI_I32) {
           int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
           if (full_chunk) {
@@ -311,21 +364,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float f = __int2float_rn((int32_t)r[j]);  // res.float()
-            const int col = col0 + j;
-            const bool ok = j < ncols;
             float v;
             if constexpr (EPI == EPI_W8A8_TENSOR) {
-              v = EO::round(__fmul_rn(f, s_tensor));
+              v = EO::round(__fmul_rn(f, s_tensor));       // .mul_(ws * xs).to(dt)
+            } else if constexpr (EPI == EPI_W8A8_ROW) {
+              v = EO::round(__fmul_rn(__fmul_rn(f, xs), wsv[j]));  // .mul_(xs).mul_(ws.T).to(dt)
             } else {
-              const float ws = ok ? __ldg(p.w_scale + col) : 0.0f;
-              v = __fmul_rn(__fmul_rn(f, xs), ws);
-              if constexpr (EPI == EPI_W8A8_ROW) v = EO::round(v);
+              v = __fmul_rn(__fmul_rn(f, xs), wsv[j]);     // float32, rounded once below
             }
-            if (p.bias != nullptr) {
-              const float b = ok ? EO::to_f(reinterpret_cast<const typename EO::T*>(p.bias)[col]) : 0.0f;
-              v = __fadd_rn(v, b);
-            }
-            y[j] = EO::round(v);
+            y[j] = v;
+          }
+          if (has_bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = EO::round(__fadd_rn(y[j], bv[j]));
+          } else if constexpr (EPI == EPI_W4A4_ROW) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
           }
           auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
           store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
@@ -338,8 +392,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       if (acc == 0) acc_phase ^= 1;
     }
   } else if constexpr (B_INT4) {
-    // ---------------- int4 -> int8 converters (warps 6..9) ----------------
-    const int ctid = threadIdx.x - 192;
+    // ---------------- int4 -> int8 converters (warps 10..13) ----------------
+    const int ctid = threadIdx.x - 32 * (2 + EPI_WARPS);
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {

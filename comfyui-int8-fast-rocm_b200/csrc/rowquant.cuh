@@ -122,37 +122,70 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
   }
 
   if constexpr (KIND != ROT_NONE) {
+    // Per-thread shared-memory offsets (floats), computed once: natural
+    // order (4 float4 of this lane's chunk) and the stage-2 column set
+    // (R rows x J consecutive floats, accessed as J2-wide vectors).
+    constexpr int J = 16 / R;           // columns handled per thread in stage 2
+    constexpr int J2 = J < 4 ? J : 4;   // vector width of one access
+    constexpr int NQ = J / J2;          // vectors per row
+    int nat[4];
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) nat[q4] = swz<R>(lane * 16 + 4 * q4);
+    int s2[R > 1 ? R : 1][NQ];
+    if constexpr (R > 1) {
+      const int g0 = (lane / R) * (16 * R);
+      const int rp = lane % R;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) s2[r][q] = swz<R>(g0 + 16 * r + rp * J + q * J2);
+    }
 #pragma unroll
     for (int i = 0; i < CHUNKS; ++i) {
       xform_regs<KIND, 16>(v[i]);
       if constexpr (R > 1) {
         // stage 2: Hadamard over the chunk index within each group of R chunks
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float4 f = make_float4(v[i][4 * q4], v[i][4 * q4 + 1], v[i][4 * q4 + 2], v[i][4 * q4 + 3]);
-          *reinterpret_cast<float4*>(wbuf + swz<R>(lane * 16 + 4 * q4)) = f;
-        }
+        for (int q4 = 0; q4 < 4; ++q4)
+          *reinterpret_cast<float4*>(wbuf + nat[q4]) =
+              make_float4(v[i][4 * q4], v[i][4 * q4 + 1], v[i][4 * q4 + 2], v[i][4 * q4 + 3]);
         __syncwarp();
-        constexpr int J = 16 / R;  // columns handled per thread
-        const int g0 = (lane / R) * (16 * R);
-        const int rp = lane % R;
         float w[J][R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
-          for (int jj = 0; jj < J; ++jj) w[jj][r] = wbuf[swz<R>(g0 + 16 * r + rp * J + jj)];
+          for (int q = 0; q < NQ; ++q) {
+            if constexpr (J2 == 4) {
+              const float4 f = *reinterpret_cast<const float4*>(wbuf + s2[r][q]);
+              w[4 * q][r] = f.x; w[4 * q + 1][r] = f.y; w[4 * q + 2][r] = f.z; w[4 * q + 3][r] = f.w;
+            } else if constexpr (J2 == 2) {
+              const float2 f = *reinterpret_cast<const float2*>(wbuf + s2[r][q]);
+              w[0][r] = f.x; w[1][r] = f.y;
+            } else {
+              w[0][r] = wbuf[s2[r][q]];
+            }
+          }
         }
 #pragma unroll
         for (int jj = 0; jj < J; ++jj) xform_regs<KIND, R>(w[jj]);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
-          for (int jj = 0; jj < J; ++jj) wbuf[swz<R>(g0 + 16 * r + rp * J + jj)] = w[jj][r];
+          for (int q = 0; q < NQ; ++q) {
+            if constexpr (J2 == 4) {
+              *reinterpret_cast<float4*>(wbuf + s2[r][q]) =
+                  make_float4(w[4 * q][r], w[4 * q + 1][r], w[4 * q + 2][r], w[4 * q + 3][r]);
+            } else if constexpr (J2 == 2) {
+              *reinterpret_cast<float2*>(wbuf + s2[r][q]) = make_float2(w[0][r], w[1][r]);
+            } else {
+              wbuf[s2[r][q]] = w[0][r];
+            }
+          }
         }
         __syncwarp();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 f = *reinterpret_cast<const float4*>(wbuf + swz<R>(lane * 16 + 4 * q4));
+          const float4 f = *reinterpret_cast<const float4*>(wbuf + nat[q4]);
           v[i][4 * q4] = f.x; v[i][4 * q4 + 1] = f.y; v[i][4 * q4 + 2] = f.z; v[i][4 * q4 + 3] = f.w;
         }
         __syncwarp();
@@ -210,13 +243,24 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
     // ---- absmax ----
     float amax_row = 0.0f;
     float amax_grp[CHUNKS];
+    if constexpr (MODE == MODE_INT8) {
+      // max of |v| as unsigned bit patterns: equals the float max for finite
+      // values and ranks Inf and NaN above every finite value.
+      uint32_t mb = 0;
 #pragma unroll
-    for (int i = 0; i < CHUNKS; ++i) {
-      float a = 0.0f;
+      for (int i = 0; i < CHUNKS; ++i)
 #pragma unroll
-      for (int j = 0; j < 16; ++j) a = fmaxf(a, fabsf(v[i][j]));
-      amax_grp[i] = a;
-      amax_row = fmaxf(amax_row, a);
+        for (int j = 0; j < 16; ++j) mb = max(mb, __float_as_uint(v[i][j]) & 0x7FFFFFFFu);
+      amax_row = __uint_as_float(mb);
+    } else {
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        float a = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a = fmaxf(a, fabsf(v[i][j]));
+        amax_grp[i] = a;
+        amax_row = fmaxf(amax_row, a);
+      }
     }
     if constexpr (MODE == MODE_INT4_G128) {
 #pragma unroll
@@ -225,18 +269,34 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
         for (int o = 1; o < 8; o <<= 1) amax_grp[i] = fmaxf(amax_grp[i], __shfl_xor_sync(0xffffffffu, amax_grp[i], o));
       }
     } else {
+      // unsigned-bit-pattern max (same order as float max for |v|, with
+      // Inf/NaN above all finite values)
+      uint32_t mb = __float_as_uint(amax_row);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax_row = fmaxf(amax_row, __shfl_xor_sync(0xffffffffu, amax_row, o));
+      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
       const int nw = tpr >> 5;
-      if (lane == 0) red[threadIdx.y][warp_in_row] = amax_row;
+      if (lane == 0) red[threadIdx.y][warp_in_row] = __uint_as_float(mb);
       __syncthreads();
-      amax_row = 0.0f;
-      for (int w2 = 0; w2 < nw; ++w2) amax_row = fmaxf(amax_row, red[threadIdx.y][w2]);
+      mb = 0;
+      for (int w2 = 0; w2 < nw; ++w2) mb = max(mb, __float_as_uint(red[threadIdx.y][w2]));
+      amax_row = __uint_as_float(mb);
     }
     if (!row_ok) return;
 
     float s_row = 0.0f, inv_row = 0.0f;
     if constexpr (MODE == MODE_INT8) {
+      const uint32_t ab = __float_as_uint(amax_row);
+      if (ab >= 0x7F800000u) {
+        // Inf or NaN in the row: the reference's scale is Inf / NaN, every
+        // code is a NaN or 0 product and casts to 0.
+        if (t == 0) p.scale[row] = ab == 0x7F800000u ? __uint_as_float(0x7F800000u) : __uint_as_float(0x7FC00000u);
+#pragma unroll
+        for (int i = 0; i < CHUNKS; ++i) {
+          const int ci = t + i * tpr;
+          if (ci < nchunks) *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = make_int4(0, 0, 0, 0);
+        }
+        return;
+      }
       s_row = fmaxf(__fdiv_rn(amax_row, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
       inv_row = __frcp_rn(s_row);                           // 1.0 / scale
       if (t == 0) p.scale[row] = s_row;
@@ -254,14 +314,26 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
         s = EQ::round(__fdiv_rn(fmaxf(amax_grp[i], p.clamp_min), 7.0f));
         if ((ci & 7) == 0) p.scale[(int64_t)row * (p.K >> 7) + (ci >> 3)] = s;
       }
+      if constexpr (MODE == MODE_INT8) {
+        // |v| <= absmax, so |v * (1/scale)| <= 127 * (1 + 3 ulp) and the
+        // round-half-even code is already in [-127, 127]: no clamp needed.
+        // The low byte of (y + 1.5*2^23) is the two's-complement code.
+        uint32_t u[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) u[j] = __float_as_uint(__fadd_rn(__fmul_rn(v[i][j], inv_row), 12582912.0f));
+        int4 o;
+        o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
+        o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
+        o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
+        o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
+        *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+        continue;
+      }
       int qv[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float y;
-        if constexpr (MODE == MODE_INT8) {
-          y = __fmul_rn(v[i][j], inv_row);
-          y = fminf(fmaxf(y, -128.0f), 127.0f);
-        } else {
+        {
           y = EQ::round(__fdiv_rn(v[i][j], s));  // (x / scale) in the compute dtype
           // NaN (0/0 on an all-zero row in f16, where the 1e-10 clamp
           // underflows) converts to code 0, as torch's float->int8 cast does

@@ -90,8 +90,11 @@ def quantize_int8(x: np.ndarray, scale) -> np.ndarray:
     ``1.0 / scale`` on a tensor is ``scale.reciprocal() * 1.0`` (an IEEE
     float32 division), the multiply is float32 RN and ``round_`` is
     round-half-even."""
-    inv = F32(1.0) / np.asarray(scale, dtype=F32)
-    q = np.rint(np.asarray(x, dtype=F32) * inv)
+    with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
+        inv = F32(1.0) / np.asarray(scale, dtype=F32)
+        q = np.rint(np.asarray(x, dtype=F32) * inv)
+    # a NaN product (Inf/NaN rows) casts to int8 code 0, as torch's cast does
+    q = np.where(np.isnan(q), 0, q)
     return np.clip(q, -128, 127).astype(np.int8)
 
 
