@@ -336,4 +336,14 @@ QLIN_API int qlin_requant_int8(const float* w, const float* scale, int scale_mod
                          static_cast<cudaStream_t>(stream));
 }
 
+QLIN_API int qlin_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, void* out, void* stream) {
+  if (M < 0 || K < 0 || ldx < 2 * K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_situ(x_dtype, x, ldx, M, K, out, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -49,6 +49,8 @@ int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const
                              const uint8_t* s_rel, int group_size, int64_t N, int64_t K, int8_t* q, float* scale,
                              cudaStream_t stream);
 
+int launch_situ(int dt, const void* x, int64_t ldx, int64_t M, int64_t K, void* y, cudaStream_t stream);
+
 int read_device_error(cudaStream_t stream, uint32_t* bits);
 
 }  // namespace qlin

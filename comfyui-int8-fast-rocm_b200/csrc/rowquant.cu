@@ -47,8 +47,23 @@ int launch_one(const RowQuantParams& p, const LaunchShape& s, cudaStream_t strea
       attr_devices.fetch_or(bit);
     }
   }
+  // Persistent grid: as many CTAs as fit on the device at once (each walks
+  // several rows), never more than there are row groups.
+  static std::atomic<int> occ_key{-1}, occ_val{1};
+  const int key = s.tpr * s.rpc * 4 + (int)(s.smem >> 10);
+  int per_sm = occ_val.load();
+  if (occ_key.load() != key) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, s.tpr * s.rpc, s.smem);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+    per_sm = nb > 0 ? nb : 1;
+    occ_val.store(per_sm);
+    occ_key.store(key);
+  }
+  const int64_t groups = (p.M + s.rpc - 1) / s.rpc;
+  const int64_t cap = (int64_t)device_sm_count() * per_sm;
   dim3 block(s.tpr, s.rpc);
-  dim3 grid((unsigned)((p.M + s.rpc - 1) / s.rpc));
+  dim3 grid((unsigned)(groups < cap ? groups : cap));
   kern<<<grid, block, s.smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rowquant launch");

@@ -44,21 +44,6 @@ struct RowQuantParams {
   uint64_t seed;         // MODE_REQUANT_SR
 };
 
-template <int DT_IN>
-__device__ __forceinline__ void load_chunk(const void* base, int64_t off, float (&v)[16], float s) {
-  if constexpr (DT_IN == DT_I8) {
-    const int4 t = __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const int8_t*>(base) + off));
-    const uint32_t w[4] = {(uint32_t)t.x, (uint32_t)t.y, (uint32_t)t.z, (uint32_t)t.w};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int b = (int)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFF);
-      v[j] = __fmul_rn((float)b, s);  // dequantize: q.float() * scale
-    }
-  } else {
-    load16<DT_IN>(reinterpret_cast<const typename Elem<DT_IN>::T*>(base) + off, v);
-  }
-}
-
 // Swizzled float index inside a warp's 512-float staging buffer.  XORs the
 // low three bits of the 16-byte chunk index with bits of the chunk index
 // above them, so both the natural-order float4 accesses and the transposed
@@ -87,274 +72,360 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(ab, cd, 0x5410);
 }
 
+// Raw 16-element chunk as loaded from HBM (converted to float only when
+// used, so a prefetched row costs 8 registers for 16-bit inputs).
+template <int DT_IN>
+struct RawChunk {
+  static constexpr int WORDS = DT_IN == DT_F32 ? 16 : (DT_IN == DT_I8 ? 4 : 8);
+  uint32_t w[WORDS];
+};
+
+template <int DT_IN>
+__device__ __forceinline__ void load_raw(const void* base, int64_t off, RawChunk<DT_IN>& r) {
+  constexpr int BYTES = DT_IN == DT_F32 ? 4 : (DT_IN == DT_I8 ? 1 : 2);
+  const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(base) + off * BYTES);
+#pragma unroll
+  for (int i = 0; i < RawChunk<DT_IN>::WORDS / 4; ++i) {
+    const uint4 t = __ldg(q + i);
+    r.w[4 * i] = t.x; r.w[4 * i + 1] = t.y; r.w[4 * i + 2] = t.z; r.w[4 * i + 3] = t.w;
+  }
+}
+
+template <int DT_IN>
+__device__ __forceinline__ void unpack_raw(const RawChunk<DT_IN>& r, float (&v)[16], float s) {
+  if constexpr (DT_IN == DT_F32) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r.w[j]);
+  } else if constexpr (DT_IN == DT_BF16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[2 * j] = __uint_as_float(r.w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(r.w[j] & 0xFFFF0000u);
+    }
+  } else if constexpr (DT_IN == DT_F16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int b = (int)(int8_t)((r.w[j >> 2] >> (8 * (j & 3))) & 0xFF);
+      v[j] = __fmul_rn((float)b, s);  // dequantize: q.float() * scale
+    }
+  }
+}
+
+// Round 16 floats to the compute dtype in pairs (one packed conversion per
+// pair), returning the rounded values as float.
+template <int DT>
+__device__ __forceinline__ void round16(float (&v)[16]) {
+  if constexpr (DT == DT_BF16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+      v[2 * j] = __uint_as_float(u << 16);
+      v[2 * j + 1] = __uint_as_float(u & 0xFFFF0000u);
+    }
+  } else if constexpr (DT == DT_F16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 f = __half22float2(__floats2half2_rn(v[2 * j], v[2 * j + 1]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// max(a, b) that returns NaN when either operand is NaN (torch's amax
+// propagates NaN; fmaxf would drop it).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Persistent row loop: each CTA walks rows blockIdx.x*RPC + k*gridDim.x*RPC,
+// prefetching the next row's chunks into registers while the current one is
+// rotated and quantised; per-thread shared-memory offsets are computed once.
 template <int DT_IN, int DT_Q, int KIND, int R, int CHUNKS, int MODE>
 __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
   using EQ = Elem<DT_Q>;
   extern __shared__ float stage_smem[];  // [warps][512] when R > 1
-  __shared__ float red[32][33];          // per row, per warp partial absmax
+  __shared__ float red[2][32][33];       // [iteration parity][row][warp] partial absmax
 
   const int tpr = blockDim.x;
   const int t = threadIdx.x;
   const int lane = t & 31;
   const int warp_in_row = t >> 5;
-  const int row = blockIdx.x * blockDim.y + threadIdx.y;
-  const bool row_ok = row < p.M;
   const int nchunks = p.K >> 4;
   const int warp_lin = threadIdx.y * (tpr >> 5) + warp_in_row;
   float* wbuf = stage_smem + warp_lin * 512;
   (void)wbuf;
 
-  float in_s = 1.0f;
-  if constexpr (DT_IN == DT_I8) {
-    if (row_ok) in_s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
-  }
-
-  float v[CHUNKS][16];
-#pragma unroll
-  for (int i = 0; i < CHUNKS; ++i) {
-    const int ci = t + i * tpr;
-    if (row_ok && ci < nchunks) {
-      load_chunk<DT_IN>(p.x, (int64_t)row * p.ldx + (int64_t)ci * 16, v[i], in_s);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
-    }
-  }
-
-  if constexpr (KIND != ROT_NONE) {
-    // Per-thread shared-memory offsets (floats), computed once: natural
-    // order (4 float4 of this lane's chunk) and the stage-2 column set
-    // (R rows x J consecutive floats, accessed as J2-wide vectors).
-    constexpr int J = 16 / R;           // columns handled per thread in stage 2
-    constexpr int J2 = J < 4 ? J : 4;   // vector width of one access
-    constexpr int NQ = J / J2;          // vectors per row
-    int nat[4];
+  // ConvRot stage-2 offsets (floats): natural order (4 float4 of this lane's
+  // chunk) and the transposed column set (R rows x J floats, J2-wide vectors).
+  constexpr int J = 16 / R;
+  constexpr int J2 = J < 4 ? J : 4;
+  constexpr int NQ = J / J2;
+  int nat[4];
+  int s2[R > 1 ? R : 1][NQ];
+  if constexpr (KIND != ROT_NONE && R > 1) {
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4) nat[q4] = swz<R>(lane * 16 + 4 * q4);
-    int s2[R > 1 ? R : 1][NQ];
-    if constexpr (R > 1) {
-      const int g0 = (lane / R) * (16 * R);
-      const int rp = lane % R;
+    const int g0 = (lane / R) * (16 * R);
+    const int rp = lane % R;
 #pragma unroll
-      for (int r = 0; r < R; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) s2[r][q] = swz<R>(g0 + 16 * r + rp * J + q * J2);
-    }
+      for (int q = 0; q < NQ; ++q) s2[r][q] = swz<R>(g0 + 16 * r + rp * J + q * J2);
+  }
+
+  const int rows_per_cta = blockDim.y;
+  const int stride_rows = gridDim.x * rows_per_cta;
+  RawChunk<DT_IN> raw[CHUNKS];
+  int first = blockIdx.x * rows_per_cta;
+  {
+    const int row = first + threadIdx.y;
 #pragma unroll
     for (int i = 0; i < CHUNKS; ++i) {
-      xform_regs<KIND, 16>(v[i]);
-      if constexpr (R > 1) {
-        // stage 2: Hadamard over the chunk index within each group of R chunks
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          *reinterpret_cast<float4*>(wbuf + nat[q4]) =
-              make_float4(v[i][4 * q4], v[i][4 * q4 + 1], v[i][4 * q4 + 2], v[i][4 * q4 + 3]);
-        __syncwarp();
-        float w[J][R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-#pragma unroll
-          for (int q = 0; q < NQ; ++q) {
-            if constexpr (J2 == 4) {
-              const float4 f = *reinterpret_cast<const float4*>(wbuf + s2[r][q]);
-              w[4 * q][r] = f.x; w[4 * q + 1][r] = f.y; w[4 * q + 2][r] = f.z; w[4 * q + 3][r] = f.w;
-            } else if constexpr (J2 == 2) {
-              const float2 f = *reinterpret_cast<const float2*>(wbuf + s2[r][q]);
-              w[0][r] = f.x; w[1][r] = f.y;
-            } else {
-              w[0][r] = wbuf[s2[r][q]];
-            }
-          }
-        }
-#pragma unroll
-        for (int jj = 0; jj < J; ++jj) xform_regs<KIND, R>(w[jj]);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-#pragma unroll
-          for (int q = 0; q < NQ; ++q) {
-            if constexpr (J2 == 4) {
-              *reinterpret_cast<float4*>(wbuf + s2[r][q]) =
-                  make_float4(w[4 * q][r], w[4 * q + 1][r], w[4 * q + 2][r], w[4 * q + 3][r]);
-            } else if constexpr (J2 == 2) {
-              *reinterpret_cast<float2*>(wbuf + s2[r][q]) = make_float2(w[0][r], w[1][r]);
-            } else {
-              wbuf[s2[r][q]] = w[0][r];
-            }
-          }
-        }
-        __syncwarp();
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 f = *reinterpret_cast<const float4*>(wbuf + nat[q4]);
-          v[i][4 * q4] = f.x; v[i][4 * q4 + 1] = f.y; v[i][4 * q4 + 2] = f.z; v[i][4 * q4 + 3] = f.w;
-        }
-        __syncwarp();
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[i][j] = EQ::round(__fmul_rn(v[i][j], p.rot_c));
+      const int ci = t + i * tpr;
+      if (row < p.M && ci < nchunks) load_raw<DT_IN>(p.x, (int64_t)row * p.ldx + (int64_t)ci * 16, raw[i]);
     }
   }
 
-  if constexpr (MODE == MODE_ROTATE) {
-    if (row_ok) {
-      auto* out = reinterpret_cast<typename EQ::T*>(p.out) + (int64_t)row * p.K;
+  for (int it = 0; first < p.M; ++it, first += stride_rows) {
+    const int row = first + threadIdx.y;
+    const bool row_ok = row < p.M;
+    float in_s = 1.0f;
+    if constexpr (DT_IN == DT_I8) {
+      if (row_ok) in_s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
+    }
+    float v[CHUNKS][16];
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int ci = t + i * tpr;
+      if (row_ok && ci < nchunks) {
+        unpack_raw<DT_IN>(raw[i], v[i], in_s);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
+      }
+    }
+    // prefetch the next row handled by this thread
+    {
+      const int nrow = row + stride_rows;
 #pragma unroll
       for (int i = 0; i < CHUNKS; ++i) {
         const int ci = t + i * tpr;
-        if (ci < nchunks) store16<DT_Q>(out + (int64_t)ci * 16, v[i]);
+        if (nrow < p.M && ci < nchunks) load_raw<DT_IN>(p.x, (int64_t)nrow * p.ldx + (int64_t)ci * 16, raw[i]);
       }
     }
-    return;
-  } else if constexpr (MODE == MODE_REQUANT || MODE == MODE_REQUANT_SR) {
-    if (!row_ok) return;
-    const float s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
-    const float inv = __frcp_rn(s);
-#pragma unroll
-    for (int i = 0; i < CHUNKS; ++i) {
-      const int ci = t + i * tpr;
-      if (ci >= nchunks) continue;
-      int qv[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float y;
-        if constexpr (MODE == MODE_REQUANT) {
-          y = __fmul_rn(v[i][j], inv);                       // x * (1/scale)
-          y = fminf(fmaxf(y, -128.0f), 127.0f);
-          qv[j] = rint_to_int(y);
-        } else {
-          const float xs = __fdiv_rn(v[i][j], s);            // x / scale
-          const float fl = floorf(xs);
-          const float frac = __fsub_rn(xs, fl);
-          const float u = uniform01(p.seed, (uint64_t)row * p.K + ci * 16 + j);
-          y = (u < frac) ? __fadd_rn(fl, 1.0f) : fl;
-          y = fminf(fmaxf(y, -128.0f), 127.0f);
-          qv[j] = (int)y;
-        }
-      }
-      int4 o;
-      o.x = (int)pack4(qv[0], qv[1], qv[2], qv[3]);
-      o.y = (int)pack4(qv[4], qv[5], qv[6], qv[7]);
-      o.z = (int)pack4(qv[8], qv[9], qv[10], qv[11]);
-      o.w = (int)pack4(qv[12], qv[13], qv[14], qv[15]);
-      *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
-    }
-    return;
-  } else {
-    // ---- absmax ----
-    float amax_row = 0.0f;
-    float amax_grp[CHUNKS];
-    if constexpr (MODE == MODE_INT8) {
-      // max of |v| as unsigned bit patterns: equals the float max for finite
-      // values and ranks Inf and NaN above every finite value.
-      uint32_t mb = 0;
-#pragma unroll
-      for (int i = 0; i < CHUNKS; ++i)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) mb = max(mb, __float_as_uint(v[i][j]) & 0x7FFFFFFFu);
-      amax_row = __uint_as_float(mb);
-    } else {
-#pragma unroll
-      for (int i = 0; i < CHUNKS; ++i) {
-        float a = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) a = fmaxf(a, fabsf(v[i][j]));
-        amax_grp[i] = a;
-        amax_row = fmaxf(amax_row, a);
-      }
-    }
-    if constexpr (MODE == MODE_INT4_G128) {
-#pragma unroll
-      for (int i = 0; i < CHUNKS; ++i) {
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) amax_grp[i] = fmaxf(amax_grp[i], __shfl_xor_sync(0xffffffffu, amax_grp[i], o));
-      }
-    } else {
-      // unsigned-bit-pattern max (same order as float max for |v|, with
-      // Inf/NaN above all finite values)
-      uint32_t mb = __float_as_uint(amax_row);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-      const int nw = tpr >> 5;
-      if (lane == 0) red[threadIdx.y][warp_in_row] = __uint_as_float(mb);
-      __syncthreads();
-      mb = 0;
-      for (int w2 = 0; w2 < nw; ++w2) mb = max(mb, __float_as_uint(red[threadIdx.y][w2]));
-      amax_row = __uint_as_float(mb);
-    }
-    if (!row_ok) return;
 
-    float s_row = 0.0f, inv_row = 0.0f;
-    if constexpr (MODE == MODE_INT8) {
-      const uint32_t ab = __float_as_uint(amax_row);
-      if (ab >= 0x7F800000u) {
-        // Inf or NaN in the row: the reference's scale is Inf / NaN, every
-        // code is a NaN or 0 product and casts to 0.
-        if (t == 0) p.scale[row] = ab == 0x7F800000u ? __uint_as_float(0x7F800000u) : __uint_as_float(0x7FC00000u);
+    if constexpr (KIND != ROT_NONE) {
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        xform_regs<KIND, 16>(v[i]);
+        if constexpr (R > 1) {
+          // stage 2: Hadamard over the chunk index within each group of R chunks
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            *reinterpret_cast<float4*>(wbuf + nat[q4]) =
+                make_float4(v[i][4 * q4], v[i][4 * q4 + 1], v[i][4 * q4 + 2], v[i][4 * q4 + 3]);
+          __syncwarp();
+          float w[J][R];
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) {
+              if constexpr (J2 == 4) {
+                const float4 f = *reinterpret_cast<const float4*>(wbuf + s2[r][q]);
+                w[4 * q][r] = f.x; w[4 * q + 1][r] = f.y; w[4 * q + 2][r] = f.z; w[4 * q + 3][r] = f.w;
+              } else if constexpr (J2 == 2) {
+                const float2 f = *reinterpret_cast<const float2*>(wbuf + s2[r][q]);
+                w[0][r] = f.x; w[1][r] = f.y;
+              } else {
+                w[0][r] = wbuf[s2[r][q]];
+              }
+            }
+          }
+#pragma unroll
+          for (int jj = 0; jj < J; ++jj) xform_regs<KIND, R>(w[jj]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) {
+              if constexpr (J2 == 4) {
+                *reinterpret_cast<float4*>(wbuf + s2[r][q]) =
+                    make_float4(w[4 * q][r], w[4 * q + 1][r], w[4 * q + 2][r], w[4 * q + 3][r]);
+              } else if constexpr (J2 == 2) {
+                *reinterpret_cast<float2*>(wbuf + s2[r][q]) = make_float2(w[0][r], w[1][r]);
+              } else {
+                wbuf[s2[r][q]] = w[0][r];
+              }
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 f = *reinterpret_cast<const float4*>(wbuf + nat[q4]);
+            v[i][4 * q4] = f.x; v[i][4 * q4 + 1] = f.y; v[i][4 * q4 + 2] = f.z; v[i][4 * q4 + 3] = f.w;
+          }
+          __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[i][j] = __fmul_rn(v[i][j], p.rot_c);
+        round16<DT_Q>(v[i]);
+      }
+    }
+
+    if constexpr (MODE == MODE_ROTATE) {
+      if (row_ok) {
+        auto* out = reinterpret_cast<typename EQ::T*>(p.out) + (int64_t)row * p.K;
 #pragma unroll
         for (int i = 0; i < CHUNKS; ++i) {
           const int ci = t + i * tpr;
-          if (ci < nchunks) *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = make_int4(0, 0, 0, 0);
+          if (ci < nchunks) store16<DT_Q>(out + (int64_t)ci * 16, v[i]);
         }
-        return;
       }
-      s_row = fmaxf(__fdiv_rn(amax_row, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
-      inv_row = __frcp_rn(s_row);                           // 1.0 / scale
-      if (t == 0) p.scale[row] = s_row;
-    } else if constexpr (MODE == MODE_INT4_ROW) {
-      s_row = EQ::round(__fdiv_rn(fmaxf(amax_row, p.clamp_min), 7.0f));
-      if (t == 0) p.scale[row] = s_row;
-    }
-
+      continue;
+    } else if constexpr (MODE == MODE_REQUANT || MODE == MODE_REQUANT_SR) {
+      if (!row_ok) continue;
+      const float s = p.in_scale_per_row ? __ldg(p.in_scale + row) : __ldg(p.in_scale);
+      const float inv = __frcp_rn(s);
 #pragma unroll
-    for (int i = 0; i < CHUNKS; ++i) {
-      const int ci = t + i * tpr;
-      if (ci >= nchunks) continue;
-      float s = s_row;
-      if constexpr (MODE == MODE_INT4_G128) {
-        s = EQ::round(__fdiv_rn(fmaxf(amax_grp[i], p.clamp_min), 7.0f));
-        if ((ci & 7) == 0) p.scale[(int64_t)row * (p.K >> 7) + (ci >> 3)] = s;
-      }
-      if constexpr (MODE == MODE_INT8) {
-        // |v| <= absmax, so |v * (1/scale)| <= 127 * (1 + 3 ulp) and the
-        // round-half-even code is already in [-127, 127]: no clamp needed.
-        // The low byte of (y + 1.5*2^23) is the two's-complement code.
-        uint32_t u[16];
+      for (int i = 0; i < CHUNKS; ++i) {
+        const int ci = t + i * tpr;
+        if (ci >= nchunks) continue;
+        int qv[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) u[j] = __float_as_uint(__fadd_rn(__fmul_rn(v[i][j], inv_row), 12582912.0f));
-        int4 o;
-        o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
-        o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
-        o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
-        o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
-        *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
-        continue;
-      }
-      int qv[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float y;
-        {
-          y = EQ::round(__fdiv_rn(v[i][j], s));  // (x / scale) in the compute dtype
-          // NaN (0/0 on an all-zero row in f16, where the 1e-10 clamp
-          // underflows) converts to code 0, as torch's float->int8 cast does
-          y = (y != y) ? 0.0f : fminf(fmaxf(y, -7.0f), 7.0f);
+        for (int j = 0; j < 16; ++j) {
+          float y;
+          if constexpr (MODE == MODE_REQUANT) {
+            y = __fmul_rn(v[i][j], inv);                       // x * (1/scale)
+            y = (y != y) ? 0.0f : fminf(fmaxf(y, -128.0f), 127.0f);
+            qv[j] = rint_to_int(y);
+          } else {
+            const float xs = __fdiv_rn(v[i][j], s);            // x / scale
+            const float fl = floorf(xs);
+            const float frac = __fsub_rn(xs, fl);
+            const float u = uniform01(p.seed, (uint64_t)row * p.K + ci * 16 + j);
+            y = (u < frac) ? __fadd_rn(fl, 1.0f) : fl;
+            y = (y != y) ? 0.0f : fminf(fmaxf(y, -128.0f), 127.0f);
+            qv[j] = (int)y;
+          }
         }
-        qv[j] = rint_to_int(y);
-      }
-      if (MODE != MODE_INT8 && p.out != nullptr) {
-        // packed int4 output [M, K/2]: low nibble = even k
-        uint32_t w2[2] = {0u, 0u};
-#pragma unroll
-        for (int j = 0; j < 16; ++j) w2[j >> 3] |= ((uint32_t)qv[j] & 0xFu) << (4 * (j & 7));
-        *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(p.out) + (int64_t)row * (p.K >> 1) + (int64_t)ci * 8) =
-            make_uint2(w2[0], w2[1]);
-      } else {
         int4 o;
         o.x = (int)pack4(qv[0], qv[1], qv[2], qv[3]);
         o.y = (int)pack4(qv[4], qv[5], qv[6], qv[7]);
         o.z = (int)pack4(qv[8], qv[9], qv[10], qv[11]);
         o.w = (int)pack4(qv[12], qv[13], qv[14], qv[15]);
         *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+      }
+      continue;
+    } else {
+      // ---- absmax ----
+      float amax_row = 0.0f;
+      float amax_grp[CHUNKS];
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        float a = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a = fmax_nan(a, fabsf(v[i][j]));
+        amax_grp[i] = a;
+        amax_row = fmax_nan(amax_row, a);
+      }
+      if constexpr (MODE == MODE_INT4_G128) {
+#pragma unroll
+        for (int i = 0; i < CHUNKS; ++i) {
+#pragma unroll
+          for (int o = 1; o < 8; o <<= 1) amax_grp[i] = fmax_nan(amax_grp[i], __shfl_xor_sync(0xffffffffu, amax_grp[i], o));
+        }
+      } else {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax_row = fmax_nan(amax_row, __shfl_xor_sync(0xffffffffu, amax_row, o));
+        const int nw = tpr >> 5;
+        float (*rb)[33] = red[it & 1];
+        if (lane == 0) rb[threadIdx.y][warp_in_row] = amax_row;
+        __syncthreads();
+        amax_row = rb[threadIdx.y][0];
+        for (int w2 = 1; w2 < nw; ++w2) amax_row = fmax_nan(amax_row, rb[threadIdx.y][w2]);
+      }
+      if (!row_ok) continue;
+
+      float s_row = 0.0f, inv_row = 0.0f;
+      if constexpr (MODE == MODE_INT8) {
+        if (!(amax_row < __uint_as_float(0x7F800000u))) {
+          // Inf or NaN in the row: the reference's scale is Inf / NaN, every
+          // code is a NaN or 0 product and casts to 0.
+          if (t == 0) p.scale[row] = amax_row;
+#pragma unroll
+          for (int i = 0; i < CHUNKS; ++i) {
+            const int ci = t + i * tpr;
+            if (ci < nchunks)
+              *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = make_int4(0, 0, 0, 0);
+          }
+          continue;
+        }
+        s_row = fmaxf(__fdiv_rn(amax_row, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
+        inv_row = __frcp_rn(s_row);                           // 1.0 / scale
+        if (t == 0) p.scale[row] = s_row;
+      } else if constexpr (MODE == MODE_INT4_ROW) {
+        s_row = EQ::round(__fdiv_rn(fmaxf(amax_row, p.clamp_min), 7.0f));
+        if (t == 0) p.scale[row] = s_row;
+      }
+
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        const int ci = t + i * tpr;
+        if (ci >= nchunks) continue;
+        if constexpr (MODE == MODE_INT8) {
+          // |v| <= absmax, so |v * (1/scale)| <= 127 * (1 + 3 ulp) and the
+          // round-half-even code is already in [-127, 127]: no clamp needed.
+          // The low byte of (y + 1.5*2^23) is the two's-complement code.
+          uint32_t u[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) u[j] = __float_as_uint(__fadd_rn(__fmul_rn(v[i][j], inv_row), 12582912.0f));
+          int4 o;
+          o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
+          o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
+          o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
+          o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
+          *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+        } else {
+          float s = s_row;
+          if constexpr (MODE == MODE_INT4_G128) {
+            s = EQ::round(__fdiv_rn(fmaxf(amax_grp[i], p.clamp_min), 7.0f));
+            if ((ci & 7) == 0) p.scale[(int64_t)row * (p.K >> 7) + (ci >> 3)] = s;
+          }
+          int qv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float y = EQ::round(__fdiv_rn(v[i][j], s));  // (x / scale) in the compute dtype
+            // NaN (0/0 on an all-zero row in f16, where the 1e-10 clamp
+            // underflows) converts to code 0, as torch's float->int8 cast does
+            y = (y != y) ? 0.0f : fminf(fmaxf(y, -7.0f), 7.0f);
+            qv[j] = rint_to_int(y);
+          }
+          if (p.out != nullptr) {
+            // packed int4 output [M, K/2]: low nibble = even k
+            uint32_t w2[2] = {0u, 0u};
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w2[j >> 3] |= ((uint32_t)qv[j] & 0xFu) << (4 * (j & 7));
+            *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(p.out) + (int64_t)row * (p.K >> 1) +
+                                      (int64_t)ci * 8) = make_uint2(w2[0], w2[1]);
+          } else {
+            int4 o;
+            o.x = (int)pack4(qv[0], qv[1], qv[2], qv[3]);
+            o.y = (int)pack4(qv[4], qv[5], qv[6], qv[7]);
+            o.z = (int)pack4(qv[8], qv[9], qv[10], qv[11]);
+            o.w = (int)pack4(qv[12], qv[13], qv[14], qv[15]);
+            *reinterpret_cast<int4*>(p.q + (int64_t)row * p.K + (int64_t)ci * 16) = o;
+          }
+        }
       }
     }
   }

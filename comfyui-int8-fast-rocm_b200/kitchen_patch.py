@@ -1,0 +1,94 @@
+"""comfy_kitchen ``int8_linear`` override backed by the sm_100a kernels
+(reference: rocm_int8_kitchen_patch.py).
+
+``int8_linear`` keeps the kitchen op's signature and behaviour
+(rocm_int8_kitchen_patch.py:114-176): SiTU / kitchen input activation,
+shape and scale validation with the same ValueErrors, optional ConvRot
+(fused into the quantisation kernel here), the W8A8 GEMM with per-tensor or
+per-channel weight scale, and kitchen's residual form.  ``apply_patch``
+installs it in kitchen's registry and in the modules that import
+``int8_linear`` directly; it runs on import when comfy_kitchen is present.
+The reference's ROCm architecture gating is not carried over (this build is
+sm_100a-only).
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from . import ops
+from .int8_quant import rot_for_group
+
+log = logging.getLogger("comfyui-int8-fast-b200")
+
+try:
+    import comfy_kitchen.backends.eager.quantization as ck_quant
+    from comfy_kitchen.registry import registry
+except ImportError:  # kitchen absent: the function is still usable directly
+    ck_quant = None
+    registry = None
+
+try:
+    import comfy_kitchen.backends.eager.w4a8_int8 as ck_w4a8_eager
+except ImportError:
+    ck_w4a8_eager = None
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor, bias=None,
+                out_dtype: torch.dtype = torch.bfloat16, convrot: bool = False, convrot_groupsize: int = 256,
+                input_act=None, input_act_weight=None, input_act_eps: float = 0.0, residual=None,
+                residual_scale=None) -> torch.Tensor:
+    if input_act == "situ":
+        x = ops.situ(x)
+        input_act = None
+    if ck_quant is not None:
+        x = ck_quant._apply_input_act(x, input_act, input_act_weight, input_act_eps)
+    elif input_act is not None:
+        raise ValueError(f"input_act={input_act!r} needs comfy_kitchen")
+    if x.shape[-1] != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {weight.shape[-1]}")
+    weight = weight.to(device=x.device).contiguous()
+    weight_scale = weight_scale.to(device=x.device, dtype=torch.float32).reshape(-1)
+    if weight_scale.numel() not in (1, weight.shape[0]):
+        raise ValueError(f"INT8 weight scale must be scalar or per-output-channel, got {tuple(weight_scale.shape)} "
+                         f"for weight shape {tuple(weight.shape)}")
+    rot = None
+    if convrot:
+        if x.shape[-1] % convrot_groupsize != 0:
+            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide input features {x.shape[-1]}")
+        rot = rot_for_group(convrot_groupsize)
+    shape = x.shape
+    xq, xs = ops.quant_act_int8(x.reshape(-1, shape[-1]), rot)
+    out = ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, out_dtype, per_row=weight_scale.numel() > 1)
+    out = out.reshape(*shape[:-1], weight.shape[0])
+    if ck_quant is not None:
+        return ck_quant._apply_residual(out, residual, residual_scale)
+    if residual is not None:
+        out = residual + (out if residual_scale is None else residual_scale * out)
+    return out
+
+
+_original_get_implementation = getattr(registry, "get_implementation", None)
+
+
+def _patched_get_implementation(name, *args, **kwargs):
+    if name == "int8_linear":
+        return int8_linear
+    return _original_get_implementation(name, *args, **kwargs)
+
+
+def apply_patch() -> bool:
+    """Route kitchen's ``int8_linear`` to this build (registry lookup and
+    the modules that bound the function at import time)."""
+    if registry is None:
+        return False
+    registry.get_implementation = _patched_get_implementation
+    ck_quant.int8_linear = int8_linear
+    if ck_w4a8_eager is not None:
+        ck_w4a8_eager.int8_linear = int8_linear
+    log.info("comfy_kitchen int8_linear -> sm_100a kernels")
+    return True
+
+
+apply_patch()

@@ -130,6 +130,21 @@ def rotate(x: torch.Tensor, kind: str, group: int) -> torch.Tensor:
     return out.reshape(shape)
 
 
+def situ(x: torch.Tensor) -> torch.Tensor:
+    """[..., 2K] ([hidden | gate]) -> [..., K] SiTU activation in x.dtype."""
+    k2 = x.shape[-1]
+    if k2 % 2:
+        raise ValueError(f"situ expects an even last dim ([hidden | gate]), got {k2}")
+    K = k2 // 2
+    x2, ldx = _rows(x.reshape(-1, k2))
+    M = x2.shape[0]
+    y = torch.empty((M, K), dtype=x.dtype, device=x.device)
+    if M and K:
+        st = _stream(x2)
+        N.call("qlin_situ", x2.data_ptr(), dtype_code(x.dtype), M, K, ldx, y.data_ptr(), st)
+    return y.reshape(*x.shape[:-1], K)
+
+
 # ---------------------------------------------------------------------------
 # (b) / (c) GEMMs
 # ---------------------------------------------------------------------------

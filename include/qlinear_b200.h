@@ -101,6 +101,13 @@ QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t 
 QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                          int rot_kind, int rot_group, float rot_c, void* out, void* stream);
 
+/* SiTU gated input activation: x[M, 2K] = [hidden | gate] (row stride ldx)
+ * -> out[M, K] = 4 tanh(gate/4) * sigmoid(gate) * 25 tanh(hidden/25),
+ * float32 math, result in x_dtype.  Replaces triton_situ
+ * (int8_fused_kernel.py:389-440), the input_act="situ" prologue of
+ * rocm_int8_linear (rocm_int8_kitchen_patch.py:131-133). */
+QLIN_API int qlin_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, void* out, void* stream);
+
 /* ---- (b) W8A8 GEMM on tcgen05 kind::i8 ------------------------------------ */
 
 /* out[M,N] = epilogue( a[M,K] int8 . w[N,K]^T int8 ) with int32 accumulation.

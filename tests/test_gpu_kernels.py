@@ -374,3 +374,28 @@ def test_empty_inputs(P):
 def test_no_device_error_flag(P):
     torch.cuda.synchronize()
     assert P.ops.device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# SiTU input activation (floating point: tolerance vs a float64 evaluation)
+# ---------------------------------------------------------------------------
+
+
+def _situ_ref(x64):
+    K = x64.shape[-1] // 2
+    h, g = x64[..., :K], x64[..., K:]
+    return 4 * np.tanh(g / 4) / (1 + np.exp(-g)) * 25 * np.tanh(h / 25)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_situ(P, dt):
+    rng = np.random.default_rng(3)
+    x = O.rnd(dt, rng.standard_normal((37, 2 * 200), dtype=np.float32) * np.float32(6.0))
+    x[0, :8] = np.float32(1e-3)  # the small-|x| polynomial branch
+    y = host_f32(P.ops.situ(dev(x, dt)))
+    ref = _situ_ref(x.astype(np.float64))
+    if dt == "f32":
+        np.testing.assert_allclose(y, ref, rtol=2e-6, atol=1e-7)
+    else:  # one rounding to bf16 of a float32 result: within 1 bf16 ulp
+        ulp = np.spacing(np.abs(ref).astype(np.float32)) * 2 ** 16
+        assert (np.abs(y - ref) <= ulp + 1e-30).all()
