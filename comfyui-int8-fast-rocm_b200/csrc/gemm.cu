@@ -1,5 +1,6 @@
 // Host side of the tcgen05 GEMMs: TMA descriptors, tile configuration, launch.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/qlinear_b200.h"
@@ -66,6 +67,44 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
   return QLIN_OK;
 }
 
+template <int EPI, int OUT_DT>
+int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  using Cfg = PairCfg<EPI, OUT_DT>;
+  auto kern = gemm_i8_pair_kernel<EPI, OUT_DT>;
+  static std::atomic<uint64_t> attr_devices{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  cudaError_t e;
+  if (!(attr_devices.load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
+    attr_devices.fetch_or(bit);
+  }
+  const int num_tiles = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN);
+  const int clusters = num_tiles < p.num_sms / 2 ? num_tiles : p.num_sms / 2;
+  kern<<<2 * clusters, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
+  return QLIN_OK;
+}
+
+int dispatch_pair(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                  cudaStream_t s) {
+  if (kind == GEMM_I32) return launch_pair_cfg<EPI_I32, DT_F32>(ta, tb, p, s);
+  if (kind == GEMM_W8A8_ROW) {
+    if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_ROW, DT_BF16>(ta, tb, p, s);
+    if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_ROW, DT_F16>(ta, tb, p, s);
+    if (out_dt == DT_F32) return launch_pair_cfg<EPI_W8A8_ROW, DT_F32>(ta, tb, p, s);
+  }
+  if (kind == GEMM_W8A8_TENSOR) {
+    if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_BF16>(ta, tb, p, s);
+    if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_F16>(ta, tb, p, s);
+    if (out_dt == DT_F32) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_F32>(ta, tb, p, s);
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported GEMM epilogue / output dtype");
+}
+
 template <int BN, bool B_INT4>
 int dispatch_epi(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                  cudaStream_t s) {
@@ -91,6 +130,15 @@ int dispatch_epi(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap&
   return fail(QLIN_ERR_UNSUPPORTED, "unsupported GEMM epilogue / output dtype");
 }
 
+// QLIN_GEMM_NO_PAIR=1 forces the single-CTA kernel (comparison runs).
+bool pair_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_GEMM_NO_PAIR");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
 }  // namespace
 
 int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
@@ -99,9 +147,18 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
   if (M == 0 || N == 0) return QLIN_OK;
   const int sms = device_sm_count();
   if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  CUtensorMap ta, tb;
+  // Large int8 x int8 problems run on CTA pairs (256 x 256 tiles).
+  if (!b_int4 && kind != GEMM_W4A4_ROW && M >= 256 && N >= 256 && sms >= 2 && !pair_disabled()) {
+    int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    GemmParams p{(int)M, (int)N, (int)K, a_scale, w_scale, bias, out, N, sms};
+    return dispatch_pair(kind, out_dt, ta, tb, p, stream);
+  }
   // Narrow outputs waste half a 256-wide tile; use 128 columns there.
   const int BN = (N <= 128) ? 128 : 256;
-  CUtensorMap ta, tb;
   int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (b_int4) {

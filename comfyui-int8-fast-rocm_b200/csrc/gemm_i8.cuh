@@ -157,6 +157,119 @@ __device__ __forceinline__ void unpack_int4_slab(const uint8_t* src, uint8_t* ds
   }
 }
 
+// Epilogue of one 128-row accumulator tile held in TMEM columns
+// [tmem_acc, tmem_acc + BN): this warp converts TMEM lane quarter `quarter`
+// (rows row0 + 32*quarter + lane) and column half `half` (EPI_WARPS == 8).
+// Per-column scales and bias are loaded before the TMEM load so their
+// latency overlaps it; full 32-column chunks take a branch-free path.
+template <int BN, int EPI, int OUT_DT>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int row0, int colt0, int quarter,
+                                              int half, int lane) {
+  using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
+  constexpr int CHUNKS = BN / 32;
+  constexpr int CPW = CHUNKS / 2;  // chunks per warp
+  const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+  const int vec_n = out16 ? 8 : 4;
+  const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(p.w_scale) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+  const bool has_bias = p.bias != nullptr;
+  const int row = row0 + quarter * 32 + lane;
+  const bool row_ok = row < p.M;
+  float xs = 0.0f;
+  if constexpr (EPI != EPI_I32) xs = row_ok ? __ldg(p.a_scale + row) : 0.0f;
+  float s_tensor = 0.0f;
+  if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
+#pragma unroll 1
+  for (int cc = 0; cc < CPW; ++cc) {
+    const int c = half * CPW + cc;
+    const int col0 = colt0 + c * 32;
+    const int ncols = min(32, p.N - col0);
+    const bool full_chunk = (ncols == 32) && vec_ok;
+    float wsv[32];
+    float bv[32];
+    if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) {
+      if (full_chunk) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0) + i);
+          wsv[4 * i] = t.x; wsv[4 * i + 1] = t.y; wsv[4 * i + 2] = t.z; wsv[4 * i + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) wsv[j] = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.0f;
+      }
+    }
+    if constexpr (EPI != EPI_I32) {
+      if (has_bias) {
+        using BT = typename EO::T;
+        const BT* bp = reinterpret_cast<const BT*>(p.bias) + col0;
+        if (full_chunk && OUT_DT != DT_F32) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 t = __ldg(reinterpret_cast<const uint4*>(bp) + i);
+            const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if constexpr (OUT_DT == DT_BF16) {
+                bv[8 * i + 2 * k] = __uint_as_float(w4[k] << 16);
+                bv[8 * i + 2 * k + 1] = __uint_as_float(w4[k] & 0xFFFF0000u);
+              } else {
+                const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+                bv[8 * i + 2 * k] = f2.x;
+                bv[8 * i + 2 * k + 1] = f2.y;
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) bv[j] = (j < ncols) ? EO::to_f(bp[j]) : 0.0f;
+        }
+      }
+    }
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tmem_acc + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
+    tmem_ld_wait();
+    if (!row_ok || col0 >= p.N) continue;
+    if constexpr (EPI == EPI_I32) {
+      int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+      if (full_chunk) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<int4*>(dst)[i] = make_int4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) dst[j] = (int32_t)r[j];
+      }
+    } else {
+      float y[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float f = __int2float_rn((int32_t)r[j]);  // res.float()
+        float v;
+        if constexpr (EPI == EPI_W8A8_TENSOR) {
+          v = EO::round(__fmul_rn(f, s_tensor));       // .mul_(ws * xs).to(dt)
+        } else if constexpr (EPI == EPI_W8A8_ROW) {
+          v = EO::round(__fmul_rn(__fmul_rn(f, xs), wsv[j]));  // .mul_(xs).mul_(ws.T).to(dt)
+        } else {
+          v = __fmul_rn(__fmul_rn(f, xs), wsv[j]);     // float32, rounded once below
+        }
+        y[j] = v;
+      }
+      if (has_bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = EO::round(__fadd_rn(y[j], bv[j]));
+      } else if constexpr (EPI == EPI_W4A4_ROW) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
+      }
+      auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
+      store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
+    }
+  }
+}
+
 template <int BN, int EPI, int OUT_DT, bool B_INT4>
 __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -269,122 +382,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
   mma_done:;
   } else if (warp < 2 + EPI_WARPS) {
     // ---------------- epilogue ----------------
-    // 8 warps: warp & 3 selects the 32-lane TMEM quarter (rows), the warp's
-    // half selects which half of the tile's 32-column chunks it converts.
-    using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
-    constexpr int CHUNKS = BN / 32;
-    constexpr int CPW = CHUNKS / 2;  // chunks per warp
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
-    const int vec_n = out16 ? 8 : 4;
-    const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
-                        ((reinterpret_cast<uintptr_t>(p.w_scale) & 15) == 0) &&
-                        ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
-    const bool has_bias = p.bias != nullptr;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
       if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * GEMM_BM + row_in_tile;
-      const bool row_ok = row < p.M;
-      float xs = 0.0f;
-      if constexpr (EPI != EPI_I32) xs = row_ok ? __ldg(p.a_scale + row) : 0.0f;
-      float s_tensor = 0.0f;
-      if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
-#pragma unroll 1
-      for (int cc = 0; cc < CPW; ++cc) {
-        const int c = half * CPW + cc;
-        const int col0 = nb * BN + c * 32;
-        const int ncols = min(32, p.N - col0);
-        const bool full_chunk = (ncols == 32) && vec_ok;
-        // per-column parameters first, so their latency overlaps the TMEM load
-        float wsv[32];
-        float bv[32];
-        if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) {
-          if (full_chunk) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0) + i);
-              wsv[4 * i] = t.x; wsv[4 * i + 1] = t.y; wsv[4 * i + 2] = t.z; wsv[4 * i + 3] = t.w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) wsv[j] = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.0f;
-          }
-        }
-        if constexpr (EPI != EPI_I32) {
-          if (has_bias) {
-            using BT = typename EO::T;
-            const BT* bp = reinterpret_cast<const BT*>(p.bias) + col0;
-            if (full_chunk && OUT_DT != DT_F32) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint4 t = __ldg(reinterpret_cast<const uint4*>(bp) + i);
-                const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  if constexpr (OUT_DT == DT_BF16) {
-                    bv[8 * i + 2 * k] = __uint_as_float(w4[k] << 16);
-                    bv[8 * i + 2 * k + 1] = __uint_as_float(w4[k] & 0xFFFF0000u);
-                  } else {
-                    const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
-                    bv[8 * i + 2 * k] = f2.x;
-                    bv[8 * i + 2 * k + 1] = f2.y;
-                  }
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) bv[j] = (j < ncols) ? EO::to_f(bp[j]) : 0.0f;
-            }
-          }
-        }
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + acc * BN + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
-        tmem_ld_wait();
-        if (!row_ok || col0 >= p.N) continue;
-        if constexpr (EPI == EPI_I32) {
-          int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
-          if (full_chunk) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              reinterpret_cast<int4*>(dst)[i] = make_int4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) dst[j] = (int32_t)r[j];
-          }
-        } else {
-          float y[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float f = __int2float_rn((int32_t)r[j]);  // res.float()
-            float v;
-            if constexpr (EPI == EPI_W8A8_TENSOR) {
-              v = EO::round(__fmul_rn(f, s_tensor));       // .mul_(ws * xs).to(dt)
-            } else if constexpr (EPI == EPI_W8A8_ROW) {
-              v = EO::round(__fmul_rn(__fmul_rn(f, xs), wsv[j]));  // .mul_(xs).mul_(ws.T).to(dt)
-            } else {
-              v = __fmul_rn(__fmul_rn(f, xs), wsv[j]);     // float32, rounded once below
-            }
-            y[j] = v;
-          }
-          if (has_bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = EO::round(__fadd_rn(y[j], bv[j]));
-          } else if constexpr (EPI == EPI_W4A4_ROW) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
-          }
-          auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
-          store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
-        }
-      }
+      epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * GEMM_BM, nb * BN, quarter, half, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -415,6 +422,161 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a 2-CTA cluster computes a 256 x 256 tile.
+// Each CTA TMA-loads its own 128 rows of A and its own 128 rows of B (no
+// multicast loads); the leader's single MMA thread issues M=256, N=256
+// tcgen05.mma that read both CTAs' shared memory, each CTA's TMEM receiving
+// its 128 output rows.  Per SM this streams 32 KB per 128-deep K step
+// instead of 48 KB, so the L2 feed keeps up with the tensor cores.
+//   full[s]   leader only: one expect_tx arrival (both CTAs' bytes)
+//   empty[s]  both CTAs: the leader's commit multicasts to the pair
+//   tfull[b]  both CTAs: multicast commit at tile end
+//   tempty[b] leader only: 8 local + 8 remote epilogue-warp arrivals
+// ---------------------------------------------------------------------------
+template <int EPI, int OUT_DT>
+struct PairCfg {
+  static constexpr int BN = 256;           // tile columns (both CTAs)
+  static constexpr int BNH = 128;          // B rows loaded per CTA
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
+  static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
+  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+template <int EPI, int OUT_DT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>::NUM_THREADS, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmParams p) {
+  using Cfg = PairCfg<EPI, OUT_DT>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;     // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int arow = mb * 2 * GEMM_BM + (int)rank * GEMM_BM;
+        const int brow = nb * BN + (int)rank * Cfg::BNH;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
+          tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_i8(2 * GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) goto mma_done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) goto mma_done;
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 32; ++k) umma_i8_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  mma_done:;
+  } else {
+    // ---------------- epilogue (both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * 2 * GEMM_BM + (int)rank * GEMM_BM, nb * BN,
+                                     quarter, half, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // all MMAs done and all remote arrivals delivered
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
