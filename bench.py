@@ -71,57 +71,70 @@ def make_inputs(rows, device, seed=SEED):
     return xt, wt, bt
 
 
+_SAMPLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+          pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    time.sleep(0.001)
+"""
+
+
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled through NVML in a
-    background thread while the timed region runs (read-only queries)."""
+    """SM clock and clock-event (throttle) reasons, sampled through NVML by a
+    separate process (read-only queries; a thread would contend for the GIL
+    with the launch loop) while the timed region runs."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index, period_s=0.005):
-        self.gpu, self.period = gpu_index, period_s
-        self.samples, self.max_mhz, self.err = [], None, None
-
-    def _run(self):
-        import pynvml
-        while not self._stop.is_set():
-            try:
-                sm = pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((sm, rs))
-            except Exception as e:  # pragma: no cover
-                self.err = str(e)
-                return
-            self._stop.wait(self.period)
+    def __init__(self, gpu_index):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ids = vis.split(",") if vis else []
+        self.nvml_index = int(ids[gpu_index]) if len(ids) > gpu_index and ids[gpu_index].isdigit() else gpu_index
+        self.proc, self.lines = None, []
 
     def __enter__(self):
-        import threading
-        self._stop = threading.Event()
-        self.thread = None
+        import subprocess
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-            idx = int(vis.split(",")[self.gpu]) if vis and vis.split(",")[0].isdigit() else self.gpu
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.thread = threading.Thread(target=self._run, daemon=True)
-            self.thread.start()
-        except Exception as e:
-            self.err = str(e)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.nvml_index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc.stdout.readline()  # wait until sampling has started
+        except Exception:
+            self.proc = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = out.splitlines()
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "error": self.err}
-        reasons = sorted({k for _, rs in self.samples for k, bit in self.REASONS.items() if rs & bit})
-        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples)}
+        samples = []
+        for ln in self.lines:
+            parts = ln.split()
+            if len(parts) == 2 and parts[0].isdigit() and parts[1].isdigit():
+                samples.append((int(parts[0]), int(parts[1])))
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(pynvml.nvmlDeviceGetHandleByIndex(self.nvml_index),
+                                                  pynvml.NVML_CLOCK_SM)
+        except Exception:
+            mx = None
+        reasons = sorted({k for _, rs in samples for k, bit in self.REASONS.items() if rs & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in samples), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(samples)}
 
 
 def cpu_baseline(min_seconds=10.0, max_runs=60):

@@ -73,6 +73,15 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 128;  // bytes (= int8 elements) of K per stage
 constexpr int EPI_WARPS = 8;  // epilogue warps (2 per TMEM lane quarter)
 
+// Per-tile epilogue parameters (float weight scales and bias of the tile's
+// columns), double-buffered by tile parity, in shared memory after the
+// barriers.
+template <int BN>
+struct EpiSmem {
+  float ws[2][BN];
+  float bias[2][BN];
+};
+
 template <int BN, bool B_INT4>
 struct GemmCfg {
   static constexpr int STAGES = B_INT4 ? 3 : 4;
@@ -80,7 +89,7 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * GEMM_BK;
   static constexpr int BP_BYTES = B_INT4 ? BN * (GEMM_BK / 2) : 0;  // packed staging
   static constexpr int NUM_THREADS = B_INT4 ? 448 : 320;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256 + 16 + sizeof(EpiSmem<BN>);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
@@ -157,27 +166,45 @@ __device__ __forceinline__ void unpack_int4_slab(const uint8_t* src, uint8_t* ds
   }
 }
 
+// Per-tile epilogue parameters staged in shared memory by the epilogue warps
+// one tile ahead (weight scales and bias of the tile's columns as float, and
+// each thread's activation-row scale in a register), so no global load
+// latency sits between the TMEM load and the stores.
+
+// Named barrier among the 8 epilogue warps only.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory"); }
+
+// Load this thread's share of a tile's per-column parameters (thread e of
+// the epilogue handles column colt0 + e) into registers.
+template <int BN, int EPI, int OUT_DT>
+__device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, int e, float& ws, float& b) {
+  ws = 0.0f;
+  b = 0.0f;
+  if (e >= BN) return;
+  const int col = colt0 + e;
+  if (col >= p.N) return;
+  if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) ws = __ldg(p.w_scale + col);
+  if constexpr (EPI != EPI_I32) {
+    if (p.bias != nullptr) b = Elem<OUT_DT>::to_f(reinterpret_cast<const typename Elem<OUT_DT>::T*>(p.bias)[col]);
+  }
+}
+
 // Epilogue of one 128-row accumulator tile held in TMEM columns
 // [tmem_acc, tmem_acc + BN): this warp converts TMEM lane quarter `quarter`
-// (rows row0 + 32*quarter + lane) and column half `half` (EPI_WARPS == 8).
-// Per-column scales and bias are loaded before the TMEM load so their
-// latency overlaps it; full 32-column chunks take a branch-free path.
+// (rows row0 + 32*quarter + lane) and column half `half` (EPI_WARPS == 8),
+// with the tile's per-column parameters in shared memory (s_ws, s_b).
 template <int BN, int EPI, int OUT_DT>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int row0, int colt0, int quarter,
-                                              int half, int lane) {
+                                              int half, int lane, const float* s_ws, const float* s_b, float xs) {
   using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
   constexpr int CHUNKS = BN / 32;
   constexpr int CPW = CHUNKS / 2;  // chunks per warp
   const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
   const int vec_n = out16 ? 8 : 4;
-  const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0) &&
-                      ((reinterpret_cast<uintptr_t>(p.w_scale) & 15) == 0) &&
-                      ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+  const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
   const bool has_bias = p.bias != nullptr;
   const int row = row0 + quarter * 32 + lane;
   const bool row_ok = row < p.M;
-  float xs = 0.0f;
-  if constexpr (EPI != EPI_I32) xs = row_ok ? __ldg(p.a_scale + row) : 0.0f;
   float s_tensor = 0.0f;
   if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
 #pragma unroll 1
@@ -186,47 +213,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
     const int col0 = colt0 + c * 32;
     const int ncols = min(32, p.N - col0);
     const bool full_chunk = (ncols == 32) && vec_ok;
-    float wsv[32];
-    float bv[32];
-    if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) {
-      if (full_chunk) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 t = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0) + i);
-          wsv[4 * i] = t.x; wsv[4 * i + 1] = t.y; wsv[4 * i + 2] = t.z; wsv[4 * i + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) wsv[j] = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.0f;
-      }
-    }
-    if constexpr (EPI != EPI_I32) {
-      if (has_bias) {
-        using BT = typename EO::T;
-        const BT* bp = reinterpret_cast<const BT*>(p.bias) + col0;
-        if (full_chunk && OUT_DT != DT_F32) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 t = __ldg(reinterpret_cast<const uint4*>(bp) + i);
-            const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if constexpr (OUT_DT == DT_BF16) {
-                bv[8 * i + 2 * k] = __uint_as_float(w4[k] << 16);
-                bv[8 * i + 2 * k + 1] = __uint_as_float(w4[k] & 0xFFFF0000u);
-              } else {
-                const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
-                bv[8 * i + 2 * k] = f2.x;
-                bv[8 * i + 2 * k + 1] = f2.y;
-              }
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) bv[j] = (j < ncols) ? EO::to_f(bp[j]) : 0.0f;
-        }
-      }
-    }
     uint32_t r[32];
     tmem_ld_32x32b_x32(tmem_acc + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
     tmem_ld_wait();
@@ -243,23 +229,40 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
           if (j < ncols) dst[j] = (int32_t)r[j];
       }
     } else {
+      const float4* w4 = reinterpret_cast<const float4*>(s_ws + c * 32);
+      const float4* b4 = reinterpret_cast<const float4*>(s_b + c * 32);
       float y[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float f = __int2float_rn((int32_t)r[j]);  // res.float()
-        float v;
-        if constexpr (EPI == EPI_W8A8_TENSOR) {
-          v = EO::round(__fmul_rn(f, s_tensor));       // .mul_(ws * xs).to(dt)
-        } else if constexpr (EPI == EPI_W8A8_ROW) {
-          v = EO::round(__fmul_rn(__fmul_rn(f, xs), wsv[j]));  // .mul_(xs).mul_(ws.T).to(dt)
-        } else {
-          v = __fmul_rn(__fmul_rn(f, xs), wsv[j]);     // float32, rounded once below
+      for (int i = 0; i < 8; ++i) {
+        float wv[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (EPI != EPI_W8A8_TENSOR) {
+          const float4 t = w4[i];
+          wv[0] = t.x; wv[1] = t.y; wv[2] = t.z; wv[3] = t.w;
         }
-        y[j] = v;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = 4 * i + k;
+          const float f = __int2float_rn((int32_t)r[j]);  // res.float()
+          float v;
+          if constexpr (EPI == EPI_W8A8_TENSOR) {
+            v = EO::round(__fmul_rn(f, s_tensor));             // .mul_(ws * xs).to(dt)
+          } else if constexpr (EPI == EPI_W8A8_ROW) {
+            v = EO::round(__fmul_rn(__fmul_rn(f, xs), wv[k]));  // .mul_(xs).mul_(ws.T).to(dt)
+          } else {
+            v = __fmul_rn(__fmul_rn(f, xs), wv[k]);            // float32, rounded once below
+          }
+          y[j] = v;
+        }
       }
       if (has_bias) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = EO::round(__fadd_rn(y[j], bv[j]));
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = b4[i];
+          y[4 * i] = EO::round(__fadd_rn(y[4 * i], t.x));
+          y[4 * i + 1] = EO::round(__fadd_rn(y[4 * i + 1], t.y));
+          y[4 * i + 2] = EO::round(__fadd_rn(y[4 * i + 2], t.z));
+          y[4 * i + 3] = EO::round(__fadd_rn(y[4 * i + 3], t.w));
+        }
       } else if constexpr (EPI == EPI_W4A4_ROW) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
@@ -267,6 +270,65 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
       auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
       store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
     }
+  }
+}
+
+// The epilogue role of a GEMM kernel: for each tile of this CTA, wait for the
+// accumulator, convert it, release it.  Parameters of tile i+1 are loaded into
+// registers while tile i is converted and staged into shared memory after it.
+// All epilogue threads pass the named barrier every tile and leave together
+// when any wait timed out (the abort flag is read after the barrier).
+template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR>
+__device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* es, uint64_t* tfull, uint64_t* tempty,
+                                              volatile int* abort_flag, uint32_t tmem_base, int first_tile,
+                                              int tile_stride, int num_tiles, int num_m, int num_n, int row_off,
+                                              int warp, int lane) {
+  const int e = (warp - 2) * 32 + lane;  // 0..255
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  float nws, nb, nxs = 0.0f;
+  int buf = 0;
+  if (first_tile < num_tiles) {
+    int mb, nb_;
+    tile_coords(first_tile, num_m, num_n, mb, nb_);
+    epi_load_params<BN, EPI, OUT_DT>(p, nb_ * BN, e, nws, nb);
+    const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
+    if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+    if (e < BN) { es->ws[0][e] = nws; es->bias[0][e] = nb; }
+  }
+  for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
+    int mb, nbk;
+    tile_coords(tile, num_m, num_n, mb, nbk);
+    const float xs = nxs;
+    mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag);
+    epi_bar();
+    if (*abort_flag) break;
+    tc_fence_after();
+    const int next = tile + tile_stride;
+    if (next < num_tiles) {
+      int mb2, nb2;
+      tile_coords(next, num_m, num_n, mb2, nb2);
+      epi_load_params<BN, EPI, OUT_DT>(p, nb2 * BN, e, nws, nb);
+      const int row = mb2 * ROWS_PER_TILE + row_off + quarter * 32 + lane;
+      if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+    }
+    epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter, half,
+                                   lane, es->ws[buf], es->bias[buf], xs);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (PAIR) {
+        mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      } else {
+        mbar_arrive(&tempty[acc]);
+      }
+    }
+    buf ^= 1;
+    if (next < num_tiles && e < BN) { es->ws[buf][e] = nws; es->bias[buf][e] = nb; }
+    acc ^= 1;
+    if (acc == 0) acc_phase ^= 1;
   }
 }
 
@@ -382,22 +444,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
   mma_done:;
   } else if (warp < 2 + EPI_WARPS) {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) break;
-      tc_fence_after();
-      epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * GEMM_BM, nb * BN, quarter, half, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
-    }
+    EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
+    epilogue_role<BN, EPI, OUT_DT, GEMM_BM, false>(p, es, tfull, tempty, abort_flag, tmem_base, blockIdx.x, gridDim.x,
+                                                   num_tiles, num_m, num_n, 0, warp, lane);
   } else if constexpr (B_INT4) {
     // ---------------- int4 -> int8 converters (warps 10..13) ----------------
     const int ctid = threadIdx.x - 32 * (2 + EPI_WARPS);
@@ -445,7 +494,7 @@ struct PairCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
   static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + 256 + 16 + sizeof(EpiSmem<BN>);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
@@ -553,23 +602,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
   mma_done:;
   } else {
     // ---------------- epilogue (both CTAs) ----------------
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) break;
-      tc_fence_after();
-      epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * 2 * GEMM_BM + (int)rank * GEMM_BM, nb * BN,
-                                     quarter, half, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
-    }
+    EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
+    epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
+                                                      num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
+                                                      lane);
   }
 
   tc_fence_before();
