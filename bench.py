@@ -227,7 +227,7 @@ def run_ours(args):
             flush.zero_()
             # keep the GPU busy while the host enqueues the step, so the
             # events time kernels, not host launch latency
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(1_000_000)
             ev[i][0].record(s)
             xq, xs = ops.quant_act_int8(x, rot)
             ev[i][1].record(s)

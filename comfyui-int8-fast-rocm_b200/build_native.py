@@ -22,7 +22,11 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libqlinear_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-         "--expt-relaxed-constexpr", "-DNDEBUG"]
+         "--expt-relaxed-constexpr", "-DNDEBUG",
+         # no implicit multiply-add contraction: the quantisers and epilogues
+         # reproduce two-rounding float32 sequences bit for bit (explicit
+         # fma / __fmaf_rn / fma.rn.f32x2 still issue fused operations)
+         "-fmad=false"]
 SOURCES = ["abi.cu", "rowquant.cu", "gemm.cu", "weights.cu"]
 
 
@@ -44,6 +48,7 @@ def build(jobs: int = 8, verbose: bool = False, ptxas_v: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     headers.append(os.path.join(os.path.dirname(HERE), "include", "qlinear_b200.h"))
+    headers.append(os.path.abspath(__file__))  # a flag change rebuilds everything
     cc = nvcc()
     cmds, objs = [], []
     for src in SOURCES:

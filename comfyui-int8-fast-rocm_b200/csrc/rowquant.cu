@@ -117,6 +117,56 @@ int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s,
   return fail(QLIN_ERR_UNSUPPORTED, "unsupported dtype/mode combination");
 }
 
+// Activation int8 quantisation, two chunks per thread (rowquant_pair_kernel).
+template <int DT, int KIND, int R>
+int launch_pair(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
+  auto kern = rowquant_pair_kernel<DT, KIND, R>;
+  const int per = (nchunks + 1) / 2;
+  const int tpr = ((per + 31) / 32) * 32;
+  int rpc = 256 / tpr;
+  if (rpc < 1) rpc = 1;
+  const size_t smem = (KIND != ROT_NONE && R > 1) ? (size_t)(rpc * tpr / 32) * 1024 * sizeof(float) : 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<uint64_t> attr_devices{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if (smem > 0 && !(attr_devices.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant pair)");
+    attr_devices.fetch_or(bit);
+  }
+  static std::atomic<int> occ_key{-1}, occ_val{1};
+  const int key = tpr * rpc * 4 + (int)(smem >> 10);
+  int per_sm = occ_val.load();
+  if (occ_key.load() != key) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, tpr * rpc, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+    per_sm = nb > 0 ? nb : 1;
+    occ_val.store(per_sm);
+    occ_key.store(key);
+  }
+  const int64_t groups = (p.M + rpc - 1) / rpc;
+  const int64_t cap = (int64_t)device_sm_count() * per_sm;
+  kern<<<dim3((unsigned)(groups < cap ? groups : cap)), dim3(tpr, rpc), smem, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rowquant pair launch");
+  return QLIN_OK;
+}
+
+template <int DT>
+int pair_by_rot(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
+  switch (rc) {
+    case RC_NONE: return launch_pair<DT, ROT_NONE, 1>(p, nchunks, s);
+    case RC_REG16: return launch_pair<DT, ROT_REGULAR, 1>(p, nchunks, s);
+    case RC_REG64: return launch_pair<DT, ROT_REGULAR, 4>(p, nchunks, s);
+    case RC_REG256: return launch_pair<DT, ROT_REGULAR, 16>(p, nchunks, s);
+    case RC_SYL32: return launch_pair<DT, ROT_SYLVESTER, 2>(p, nchunks, s);
+    case RC_SYL128: return launch_pair<DT, ROT_SYLVESTER, 8>(p, nchunks, s);
+    default: return fail(QLIN_ERR_UNSUPPORTED, "unsupported rotation");
+  }
+}
+
 }  // namespace
 
 int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t M, int64_t K, float rot_c,
@@ -136,12 +186,20 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
   p.scale = scale;
   p.out = out;
   p.seed = seed;
+  p.one = 1.0f;
 
   const RotCode rc = rot_code(L.rot_kind, L.rot_group);
   if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
 
   const int64_t nchunks = K / 16;
   if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  // Activation int8 hot path (1024 <= K <= 16384): two chunks per thread in
+  // packed f32x2 lanes.
+  if (L.mode == MODE_INT8 && L.dt_in == L.dt_q && nchunks >= 64 && nchunks <= 1024) {
+    if (L.dt_in == DT_BF16) return pair_by_rot<DT_BF16>(rc, p, (int)nchunks, stream);
+    if (L.dt_in == DT_F16) return pair_by_rot<DT_F16>(rc, p, (int)nchunks, stream);
+    if (L.dt_in == DT_F32) return pair_by_rot<DT_F32>(rc, p, (int)nchunks, stream);
+  }
   LaunchShape s;
   s.chunks = nchunks <= 1024 ? 1 : 2;
   const int64_t per = (nchunks + s.chunks - 1) / s.chunks;

@@ -42,6 +42,7 @@ struct RowQuantParams {
   void* out;             // MODE_ROTATE output [M, K] in the compute dtype,
                          // or packed int4 codes [M, K/2] for the int4 modes
   uint64_t seed;         // MODE_REQUANT_SR
+  float one;             // 1.0f, unknown to the compiler (see rowquant_pair_kernel)
 };
 
 // Swizzled float index inside a warp's 512-float staging buffer.  XORs the
@@ -427,6 +428,257 @@ __global__ void __launch_bounds__(1024) rowquant_kernel(RowQuantParams p) {
           }
         }
       }
+    }
+  }
+}
+
+// Paired-chunk per-token int8 kernel (the activation hot path).  Each thread
+// owns chunks t and t + TPR of its row and keeps element j of both in one
+// float2, so the butterflies, the normalisation and the quantiser issue as
+// packed f32x2 instructions (two independent IEEE float32 operations per
+// instruction, each rounded exactly like its scalar form).
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+  return f2_fma(b, make_float2(-1.0f, -1.0f), a);  // RN(a - b)
+}
+__device__ __forceinline__ void h4_regular2(float2& a0, float2& a1, float2& a2, float2& a3) {
+  const float2 m2 = make_float2(-2.0f, -2.0f);
+  const float2 s = f2_add(f2_add(a0, a1), f2_add(a2, a3));
+  const float2 y0 = f2_fma(a3, m2, s);  // RN(S - 2 a3); 2a is exact
+  const float2 y1 = f2_fma(a2, m2, s);
+  const float2 y2 = f2_fma(a1, m2, s);
+  const float2 y3 = f2_fma(a0, m2, s);
+  a0 = y0; a1 = y1; a2 = y2; a3 = y3;
+}
+__device__ __forceinline__ void h2_sylvester2(float2& a0, float2& a1) {
+  const float2 y0 = f2_add(a0, a1);
+  const float2 y1 = f2_sub(a0, a1);
+  a0 = y0; a1 = y1;
+}
+template <int KIND, int N>
+__device__ __forceinline__ void xform_regs2(float2* v) {
+  if constexpr (KIND == ROT_REGULAR) {
+    static_assert(N == 4 || N == 16, "regular Hadamard digits are base 4");
+#pragma unroll
+    for (int stride = 1; stride < N; stride *= 4)
+#pragma unroll
+      for (int base = 0; base < N; base += 4 * stride)
+#pragma unroll
+        for (int o = 0; o < stride; ++o)
+          h4_regular2(v[base + o], v[base + o + stride], v[base + o + 2 * stride], v[base + o + 3 * stride]);
+  } else if constexpr (KIND == ROT_SYLVESTER) {
+#pragma unroll
+    for (int stride = 1; stride < N; stride *= 2)
+#pragma unroll
+      for (int base = 0; base < N; base += 2 * stride)
+#pragma unroll
+        for (int o = 0; o < stride; ++o) h2_sylvester2(v[base + o], v[base + o + stride]);
+  }
+}
+
+template <int DT, int KIND, int R>
+__global__ void __launch_bounds__(512) rowquant_pair_kernel(RowQuantParams p) {
+  extern __shared__ float stage_smem[];  // [warps][2][512] when R > 1
+  __shared__ float red[2][32][33];
+
+  const int tpr = blockDim.x;
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp_in_row = t >> 5;
+  const int nchunks = p.K >> 4;
+  const int ciA = t, ciB = t + tpr;
+  const bool hasA = ciA < nchunks, hasB = ciB < nchunks;
+  const int warp_lin = threadIdx.y * (tpr >> 5) + warp_in_row;
+  float* bufA = stage_smem + warp_lin * 1024;
+  float* bufB = bufA + 512;
+  (void)bufA; (void)bufB;
+
+  constexpr int J = 16 / R;
+  constexpr int J2 = J < 4 ? J : 4;
+  constexpr int NQ = J / J2;
+  int nat[4];
+  int s2[R > 1 ? R : 1][NQ];
+  if constexpr (KIND != ROT_NONE && R > 1) {
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) nat[q4] = swz<R>(lane * 16 + 4 * q4);
+    const int g0 = (lane / R) * (16 * R);
+    const int rp = lane % R;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) s2[r][q] = swz<R>(g0 + 16 * r + rp * J + q * J2);
+  }
+  const float2 c2 = make_float2(p.rot_c, p.rot_c);
+
+  const int rows_per_cta = blockDim.y;
+  const int stride_rows = gridDim.x * rows_per_cta;
+  RawChunk<DT> rawA, rawB;
+  int first = blockIdx.x * rows_per_cta;
+  {
+    const int row = first + threadIdx.y;
+    if (row < p.M && hasA) load_raw<DT>(p.x, (int64_t)row * p.ldx + (int64_t)ciA * 16, rawA);
+    if (row < p.M && hasB) load_raw<DT>(p.x, (int64_t)row * p.ldx + (int64_t)ciB * 16, rawB);
+  }
+
+  for (int it = 0; first < p.M; ++it, first += stride_rows) {
+    const int row = first + threadIdx.y;
+    const bool row_ok = row < p.M;
+    float2 v[16];
+    {
+      float va[16], vb[16];
+      if (row_ok && hasA) {
+        unpack_raw<DT>(rawA, va, 1.0f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) va[j] = 0.0f;
+      }
+      if (row_ok && hasB) {
+        unpack_raw<DT>(rawB, vb, 1.0f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) vb[j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = make_float2(va[j], vb[j]);
+    }
+    {
+      const int nrow = row + stride_rows;
+      if (nrow < p.M && hasA) load_raw<DT>(p.x, (int64_t)nrow * p.ldx + (int64_t)ciA * 16, rawA);
+      if (nrow < p.M && hasB) load_raw<DT>(p.x, (int64_t)nrow * p.ldx + (int64_t)ciB * 16, rawB);
+    }
+
+    if constexpr (KIND != ROT_NONE) {
+      xform_regs2<KIND, 16>(v);
+      if constexpr (R > 1) {
+        // stage 2 for both chunks: same swizzled transpose as rowquant_kernel,
+        // one 512-float region per chunk
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          *reinterpret_cast<float4*>(bufA + nat[q4]) =
+              make_float4(v[4 * q4].x, v[4 * q4 + 1].x, v[4 * q4 + 2].x, v[4 * q4 + 3].x);
+          *reinterpret_cast<float4*>(bufB + nat[q4]) =
+              make_float4(v[4 * q4].y, v[4 * q4 + 1].y, v[4 * q4 + 2].y, v[4 * q4 + 3].y);
+        }
+        __syncwarp();
+        float2 w[J][R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            if constexpr (J2 == 4) {
+              const float4 fa = *reinterpret_cast<const float4*>(bufA + s2[r][q]);
+              const float4 fb = *reinterpret_cast<const float4*>(bufB + s2[r][q]);
+              w[4 * q][r] = make_float2(fa.x, fb.x); w[4 * q + 1][r] = make_float2(fa.y, fb.y);
+              w[4 * q + 2][r] = make_float2(fa.z, fb.z); w[4 * q + 3][r] = make_float2(fa.w, fb.w);
+            } else if constexpr (J2 == 2) {
+              const float2 fa = *reinterpret_cast<const float2*>(bufA + s2[r][q]);
+              const float2 fb = *reinterpret_cast<const float2*>(bufB + s2[r][q]);
+              w[0][r] = make_float2(fa.x, fb.x); w[1][r] = make_float2(fa.y, fb.y);
+            } else {
+              w[0][r] = make_float2(bufA[s2[r][q]], bufB[s2[r][q]]);
+            }
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) xform_regs2<KIND, R>(w[jj]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            if constexpr (J2 == 4) {
+              *reinterpret_cast<float4*>(bufA + s2[r][q]) =
+                  make_float4(w[4 * q][r].x, w[4 * q + 1][r].x, w[4 * q + 2][r].x, w[4 * q + 3][r].x);
+              *reinterpret_cast<float4*>(bufB + s2[r][q]) =
+                  make_float4(w[4 * q][r].y, w[4 * q + 1][r].y, w[4 * q + 2][r].y, w[4 * q + 3][r].y);
+            } else if constexpr (J2 == 2) {
+              *reinterpret_cast<float2*>(bufA + s2[r][q]) = make_float2(w[0][r].x, w[1][r].x);
+              *reinterpret_cast<float2*>(bufB + s2[r][q]) = make_float2(w[0][r].y, w[1][r].y);
+            } else {
+              bufA[s2[r][q]] = w[0][r].x;
+              bufB[s2[r][q]] = w[0][r].y;
+            }
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 fa = *reinterpret_cast<const float4*>(bufA + nat[q4]);
+          const float4 fb = *reinterpret_cast<const float4*>(bufB + nat[q4]);
+          v[4 * q4] = make_float2(fa.x, fb.x); v[4 * q4 + 1] = make_float2(fa.y, fb.y);
+          v[4 * q4 + 2] = make_float2(fa.z, fb.z); v[4 * q4 + 3] = make_float2(fa.w, fb.w);
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[j] = f2_mul(v[j], c2);
+        if constexpr (DT == DT_BF16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v[j].x, v[j].y);
+          const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+          v[j] = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+        } else if constexpr (DT == DT_F16) {
+          v[j] = __half22float2(__floats2half2_rn(v[j].x, v[j].y));
+        }
+      }
+    }
+
+    // per-row absmax (NaN-propagating)
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmax_nan(fmax_nan(amax, fabsf(v[j].x)), fabsf(v[j].y));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    {
+      const int nw = tpr >> 5;
+      float (*rb)[33] = red[it & 1];
+      if (lane == 0) rb[threadIdx.y][warp_in_row] = amax;
+      __syncthreads();
+      amax = rb[threadIdx.y][0];
+      for (int w2 = 1; w2 < nw; ++w2) amax = fmax_nan(amax, rb[threadIdx.y][w2]);
+    }
+    if (!row_ok) continue;
+    int8_t* qrow = p.q + (int64_t)row * p.K;
+    if (!(amax < __uint_as_float(0x7F800000u))) {
+      // Inf or NaN in the row: scale Inf / NaN and every code 0 (torch's result)
+      if (t == 0) p.scale[row] = amax;
+      if (hasA) *reinterpret_cast<int4*>(qrow + (int64_t)ciA * 16) = make_int4(0, 0, 0, 0);
+      if (hasB) *reinterpret_cast<int4*>(qrow + (int64_t)ciB * 16) = make_int4(0, 0, 0, 0);
+      continue;
+    }
+    const float s_row = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
+    const float inv = __frcp_rn(s_row);                          // 1.0 / scale
+    if (t == 0) p.scale[row] = s_row;
+    // |v| <= absmax: the round-half-even code of v * (1/scale) is already in
+    // [-127, 127]; the low byte of y + 1.5*2^23 is its two's complement.
+    // The product must be rounded before the add (torch rounds x * (1/s),
+    // then rounds to an integer).  The assembler has been seen to fuse a
+    // packed multiply with a following packed add even when both carry
+    // .rn, so the add is written as fma(product, one, magic) with `one` a
+    // kernel parameter equal to 1.0f: no single fused operation computes it.
+    const float2 inv2 = make_float2(inv, inv);
+    const float2 one2 = make_float2(p.one, p.one);
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    uint32_t ua[16], ub[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 y = f2_fma(f2_mul(v[j], inv2), one2, magic);
+      ua[j] = __float_as_uint(y.x);
+      ub[j] = __float_as_uint(y.y);
+    }
+    if (hasA) {
+      int4 o;
+      o.x = (int)pack4((int)ua[0], (int)ua[1], (int)ua[2], (int)ua[3]);
+      o.y = (int)pack4((int)ua[4], (int)ua[5], (int)ua[6], (int)ua[7]);
+      o.z = (int)pack4((int)ua[8], (int)ua[9], (int)ua[10], (int)ua[11]);
+      o.w = (int)pack4((int)ua[12], (int)ua[13], (int)ua[14], (int)ua[15]);
+      *reinterpret_cast<int4*>(qrow + (int64_t)ciA * 16) = o;
+    }
+    if (hasB) {
+      int4 o;
+      o.x = (int)pack4((int)ub[0], (int)ub[1], (int)ub[2], (int)ub[3]);
+      o.y = (int)pack4((int)ub[4], (int)ub[5], (int)ub[6], (int)ub[7]);
+      o.z = (int)pack4((int)ub[8], (int)ub[9], (int)ub[10], (int)ub[11]);
+      o.w = (int)pack4((int)ub[12], (int)ub[13], (int)ub[14], (int)ub[15]);
+      *reinterpret_cast<int4*>(qrow + (int64_t)ciB * 16) = o;
     }
   }
 }

@@ -125,6 +125,47 @@ def test_fused_rotate_quant_long_rows(P):
     np.testing.assert_array_equal(s.cpu().numpy(), so)
 
 
+# Row lengths 1024..16384 run the two-chunks-per-thread kernel: 64 chunks
+# (smallest), 65 (odd: the last thread has one chunk), 193, 1024 (largest).
+PAIR_CASES = [(1024, None), (1040, None), (3088, ("regular", 16)), (16384, None), (1024, ("sylvester", 32)),
+              (1024, ("regular", 64)), (16384, ("regular", 256)), (16384, ("sylvester", 128)), (1040, ("regular", 16))]
+
+
+@pytest.mark.parametrize("K,rot", PAIR_CASES)
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+def test_quant_int8_paired_chunks(P, K, rot, dt):
+    x = gi.activation(17, 45, K, dt, zero_row=3)
+    q, s = P.ops.quant_act_int8(dev(x, dt), rot)
+    xr = x if rot is None else O.rotate(x, rot[1], rot[0], dt)
+    qo, so = O.quantize_int8_axiswise(xr, -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+@pytest.mark.parametrize("K", [256, 2048, 24576])  # one-chunk, two-chunk-pair and long-row kernels
+def test_quant_int8_round_half_even_ties(P, K):
+    # scale 1.0 (absmax 127): codes of exact halves must round to even
+    rng = np.random.default_rng(19)
+    halves = np.float32(0.5) + rng.integers(-127, 127, size=(6, K)).astype(np.float32)
+    x = np.clip(halves, -126.5, 126.5)
+    x[:, 0] = 127.0
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
+    qo, so = O.quantize_int8_axiswise(O.rnd("bf16", x), -1)
+    assert np.all(so == 1.0)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+
+
+def test_quant_int8_paired_nonfinite_rows(P):
+    x = gi.activation(18, 9, 2048, "bf16")
+    x[1, 100] = np.inf
+    x[4, 2047] = -np.inf
+    x[6, 1500] = np.nan
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
+    qo, so = O.quantize_int8_axiswise(x, -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)  # NaN matches NaN, Inf matches Inf
+
+
 def test_rotate_vs_reference_golden(P, golden):
     # the reference's own bf16 matmul rotation: within 1 bf16 ulp
     x = gi.activation(4, 32, 1024, "bf16")
