@@ -38,7 +38,7 @@ SEED = 1
 CPU_SAMPLE_ROWS = 4096  # the whole batch: the CPU sample is bounded by time instead
 # dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch at this
 # workload, from the ncu capture summarised in profiles/ (None until taken).
-GEMM_TRAFFIC_BYTES = None
+GEMM_TRAFFIC_BYTES = 131576832  # ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/gemm_i8_pair_w8a8_4096x12288x3072.md)
 
 
 def load_pkg():
@@ -284,11 +284,11 @@ def run_ours(args):
                                    f"per-token x per-channel int8, bias; one batch per GPU",
                        "M": M, "N": N, "K": K, "l2": "flushed (256 MB write) before every timed step",
                        "parallelism": f"dp{world} (independent batches, no collective)"},
-            "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel (tcgen05 kind::i8)",
+            "roofline": {"bound": "tensor", "kernel": "gemm_i8_pair_kernel (tcgen05 kind::i8, CTA pair)",
                          "achieved": round(gemm_tops, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                          "frac": round(gemm_tops / int8_peak, 4), "traffic": GEMM_TRAFFIC_BYTES,
                          "peak_source": f"2 x {src} dense bf16 ({bf16_tf} TFLOP/s) = dense int8"},
-            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_kernel (fused Hadamard-128 + int8)",
+            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_pair_kernel (fused Hadamard-128 + int8)",
                                "achieved": round(quant_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
                                "frac": round(quant_gbs / hbm_gbs, 4), "bytes": quant_bytes,
                                "us": round(quant_ms * 1e3, 2)},
