@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "../../include/qlinear_b200.h"
+#include "gemm_g128.cuh"
 #include "gemm_i8.cuh"
 #include "internal.h"
 
@@ -184,6 +185,67 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
   }
   if (BN == 128) return dispatch_epi<128, false>(kind, out_dt, ta, tb, p, stream);
   return dispatch_epi<256, false>(kind, out_dt, ta, tb, p, stream);
+}
+
+namespace {
+
+template <int MODE, int OUT_DT>
+int launch_g128_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const G128Params& p, int sms, cudaStream_t stream) {
+  auto kern = gemm_g128_kernel<MODE, OUT_DT>;
+  static std::atomic<uint64_t> attr_devices{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  cudaError_t e;
+  if (!(attr_devices.load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G128Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm g128)");
+    attr_devices.fetch_or(bit);
+  }
+  const int num_tiles = ((p.M + G128Cfg::BM - 1) / G128Cfg::BM) * ((p.N + G128Cfg::BN - 1) / G128Cfg::BN);
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  kern<<<grid, G128Cfg::NUM_THREADS, G128Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm g128 launch");
+  return QLIN_OK;
+}
+
+template <int MODE>
+int dispatch_g128(int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const G128Params& p, int sms,
+                  cudaStream_t s) {
+  if (out_dt == DT_BF16) return launch_g128_cfg<MODE, DT_BF16>(ta, tb, p, sms, s);
+  if (out_dt == DT_F16) return launch_g128_cfg<MODE, DT_F16>(ta, tb, p, sms, s);
+  if (out_dt == DT_F32) return launch_g128_cfg<MODE, DT_F32>(ta, tb, p, sms, s);
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported output dtype");
+}
+
+}  // namespace
+
+int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
+                     const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
+                     int64_t K, cudaStream_t stream) {
+  if (M == 0 || N == 0) return QLIN_OK;
+  const int sms = device_sm_count();
+  if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  if (K % G128Cfg::BK) return fail(QLIN_ERR_ALIGNMENT, "K must be a multiple of 128");
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, G128Cfg::BK, G128Cfg::BM,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap(&tb, w_packed, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), G128Cfg::BK / 2, G128Cfg::BN,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  G128Params p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.a_scale = a_scale;
+  p.w_gscale = w_gscale;
+  p.bias = bias;
+  p.out = out;
+  p.ldo = N;
+  if (a_int4_groups) return dispatch_g128<G128_W4A4>(out_dt, ta, tb, p, sms, stream);
+  return dispatch_g128<G128_W4A8>(out_dt, ta, tb, p, sms, stream);
 }
 
 int read_device_error(cudaStream_t stream, uint32_t* bits) {

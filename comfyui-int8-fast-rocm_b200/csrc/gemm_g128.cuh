@@ -1,0 +1,432 @@
+// Group-128 packed-int4-weight GEMMs on the tcgen05 tensor cores:
+//
+//   W4A8: acc = 0; for g: acc = fmaf(float(P_g[m,n]), ws[n,g], acc)
+//         out = dt(dt32(acc * xs[m]) + bias[n])
+//   W4A4: acc = 0; for g: acc = fmaf(float(P_g[m,n]), dt32(xs[m,g] * ws[n,g]), acc)
+//         out = dt(acc + bias[n])
+//
+// with P_g the exact int32 dot product over K-group g (128 elements), A int8
+// codes [M, K] (int8 per-token for W4A8, int4-range codes for W4A4), W packed
+// int4 [N, K/2] (low nibble = even k), ws bf16 [N, K/128].
+//
+// One K-slab of the pipeline is exactly one scale group, so the MMA writes
+// each group's partial into its own TMEM buffer (two, alternating) and the
+// epilogue warps fold it into a float32 accumulator held in registers:
+//   warpgroup 0 (64 registers): warp 0 TMA producer (A slab 128x128 int8,
+//               swizzled; packed W slab), warp 1 TMEM allocator + MMA issuer
+//               (M=128, N=128, K=32 x 4 per group), warps 2-3 idle
+//   warpgroups 1-2 (184 registers): epilogue, per group TMEM partial ->
+//               float -> fma into a 64-float register accumulator (rows: the
+//               warp's TMEM lane quarter, columns: its half of the tile)
+//   warpgroup 3 (64 registers): nibble unpack of the W slab into the
+//               swizzled int8 layout.
+// Registers at launch: 512 threads x 128; after setmaxnreg
+// 128 x 64 + 256 x 184 + 128 x 64 = 63488 <= 65536.
+//
+// Two exact transformations keep the epilogue short:
+//  * nibbles are unpacked as 16*q (the nibble moved to the high half of the
+//    byte: no sign extension), so the MMA produces 16*P_g; the group scales
+//    are stored divided by 16, and 16*P * (s/16) == P * s exactly;
+//  * each partial buffer is pre-loaded with the bits of 1.5*2^23 and the MMA
+//    accumulates on top, so float(16*P) = as_float(bits) - 1.5*2^23 exactly
+//    (|16*P| < 2^22), one subtraction instead of an int-to-float conversion.
+// No TMA multicast; every pipeline wait is bounded (g_error_bits, abort flag).
+#pragma once
+
+#include "gemm_i8.cuh"
+
+namespace qlin {
+
+enum : int { G128_W4A8 = 0, G128_W4A4 = 1 };
+
+struct G128Params {
+  int M, N, K;
+  const float* a_scale;       // W4A8: [M]; W4A4: [M, K/128]
+  const uint16_t* w_gscale;   // bf16 bits [N, K/128]
+  const void* bias;           // [N] in the output dtype, or null
+  void* out;                  // [M, N]
+  int64_t ldo;
+};
+
+struct G128Cfg {
+  static constexpr int BM = 128, BN = 128, BK = 128;  // BK = scale group
+  static constexpr int STAGES = 5;
+  static constexpr int A_BYTES = BM * BK;             // 16 KB
+  static constexpr int B_BYTES = BN * BK;             // 16 KB unpacked
+  static constexpr int BP_BYTES = BN * BK / 2;        // 8 KB packed
+  static constexpr int NUM_THREADS = 512;  // 4 warpgroups
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256 + 16 + 2 * BN * 4 + 16;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+constexpr uint32_t kG128Magic = 0x4B400000u;  // bits of 1.5 * 2^23
+
+// 32 lanes x 8 columns of 32-bit TMEM <- 8 registers per thread.
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Store 8 consecutive outputs (already rounded to DT) of one row.
+template <int DT>
+__device__ __forceinline__ void store8(typename Elem<DT>::T* dst, const float (&y)[8], bool vec, int n) {
+  if (vec && n >= 8) {
+    if constexpr (DT == DT_F32) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (DT == DT_BF16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < n) dst[j] = Elem<DT>::from_f(y[j]);
+  }
+}
+
+// Unpack a packed int4 slab (BN rows x 64 bytes, row-major) into the
+// 128B-swizzled int8 operand layout, each code q as the byte 16*q.
+template <int BN>
+__device__ __forceinline__ void unpack_int4_slab_x16(const uint8_t* src, uint8_t* dst, int tid, int nthr) {
+  for (int item = tid; item < BN * 8; item += nthr) {
+    const int r = item >> 3;
+    const int c = item & 7;
+    const uint2 pk = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+    const uint32_t l0 = (pk.x << 4) & 0xF0F0F0F0u, h0 = pk.x & 0xF0F0F0F0u;
+    const uint32_t l1 = (pk.y << 4) & 0xF0F0F0F0u, h1 = pk.y & 0xF0F0F0F0u;
+    // interleave: k even <- low nibble, k odd <- high nibble
+    const uint4 o = make_uint4(__byte_perm(l0, h0, 0x5140), __byte_perm(l0, h0, 0x7362),
+                               __byte_perm(l1, h1, 0x5140), __byte_perm(l1, h1, 0x7362));
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+  }
+}
+
+// Group scale of column `col`, group g, as float divided by 16 (exact).
+__device__ __forceinline__ float g128_wscale16(const G128Params& p, int G, int col, int g) {
+  if (col >= p.N) return 0.0f;
+  const uint16_t b = __ldg(p.w_gscale + (int64_t)col * G + g);
+  return __uint_as_float((uint32_t)b << 16) * 0.0625f;
+}
+
+template <int MODE, int OUT_DT>
+__global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
+    gemm_g128_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     G128Params p) {
+  using Cfg = G128Cfg;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
+  uint8_t* sBP = sB + STAGES * Cfg::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBP + STAGES * Cfg::BP_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* conv = empty + STAGES;
+  uint64_t* pfull = conv + STAGES;    // [2] partial of a group ready
+  uint64_t* pempty = pfull + 2;       // [2] partial consumed and re-biased
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
+  // s_ws[2][BN]: group scales / 16, double-buffered by step parity
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + Cfg::BM - 1) / Cfg::BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int G = p.K / Cfg::BK;
+
+  // each role's code sits inside the branch that set its register limit
+  if (warp < 4) {
+    regs_dec<64>();
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int g = 0; g < G; ++g) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::BP_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], g * Cfg::BK, mb * Cfg::BM);
+          tma_load_2d(sBP + stage * Cfg::BP_BYTES, &tmB, &full[stage], g * (Cfg::BK / 2), nb * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = umma_idesc_i8(Cfg::BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int b = 0;
+      uint32_t pph[2] = {0u, 0u};
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        for (int g = 0; g < G; ++g) {
+          if (!mbar_wait_bounded(&conv[stage], phase, abort_flag) ||
+              !mbar_wait_bounded(&pempty[b], pph[b], abort_flag)) {
+            ok = false;
+            break;
+          }
+          pph[b] ^= 1;
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 32; ++k)  // accumulate onto the 1.5*2^23 bias
+            umma_i8(tmem_base + b * BN, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
+          umma_commit(&empty[stage]);
+          umma_commit(&pfull[b]);
+          b ^= 1;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp < 12) {
+    regs_inc<184>();
+    // ---------------- epilogue ----------------
+    using EO = Elem<OUT_DT>;
+    const int e = (warp - 4) * 32 + lane;  // 0..255
+    const int quarter = warp & 3;          // TMEM lanes 32*quarter.. (warp % 4 rule)
+    const int half = (warp - 4) >> 2;      // columns 64*half..
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+
+    // bias every partial buffer region this warp owns, then hand both
+    // buffers to the MMA (phase 0 of pempty)
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) tmem_st_32x32b_x8(tmem_base + b * BN + half * 64 + c8 * 8 + lane_off, kG128Magic);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&pempty[0]);
+      mbar_arrive(&pempty[1]);
+    }
+
+    // step = (tile, g) in issue order; per-column group scales for the next
+    // step are prefetched into a register and staged into s_ws one step ahead
+    int tile = blockIdx.x, g = 0;
+    int ntile = tile, ng = 0;  // step + 1
+    auto advance = [&](int& t, int& gg) {
+      if (++gg == G) { gg = 0; t += gridDim.x; }
+    };
+    auto col_of = [&](int t) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      return nb * BN + e;
+    };
+    if (tile < num_tiles && e < BN) s_ws[e] = g128_wscale16(p, G, col_of(tile), 0);
+    advance(ntile, ng);
+    float pws = (ntile < num_tiles && e < BN) ? g128_wscale16(p, G, col_of(ntile), ng) : 0.0f;
+
+    float2 acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
+    float xs_row = 0.0f;   // W4A8: this thread's row scale for the current tile
+    float pxs = 0.0f;      // W4A4: row scale of the next step
+    const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+    int b = 0;
+    uint32_t pph[2] = {0u, 0u};
+    int step = 0;
+    int mb = 0, nbk = 0;
+    if (tile < num_tiles) {
+      tile_coords(tile, num_m, num_n, mb, nbk);
+      const int row = mb * Cfg::BM + quarter * 32 + lane;
+      if (row < p.M) {
+        if constexpr (MODE == G128_W4A8) xs_row = __ldg(p.a_scale + row);
+        else pxs = __ldg(p.a_scale + (int64_t)row * G);
+      }
+    }
+    while (tile < num_tiles) {
+      mbar_wait_bounded(&pfull[b], pph[b], abort_flag);
+      pph[b] ^= 1;
+      epi_bar();  // s_ws[step & 1] visible; reads of s_ws[(step + 1) & 1] done
+      if (*abort_flag) break;
+      tc_fence_after();
+      float* ws_cur = s_ws + (step & 1) * BN;
+      float* ws_nxt = s_ws + ((step + 1) & 1) * BN;
+      if (e < BN) ws_nxt[e] = pws;
+      // prefetch the scale of step + 2
+      {
+        int t2 = ntile, g2 = ng;
+        advance(t2, g2);
+        pws = (t2 < num_tiles && e < BN) ? g128_wscale16(p, G, col_of(t2), g2) : 0.0f;
+      }
+      const int row = mb * Cfg::BM + quarter * 32 + lane;
+      float xs_g = 0.0f;
+      if constexpr (MODE == G128_W4A4) {
+        xs_g = pxs;
+        pxs = 0.0f;
+        if (ntile < num_tiles) {
+          int mb2, nb2;
+          tile_coords(ntile, num_m, num_n, mb2, nb2);
+          const int row2 = mb2 * Cfg::BM + quarter * 32 + lane;
+          if (row2 < p.M) pxs = __ldg(p.a_scale + (int64_t)row2 * G + ng);
+        }
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_base + b * BN + half * 64 + cc * 16 + lane_off, r);
+        tmem_ld_wait();
+        const float4* w4 = reinterpret_cast<const float4*>(ws_cur + half * 64 + cc * 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 w = w4[i];
+          float2 s0 = make_float2(w.x, w.y), s1 = make_float2(w.z, w.w);
+          if constexpr (MODE == G128_W4A4) {
+            const float2 x2 = make_float2(xs_g, xs_g);
+            s0 = f2_mul(x2, s0);  // dt32(xs * ws) / 16
+            s1 = f2_mul(x2, s1);
+          }
+          const float2 p0 = f2_add(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), neg_magic);
+          const float2 p1 =
+              f2_add(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), neg_magic);
+          acc[cc * 8 + 2 * i] = f2_fma(p0, s0, acc[cc * 8 + 2 * i]);
+          acc[cc * 8 + 2 * i + 1] = f2_fma(p1, s1, acc[cc * 8 + 2 * i + 1]);
+        }
+      }
+      // re-bias the partial buffer and return it to the MMA
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) tmem_st_32x32b_x8(tmem_base + b * BN + half * 64 + c8 * 8 + lane_off, kG128Magic);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);
+      b ^= 1;
+
+      if (g == G - 1) {
+        // tile done: scale, bias, round, store this thread's 64 columns
+        const int col0 = nbk * BN + half * 64;
+        if (row < p.M && col0 < p.N) {
+          const bool vec_ok = ((p.ldo % 8) == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
+          auto* orow = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo;
+          const auto* bias = reinterpret_cast<const typename EO::T*>(p.bias);
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int c0 = col0 + c8 * 8;
+            if (c0 < p.N) {
+              const int n = min(8, p.N - c0);
+              float y[8];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float a0 = acc[c8 * 4 + j].x, a1 = acc[c8 * 4 + j].y;
+                if constexpr (MODE == G128_W4A8) {
+                  a0 = __fmul_rn(a0, xs_row);  // dt32(acc * xs)
+                  a1 = __fmul_rn(a1, xs_row);
+                }
+                y[2 * j] = a0;
+                y[2 * j + 1] = a1;
+              }
+              if (bias != nullptr) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  if (j < n) y[j] = __fadd_rn(y[j], EO::to_f(bias[c0 + j]));
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) y[j] = EO::round(y[j]);
+              store8<OUT_DT>(orow + c0, y, vec_ok, n);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
+      }
+      // advance to the next step
+      const bool new_tile = (g == G - 1);
+      tile = ntile;
+      g = ng;
+      advance(ntile, ng);
+      ++step;
+      if (new_tile && tile < num_tiles) {
+        tile_coords(tile, num_m, num_n, mb, nbk);
+        if constexpr (MODE == G128_W4A8) {
+          const int row2 = mb * Cfg::BM + quarter * 32 + lane;
+          xs_row = row2 < p.M ? __ldg(p.a_scale + row2) : 0.0f;
+        }
+      }
+    }
+  } else {
+    regs_dec<64>();
+    // ---------------- int4 -> 16*int4 unpack (warps 12..15) ----------------
+    const int ctid = threadIdx.x - 32 * 12;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int g = 0; g < G; ++g) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
+        unpack_int4_slab_x16<BN>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid, 128);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace qlin

@@ -132,9 +132,4 @@ int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const
   return QLIN_OK;
 }
 
-int launch_gemm_g128(bool, const int8_t*, const float*, const int8_t*, const uint16_t*, const void*, void*, int,
-                     int64_t, int64_t, int64_t, cudaStream_t) {
-  return fail(QLIN_ERR_UNSUPPORTED, "group-128 int4 GEMM not built yet");
-}
-
 }  // namespace qlin

@@ -345,6 +345,93 @@ def test_w4a4_vs_oracle(P, dt):
 
 
 # ---------------------------------------------------------------------------
+# (c) group-128 int4-weight GEMMs (W4A8, W4A4)
+# ---------------------------------------------------------------------------
+
+G128_SHAPES = [(37, 128, 128), (300, 520, 512), (130, 300, 384), (256, 384, 3072)]
+
+
+def _g128_weight(P, seed, N, K, rot=None):
+    """bf16 weight, optional rotation, symmetric int4 per-group-128 in bf16
+    math; kernel output checked against the oracle quantiser."""
+    w = O.rnd("bf16", gi.weight(seed, N, K))
+    wr = w if rot is None else O.rotate(w, rot[1], rot[0], "bf16")
+    qo, so = O.quantize_signed_int4_grouped(wr, "bf16")
+    gp, gs = P.ops.quant_weight_int4(dev(w, "bf16"), rot, group=128)
+    np.testing.assert_array_equal(gp.cpu().numpy(), O.pack_int4_row_major(qo))
+    np.testing.assert_array_equal(gs.cpu().numpy(), so)
+    return gp, gs
+
+
+@pytest.mark.parametrize("M,N,K", G128_SHAPES)
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+def test_w4a8_g128_vs_oracle(P, M, N, K, dt):
+    x = gi.activation(30, M, K, dt)
+    b = gi.bias(30, N, dt) if dt != "f16" else None
+    gp, gs = _g128_weight(P, 30, N, K)
+    qa, sa = P.ops.quant_act_int8(dev(x, dt))
+    y = P.ops.gemm_w4_g128(qa, sa, gp, gs, None if b is None else dev(b, dt), TDT[dt])
+    yo = O.w4a8_g128_forward_from_q(qa.cpu().numpy(), sa.cpu().numpy(), gp.cpu().numpy(), gs.cpu().numpy(), b, dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+
+
+@pytest.mark.parametrize("M,N,K", G128_SHAPES)
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_w4a4_g128_vs_oracle(P, M, N, K, dt):
+    rot = ("sylvester", 128)
+    x = gi.activation(31, M, K, dt)
+    b = gi.bias(31, N, dt)
+    gp, gs = _g128_weight(P, 31, N, K, rot)
+    qa, sa = P.ops.quant_act_int4(dev(x, dt), rot, group=128)
+    y = P.ops.gemm_w4_g128(qa, sa, gp, gs, dev(b, dt), TDT[dt], a_int4_groups=True)
+    yo = O.w4a4_g128_forward_from_q(qa.cpu().numpy(), sa.cpu().numpy(), gp.cpu().numpy(), gs.cpu().numpy(), b, dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+
+
+def _rows_sample(M, n=48, seed=0):
+    rng = np.random.default_rng(seed)
+    return np.unique(np.concatenate([[0, M - 1], rng.choice(M, n, replace=False)]))
+
+
+def test_w4a8_g128_full_size_rows(P):
+    # Packed-INT4 W4A8 linear, M=4096 N=12288 K=3072, seed 2: whole GEMM on
+    # the GPU, oracle on a sample of rows (rows are independent)
+    M, N, K = 4096, 12288, 3072
+    x = gi.activation(2, M, K, "bf16")
+    gp, gs = P.ops.quant_weight_int4(dev(O.rnd("bf16", gi.weight(2, N, K)), "bf16"), None, group=128)
+    qa, sa = P.ops.quant_act_int8(dev(x, "bf16"))
+    b = gi.bias(2, N, "bf16")
+    y = P.ops.gemm_w4_g128(qa, sa, gp, gs, dev(b, "bf16"), torch.bfloat16)
+    rows = _rows_sample(M)
+    yo = O.w4a8_g128_forward_from_q(qa.cpu().numpy()[rows], sa.cpu().numpy()[rows], gp.cpu().numpy(),
+                                    gs.cpu().numpy(), b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
+@pytest.mark.parametrize("N", [3072, 12288])
+def test_w4a4_g128_full_size_rows(P, N):
+    # Packed-INT4 W4A4 linear with ConvRot (Sylvester 128), M=4096, K=3072, seed 3
+    M, K = 4096, 3072
+    rot = ("sylvester", 128)
+    x = gi.activation(3, M, K, "bf16")
+    gp, gs = P.ops.quant_weight_int4(dev(O.rnd("bf16", gi.weight(3, N, K)), "bf16"), rot, group=128)
+    qa, sa = P.ops.quant_act_int4(dev(x, "bf16"), rot, group=128)
+    b = gi.bias(3, N, "bf16")
+    y = P.ops.gemm_w4_g128(qa, sa, gp, gs, dev(b, "bf16"), torch.bfloat16, a_int4_groups=True)
+    rows = _rows_sample(M, seed=1)
+    yo = O.w4a4_g128_forward_from_q(qa.cpu().numpy()[rows], sa.cpu().numpy()[rows], gp.cpu().numpy(),
+                                    gs.cpu().numpy(), b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
+def test_g128_rejects_bad_k(P):
+    a = torch.zeros((16, 192), dtype=torch.int8, device="cuda")
+    w = torch.zeros((16, 96), dtype=torch.int8, device="cuda")
+    with pytest.raises(Exception):
+        P.ops.gemm_w4_g128(a, torch.ones(16, device="cuda"), w, torch.ones((16, 1), device="cuda"))
+
+
+# ---------------------------------------------------------------------------
 # (d) weight-side kernels
 # ---------------------------------------------------------------------------
 
