@@ -212,9 +212,13 @@ def run_ours(args):
         xq, xs = ops.quant_act_int8(x, rot)
         return xq, xs
 
+    # warm-up runs exactly the timed body, so the caching allocator already
+    # holds two output blocks (the previous step's y is alive while the next
+    # one is allocated) and no cudaMalloc lands inside a timed step
+    y = None
     for _ in range(max(3, args.warmup)):
         xq, xs = ops.quant_act_int8(x, rot)
-        ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16)
+        y = ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16)
     torch.cuda.synchronize()
 
     s = torch.cuda.current_stream(dev)

@@ -151,38 +151,15 @@ __device__ __forceinline__ void xform_regs(float* v) {
 }
 
 // Packed float32x2 arithmetic (sm_100): two IEEE float32 operations per
-// instruction, each rounded to nearest even.  Note: a packed multiply whose
-// only use is a following packed add has been fused into one FMA by the
-// assembler despite the explicit .rn (and -fmad=false); code that needs the
-// two roundings must not write that pair (see rowquant_pair_kernel).
-__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
-__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
+// instruction on a register pair, each rounded to nearest even.
+// Caution: a packed multiply whose only use is a following packed add has
+// been fused into one FMA by the assembler (even with -fmad=false); code that
+// needs those two roundings must not write that pair (rowquant_pair_kernel
+// adds through an FMA with a run-time 1.0 instead).
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
 // a * b + c with one rounding per component.
-__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return r;
-}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // ---------------------------------------------------------------------------
 // PTX wrappers: shared-memory addresses, mbarriers, TMA, tcgen05

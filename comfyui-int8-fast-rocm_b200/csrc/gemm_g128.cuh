@@ -10,18 +10,18 @@
 // int4 [N, K/2] (low nibble = even k), ws bf16 [N, K/128].
 //
 // One K-slab of the pipeline is exactly one scale group, so the MMA writes
-// each group's partial into its own TMEM buffer (two, alternating) and the
+// each group's partial into its own TMEM buffer (four, in rotation) and the
 // epilogue warps fold it into a float32 accumulator held in registers:
 //   warpgroup 0 (64 registers): warp 0 TMA producer (A slab 128x128 int8,
 //               swizzled; packed W slab), warp 1 TMEM allocator + MMA issuer
 //               (M=128, N=128, K=32 x 4 per group), warps 2-3 idle
-//   warpgroups 1-2 (184 registers): epilogue, per group TMEM partial ->
+//   warpgroups 1-2 (192 registers): epilogue, per group TMEM partial ->
 //               float -> fma into a 64-float register accumulator (rows: the
 //               warp's TMEM lane quarter, columns: its half of the tile)
 //   warpgroup 3 (64 registers): nibble unpack of the W slab into the
 //               swizzled int8 layout.
 // Registers at launch: 512 threads x 128; after setmaxnreg
-// 128 x 64 + 256 x 184 + 128 x 64 = 63488 <= 65536.
+// 128 x 64 + 256 x 192 + 128 x 64 = 65536, the launch total.
 //
 // Two exact transformations keep the epilogue short:
 //  * nibbles are unpacked as 16*q (the nibble moved to the high half of the
@@ -32,6 +32,8 @@
 //    (|16*P| < 2^22), one subtraction instead of an int-to-float conversion.
 // No TMA multicast; every pipeline wait is bounded (g_error_bits, abort flag).
 #pragma once
+
+#include <type_traits>
 
 #include "gemm_i8.cuh"
 
@@ -55,11 +57,13 @@ struct G128Cfg {
   static constexpr int B_BYTES = BN * BK;             // 16 KB unpacked
   static constexpr int BP_BYTES = BN * BK / 2;        // 8 KB packed
   static constexpr int NUM_THREADS = 512;  // 4 warpgroups
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256 + 16 + 2 * BN * 4 + 16;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + 256 + 16 + 8 * 2 * 64 * 4 + 16;
+  static_assert(3 * STAGES * 8 + 2 * 4 * 8 + 16 + 16 <= 256 + 16 + 16, "barrier block overflows its reserve");
+  static constexpr uint32_t TMEM_COLS = 4 * BN;  // G128_NBUF partial buffers
 };
 
 constexpr uint32_t kG128Magic = 0x4B400000u;  // bits of 1.5 * 2^23
+constexpr int G128_NBUF = 4;                   // TMEM partial buffers (4 x 128 columns)
 
 // 32 lanes x 8 columns of 32-bit TMEM <- 8 registers per thread.
 __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, uint32_t v) {
@@ -109,23 +113,6 @@ __device__ __forceinline__ void store8(typename Elem<DT>::T* dst, const float (&
   }
 }
 
-// Unpack a packed int4 slab (BN rows x 64 bytes, row-major) into the
-// 128B-swizzled int8 operand layout, each code q as the byte 16*q.
-template <int BN>
-__device__ __forceinline__ void unpack_int4_slab_x16(const uint8_t* src, uint8_t* dst, int tid, int nthr) {
-  for (int item = tid; item < BN * 8; item += nthr) {
-    const int r = item >> 3;
-    const int c = item & 7;
-    const uint2 pk = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-    const uint32_t l0 = (pk.x << 4) & 0xF0F0F0F0u, h0 = pk.x & 0xF0F0F0F0u;
-    const uint32_t l1 = (pk.y << 4) & 0xF0F0F0F0u, h1 = pk.y & 0xF0F0F0F0u;
-    // interleave: k even <- low nibble, k odd <- high nibble
-    const uint4 o = make_uint4(__byte_perm(l0, h0, 0x5140), __byte_perm(l0, h0, 0x7362),
-                               __byte_perm(l1, h1, 0x5140), __byte_perm(l1, h1, 0x7362));
-    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
-  }
-}
-
 // Group scale of column `col`, group g, as float divided by 16 (exact).
 __device__ __forceinline__ float g128_wscale16(const G128Params& p, int G, int col, int g) {
   if (col >= p.N) return 0.0f;
@@ -148,12 +135,12 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sBP + STAGES * Cfg::BP_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* conv = empty + STAGES;
-  uint64_t* pfull = conv + STAGES;    // [2] partial of a group ready
-  uint64_t* pempty = pfull + 2;       // [2] partial consumed and re-biased
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pfull = conv + STAGES;           // [G128_NBUF] partial of a group ready
+  uint64_t* pempty = pfull + G128_NBUF;      // [G128_NBUF] partial consumed and re-biased
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + G128_NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
-  // s_ws[2][BN]: group scales / 16, double-buffered by step parity
+  // s_ws[8 warps][2][64]: group scales / 16 of each epilogue warp's columns
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -164,7 +151,7 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], 4);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < G128_NBUF; ++b) {
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], EPI_WARPS);
     }
@@ -212,16 +199,15 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int b = 0;
-      uint32_t pph[2] = {0u, 0u};
+      uint32_t pph = 0;  // phase of the pempty round (flips when b wraps)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         for (int g = 0; g < G; ++g) {
           if (!mbar_wait_bounded(&conv[stage], phase, abort_flag) ||
-              !mbar_wait_bounded(&pempty[b], pph[b], abort_flag)) {
+              !mbar_wait_bounded(&pempty[b], pph, abort_flag)) {
             ok = false;
             break;
           }
-          pph[b] ^= 1;
           tc_fence_after();
           const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
           const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
@@ -230,13 +216,13 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
             umma_i8(tmem_base + b * BN, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
           umma_commit(&empty[stage]);
           umma_commit(&pfull[b]);
-          b ^= 1;
+          if (++b == G128_NBUF) { b = 0; pph ^= 1; }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp < 12) {
-    regs_inc<184>();
+    regs_inc<192>();
     // ---------------- epilogue ----------------
     using EO = Elem<OUT_DT>;
     const int e = (warp - 4) * 32 + lane;  // 0..255
@@ -244,115 +230,140 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
     const int half = (warp - 4) >> 2;      // columns 64*half..
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
 
-    // bias every partial buffer region this warp owns, then hand both
+    // bias every partial buffer region this warp owns, then hand all
     // buffers to the MMA (phase 0 of pempty)
 #pragma unroll
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < G128_NBUF; ++b)
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) tmem_st_32x32b_x8(tmem_base + b * BN + half * 64 + c8 * 8 + lane_off, kG128Magic);
     tmem_st_wait();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&pempty[0]);
-      mbar_arrive(&pempty[1]);
-    }
+    if (lane == 0)
+      for (int b = 0; b < G128_NBUF; ++b) mbar_arrive(&pempty[b]);
 
-    // step = (tile, g) in issue order; per-column group scales for the next
-    // step are prefetched into a register and staged into s_ws one step ahead
-    int tile = blockIdx.x, g = 0;
-    int ntile = tile, ng = 0;  // step + 1
-    auto advance = [&](int& t, int& gg) {
-      if (++gg == G) { gg = 0; t += gridDim.x; }
+    // A step is one (tile, group) in issue order.  Each warp stages the 64
+    // column scales of its half of the tile in its own shared-memory buffer
+    // (double-buffered by step parity, __syncwarp only); every lane loads two
+    // of them, five steps ahead, into a 4-slot register ring whose slot index
+    // is static (the step loop is unrolled by 4).  W4A4 row scales are loaded
+    // four steps ahead the same way.
+    struct It {
+      int tile, g, mb, nb;
     };
-    auto col_of = [&](int t) {
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
-      return nb * BN + e;
+    auto it_at = [&](int tile) {
+      It t{tile, 0, 0, 0};
+      if (tile < num_tiles) tile_coords(tile, num_m, num_n, t.mb, t.nb);
+      return t;
     };
-    if (tile < num_tiles && e < BN) s_ws[e] = g128_wscale16(p, G, col_of(tile), 0);
-    advance(ntile, ng);
-    float pws = (ntile < num_tiles && e < BN) ? g128_wscale16(p, G, col_of(ntile), ng) : 0.0f;
+    auto it_adv = [&](It& t) {
+      if (++t.g == G) {
+        t.g = 0;
+        t.tile += gridDim.x;
+        if (t.tile < num_tiles) tile_coords(t.tile, num_m, num_n, t.mb, t.nb);
+      }
+    };
+    auto load_ws = [&](const It& t, int j) -> float {  // column half*64 + 32*j + lane
+      if (t.tile >= num_tiles) return 0.0f;
+      return g128_wscale16(p, G, t.nb * BN + half * 64 + 32 * j + lane, t.g);
+    };
+    auto load_xs = [&](const It& t) -> float {
+      if (t.tile >= num_tiles) return 0.0f;
+      const int row2 = t.mb * Cfg::BM + quarter * 32 + lane;
+      if (row2 >= p.M) return 0.0f;
+      if constexpr (MODE == G128_W4A8) return __ldg(p.a_scale + row2);
+      else return __ldg(p.a_scale + (int64_t)row2 * G + t.g);
+    };
+
+    float* wbuf = s_ws + (warp - 4) * 128;  // [2][64] floats of this warp
+    It cur = it_at(blockIdx.x);
+    It la = cur;
+    wbuf[lane] = load_ws(la, 0);
+    wbuf[32 + lane] = load_ws(la, 1);
+    float rw0[4], rw1[4];  // scale of step t in slot t % 4
+#pragma unroll
+    for (int k = 1; k <= 4; ++k) {
+      it_adv(la);
+      rw0[k & 3] = load_ws(la, 0);
+      rw1[k & 3] = load_ws(la, 1);
+    }
+    it_adv(la);  // step 5
+    It lx = cur;
+    float rxs[4];  // W4A4: row scale of step t in slot t % 4
+    if constexpr (MODE == G128_W4A4) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        rxs[k] = load_xs(lx);
+        it_adv(lx);
+      }
+    }
+    float xs_row = 0.0f, xs_next = 0.0f;  // W4A8 row scale: this tile, next tile
+    if constexpr (MODE == G128_W4A8) {
+      xs_row = load_xs(cur);
+      xs_next = load_xs(it_at(cur.tile + (int)gridDim.x));
+    }
+    __syncwarp();
 
     float2 acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
-    float xs_row = 0.0f;   // W4A8: this thread's row scale for the current tile
-    float pxs = 0.0f;      // W4A4: row scale of the next step
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
     int b = 0;
-    uint32_t pph[2] = {0u, 0u};
-    int step = 0;
-    int mb = 0, nbk = 0;
-    if (tile < num_tiles) {
-      tile_coords(tile, num_m, num_n, mb, nbk);
-      const int row = mb * Cfg::BM + quarter * 32 + lane;
-      if (row < p.M) {
-        if constexpr (MODE == G128_W4A8) xs_row = __ldg(p.a_scale + row);
-        else pxs = __ldg(p.a_scale + (int64_t)row * G);
-      }
-    }
-    while (tile < num_tiles) {
-      mbar_wait_bounded(&pfull[b], pph[b], abort_flag);
-      pph[b] ^= 1;
-      epi_bar();  // s_ws[step & 1] visible; reads of s_ws[(step + 1) & 1] done
-      if (*abort_flag) break;
+    uint32_t pph = 0;  // phase of the pfull round (flips when b wraps)
+
+    // one step; K = step % 4 (static).  Returns false when this CTA is done.
+    auto step_fn = [&](auto kc) -> bool {
+      constexpr int K = decltype(kc)::value;
+      constexpr int K1 = (K + 1) & 3;
+      if (cur.tile >= num_tiles) return false;
+      const bool ok = mbar_wait_bounded(&pfull[b], pph, abort_flag);
+      if (__any_sync(0xffffffffu, !ok || *abort_flag)) return false;
       tc_fence_after();
-      float* ws_cur = s_ws + (step & 1) * BN;
-      float* ws_nxt = s_ws + ((step + 1) & 1) * BN;
-      if (e < BN) ws_nxt[e] = pws;
-      // prefetch the scale of step + 2
-      {
-        int t2 = ntile, g2 = ng;
-        advance(t2, g2);
-        pws = (t2 < num_tiles && e < BN) ? g128_wscale16(p, G, col_of(t2), g2) : 0.0f;
-      }
-      const int row = mb * Cfg::BM + quarter * 32 + lane;
+      uint32_t r[64];
+      tmem_ld_32x32b_x32(tmem_base + b * BN + half * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(tmem_base + b * BN + half * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      const float* ws_cur = wbuf + (K & 1) * 64;
+      float* ws_nxt = wbuf + (K1 & 1) * 64;
+      ws_nxt[lane] = rw0[K1];
+      ws_nxt[32 + lane] = rw1[K1];
+      rw0[K1] = load_ws(la, 0);  // step + 5
+      rw1[K1] = load_ws(la, 1);
+      it_adv(la);
       float xs_g = 0.0f;
       if constexpr (MODE == G128_W4A4) {
-        xs_g = pxs;
-        pxs = 0.0f;
-        if (ntile < num_tiles) {
-          int mb2, nb2;
-          tile_coords(ntile, num_m, num_n, mb2, nb2);
-          const int row2 = mb2 * Cfg::BM + quarter * 32 + lane;
-          if (row2 < p.M) pxs = __ldg(p.a_scale + (int64_t)row2 * G + ng);
-        }
+        xs_g = rxs[K];
+        rxs[K] = load_xs(lx);  // step + 4
+        it_adv(lx);
       }
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(tmem_base + b * BN + half * 64 + cc * 16 + lane_off, r);
-        tmem_ld_wait();
-        const float4* w4 = reinterpret_cast<const float4*>(ws_cur + half * 64 + cc * 16);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 w = w4[i];
-          float2 s0 = make_float2(w.x, w.y), s1 = make_float2(w.z, w.w);
-          if constexpr (MODE == G128_W4A4) {
-            const float2 x2 = make_float2(xs_g, xs_g);
-            s0 = f2_mul(x2, s0);  // dt32(xs * ws) / 16
-            s1 = f2_mul(x2, s1);
-          }
-          const float2 p0 = f2_add(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), neg_magic);
-          const float2 p1 =
-              f2_add(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), neg_magic);
-          acc[cc * 8 + 2 * i] = f2_fma(p0, s0, acc[cc * 8 + 2 * i]);
-          acc[cc * 8 + 2 * i + 1] = f2_fma(p1, s1, acc[cc * 8 + 2 * i + 1]);
-        }
-      }
-      // re-bias the partial buffer and return it to the MMA
+      tmem_ld_wait();
+      // re-bias the partial in TMEM while this step's math runs
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) tmem_st_32x32b_x8(tmem_base + b * BN + half * 64 + c8 * 8 + lane_off, kG128Magic);
+      const float4* w4 = reinterpret_cast<const float4*>(ws_cur);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 w = w4[i];
+        float2 s0 = make_float2(w.x, w.y), s1 = make_float2(w.z, w.w);
+        if constexpr (MODE == G128_W4A4) {
+          const float2 x2 = make_float2(xs_g, xs_g);
+          s0 = f2_mul(x2, s0);  // dt32(xs * ws) / 16
+          s1 = f2_mul(x2, s1);
+        }
+        const float2 p0 = f2_add(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), neg_magic);
+        const float2 p1 = f2_add(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), neg_magic);
+        acc[2 * i] = f2_fma(p0, s0, acc[2 * i]);
+        acc[2 * i + 1] = f2_fma(p1, s1, acc[2 * i + 1]);
+      }
       tmem_st_wait();
       tc_fence_before();
-      __syncwarp();
+      __syncwarp();  // also orders this step's ws_cur reads / ws_nxt writes
       if (lane == 0) mbar_arrive(&pempty[b]);
-      b ^= 1;
+      if (++b == G128_NBUF) { b = 0; pph ^= 1; }
 
-      if (g == G - 1) {
+      if (cur.g == G - 1) {
         // tile done: scale, bias, round, store this thread's 64 columns
-        const int col0 = nbk * BN + half * 64;
+        const int row = cur.mb * Cfg::BM + quarter * 32 + lane;
+        const int col0 = cur.nb * BN + half * 64;
         if (row < p.M && col0 < p.N) {
           const bool vec_ok = ((p.ldo % 8) == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
           auto* orow = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo;
@@ -386,20 +397,16 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
-      }
-      // advance to the next step
-      const bool new_tile = (g == G - 1);
-      tile = ntile;
-      g = ng;
-      advance(ntile, ng);
-      ++step;
-      if (new_tile && tile < num_tiles) {
-        tile_coords(tile, num_m, num_n, mb, nbk);
         if constexpr (MODE == G128_W4A8) {
-          const int row2 = mb * Cfg::BM + quarter * 32 + lane;
-          xs_row = row2 < p.M ? __ldg(p.a_scale + row2) : 0.0f;
+          xs_row = xs_next;
+          xs_next = load_xs(it_at(cur.tile + 2 * (int)gridDim.x));
         }
       }
+      it_adv(cur);
+      return true;
+    };
+    while (step_fn(std::integral_constant<int, 0>{}) && step_fn(std::integral_constant<int, 1>{}) &&
+           step_fn(std::integral_constant<int, 2>{}) && step_fn(std::integral_constant<int, 3>{})) {
     }
   } else {
     regs_dec<64>();
@@ -411,7 +418,7 @@ __global__ void __launch_bounds__(G128Cfg::NUM_THREADS, 1)
       bool ok = true;
       for (int g = 0; g < G; ++g) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
-        unpack_int4_slab_x16<BN>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid, 128);
+        unpack_int4_slab_x16<BN, 128>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);

@@ -137,32 +137,30 @@ __device__ __forceinline__ void store_out_chunk(typename Elem<DT>::T* dst, const
 
 // Unpack one packed-int4 K-slab (BN rows x 64 bytes, row-major, unswizzled)
 // into the 128B-swizzled int8 layout TMA would have produced for an int8
-// slab (16-byte chunk c of row r lands at chunk c ^ (r & 7)).
-template <int BN>
-__device__ __forceinline__ void unpack_int4_slab(const uint8_t* src, uint8_t* dst, int tid, int nthr) {
-  // each work item: one row, one 16-byte output chunk (= 8 packed bytes)
-  for (int item = tid; item < BN * 8; item += nthr) {
-    const int r = item >> 3;
-    const int c = item & 7;
-    const uint2 pk = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-    const uint32_t pw[2] = {pk.x, pk.y};
-    uint32_t o[4];
+// slab (16-byte chunk c of row r lands at chunk c ^ (r & 7)), each code q as
+// the byte 16*q: the nibble moved to the high half of its byte needs no sign
+// extension.  Consumers divide the products by 16 exactly (a power of two).
+// Thread `tid` of NTHR handles rows tid/8 + k*NTHR/8, chunk tid%8: all its
+// loads are issued before the first store, offsets are per-thread constants.
+template <int BN, int NTHR>
+__device__ __forceinline__ void unpack_int4_slab_x16(const uint8_t* src, uint8_t* dst, int tid) {
+  static_assert(NTHR % 64 == 0 && (BN * 8) % NTHR == 0, "row step must keep r & 7");
+  constexpr int ITEMS = BN * 8 / NTHR;
+  constexpr int RSTEP = NTHR / 8;
+  const int r0 = tid >> 3, c = tid & 7;
+  const uint8_t* s0 = src + r0 * 64 + c * 8;
+  uint8_t* d0 = dst + r0 * 128 + ((c ^ (r0 & 7)) << 4);
+  uint2 pk[ITEMS];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t v = pw[h];
+  for (int k = 0; k < ITEMS; ++k) pk[k] = *reinterpret_cast<const uint2*>(s0 + k * RSTEP * 64);
 #pragma unroll
-      for (int b2 = 0; b2 < 2; ++b2) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const uint32_t nib = (v >> (4 * (4 * b2 + n))) & 0xFu;
-          const uint32_t sx = (nib ^ 0x8u) - 0x8u;  // sign-extend 4 -> 32 bits
-          word |= (sx & 0xFFu) << (8 * n);
-        }
-        o[2 * h + b2] = word;
-      }
-    }
-    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int k = 0; k < ITEMS; ++k) {
+    const uint32_t l0 = (pk[k].x << 4) & 0xF0F0F0F0u, h0 = pk[k].x & 0xF0F0F0F0u;
+    const uint32_t l1 = (pk[k].y << 4) & 0xF0F0F0F0u, h1 = pk[k].y & 0xF0F0F0F0u;
+    // interleave: k even <- low nibble, k odd <- high nibble
+    *reinterpret_cast<uint4*>(d0 + k * RSTEP * 128) =
+        make_uint4(__byte_perm(l0, h0, 0x5140), __byte_perm(l0, h0, 0x7362), __byte_perm(l1, h1, 0x5140),
+                   __byte_perm(l1, h1, 0x7362));
   }
 }
 
@@ -183,7 +181,9 @@ __device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, 
   if (e >= BN) return;
   const int col = colt0 + e;
   if (col >= p.N) return;
-  if constexpr (EPI == EPI_W8A8_ROW || EPI == EPI_W4A4_ROW) ws = __ldg(p.w_scale + col);
+  if constexpr (EPI == EPI_W8A8_ROW) ws = __ldg(p.w_scale + col);
+  // packed-int4 B is unpacked as 16*q: ws/16 (exact) restores the products
+  if constexpr (EPI == EPI_W4A4_ROW) ws = __ldg(p.w_scale + col) * 0.0625f;
   if constexpr (EPI != EPI_I32) {
     if (p.bias != nullptr) b = Elem<OUT_DT>::to_f(reinterpret_cast<const typename Elem<OUT_DT>::T*>(p.bias)[col]);
   }
@@ -193,7 +193,7 @@ __device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, 
 // [tmem_acc, tmem_acc + BN): this warp converts TMEM lane quarter `quarter`
 // (rows row0 + 32*quarter + lane) and column half `half` (EPI_WARPS == 8),
 // with the tile's per-column parameters in shared memory (s_ws, s_b).
-template <int BN, int EPI, int OUT_DT>
+template <int BN, int EPI, int OUT_DT, int ISHIFT>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int row0, int colt0, int quarter,
                                               int half, int lane, const float* s_ws, const float* s_b, float xs) {
   using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
@@ -218,6 +218,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
     tmem_ld_wait();
     if (!row_ok || col0 >= p.N) continue;
     if constexpr (EPI == EPI_I32) {
+      if constexpr (ISHIFT > 0) {
+        // 16*q weights: the accumulator is 16x the product, exactly
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = (uint32_t)((int32_t)r[j] >> ISHIFT);
+      }
       int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
       if (full_chunk) {
 #pragma unroll
@@ -278,7 +283,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
 // registers while tile i is converted and staged into shared memory after it.
 // All epilogue threads pass the named barrier every tile and leave together
 // when any wait timed out (the abort flag is read after the barrier).
-template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR>
+template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR, int ISHIFT = 0>
 __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* es, uint64_t* tfull, uint64_t* tempty,
                                               volatile int* abort_flag, uint32_t tmem_base, int first_tile,
                                               int tile_stride, int num_tiles, int num_m, int num_n, int row_off,
@@ -314,7 +319,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       const int row = mb2 * ROWS_PER_TILE + row_off + quarter * 32 + lane;
       if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
     }
-    epilogue_tile<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter, half,
+    epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter, half,
                                    lane, es->ws[buf], es->bias[buf], xs);
     tc_fence_before();
     __syncwarp();
@@ -445,7 +450,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
   } else if (warp < 2 + EPI_WARPS) {
     // ---------------- epilogue ----------------
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
-    epilogue_role<BN, EPI, OUT_DT, GEMM_BM, false>(p, es, tfull, tempty, abort_flag, tmem_base, blockIdx.x, gridDim.x,
+    epilogue_role<BN, EPI, OUT_DT, GEMM_BM, false, B_INT4 ? 4 : 0>(p, es, tfull, tempty, abort_flag, tmem_base, blockIdx.x, gridDim.x,
                                                    num_tiles, num_m, num_n, 0, warp, lane);
   } else if constexpr (B_INT4) {
     // ---------------- int4 -> int8 converters (warps 10..13) ----------------
@@ -456,7 +461,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       bool ok = true;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
-        unpack_int4_slab<BN>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid, 128);
+        unpack_int4_slab_x16<BN, 128>(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, ctid);
         fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
         __syncwarp();
         if (lane == 0) mbar_arrive(&conv[stage]);
