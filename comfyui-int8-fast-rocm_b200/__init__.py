@@ -72,15 +72,17 @@ Int4ConvRotOps = getattr(int4_quant, "Int4ConvRotOps", None)
 NODE_CLASS_MAPPINGS = {}
 NODE_DISPLAY_NAME_MAPPINGS = {}
 try:
-    from .int8_unet_loader import UNetLoaderINTW8A8
+    from .int8_unet_loader import PreLoraLoader, UNetLoaderINTW8A8
     from .int4_unet_loader import UNetLoaderINT4ConvRot
 
     NODE_CLASS_MAPPINGS = {
         "OTUNetLoaderW8A8": UNetLoaderINTW8A8,
+        "INT8PreLoraLoader": PreLoraLoader,
         "UNetLoaderINT4ConvRot": UNetLoaderINT4ConvRot,
     }
     NODE_DISPLAY_NAME_MAPPINGS = {
         "OTUNetLoaderW8A8": "Load Diffusion Model Int8",
+        "INT8PreLoraLoader": "Int8 Pre-Lora Loader",
         "UNetLoaderINT4ConvRot": "Load Diffusion Model Int4",
     }
 except ImportError:

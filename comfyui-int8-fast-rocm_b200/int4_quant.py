@@ -112,6 +112,67 @@ def convrot_w4a4_forward(x: Tensor, qweight: Tensor, wscales: Tensor, bias, conv
     return out.reshape(*orig_shape[:-1], wscales.shape[0])
 
 
+def quantize_signed_int4_packed_with_scale(x: Tensor, scale: Tensor) -> Tensor:
+    """Packed int4 with a given per-row scale, ``round(x / s)`` clamped to
+    +-7 (int4_quant.py:86-93); used when baking LoRA into an int4 layer."""
+    s = scale.reshape(-1, 1).float()
+    q = torch.round(x.float() / s).clamp_(-_INT4_MAX, _INT4_MAX).to(torch.int8)
+    return pack_int4_row_major(q)
+
+
+def stochastic_round_int4_packed_delta(x: Tensor, scale: Tensor, seed: int = 0) -> Tensor:
+    """Stochastic-rounding variant (int4_quant.py:96-114): floor + Bernoulli
+    of the fraction, clamped to +-7.  torch's RNG stream: matches the
+    reference in distribution, not element by element."""
+    s = scale.reshape(-1, 1).float()
+    y = x.float() / s
+    fl = torch.floor(y)
+    gen = torch.Generator(device=x.device)
+    gen.manual_seed(seed)
+    r = torch.rand(fl.shape, generator=gen, device=x.device, dtype=fl.dtype)
+    q = torch.where(r < (y - fl), fl + 1, fl).clamp_(-_INT4_MAX, _INT4_MAX).to(torch.int8)
+    return pack_int4_row_major(q)
+
+
+def dequantize_simple_int8_rowwise(weight: Tensor, scale: Tensor, out_features: int, convrot: bool = False,
+                                   convrot_groupsize: int = CONVROT_W4A4_GROUP_SIZE) -> Tensor:
+    """float32 weight of an ``int8_tensorwise`` layer inside an int4 model,
+    un-rotated when the layer is ConvRot (int4_quant.py:137-160)."""
+    rot = rot_for_group(convrot_groupsize) if convrot else None
+    return ops.dequant_int8(weight, scale.float().reshape(-1, 1) if scale.numel() == out_features else scale.float(),
+                            rot)
+
+
+def quantize_int8_with_scale(x: Tensor, scale: Tensor) -> Tensor:
+    """int8 with a given per-row scale, ``round(x / s)`` clamped to +-127
+    (int4_quant.py:1007-1015)."""
+    s = scale.reshape(-1, 1).float()
+    return torch.round(x.float() / s).clamp_(-127.0, 127.0).to(torch.int8)
+
+
+# Layers kept in high precision when quantising on the fly, per model family
+# (int4_quant.py:371-391; same names as the reference).
+MODEL_TYPE_EXCLUSIONS = {
+    "flux2": ["img_in", "time_in", "guidance_in", "txt_in", "double_stream_modulation_img",
+              "double_stream_modulation_txt", "single_stream_modulation"],
+    "z-image": ["cap_embedder", "t_embedder", "x_embedder", "cap_pad_token", "context_refiner", "final_layer",
+                "noise_refiner", "adaLN", "x_pad_token", "layers.0."],
+    "chroma": ["distilled_guidance_layer", "final_layer", "img_in", "txt_in", "nerf_image_embedder", "nerf_blocks",
+               "nerf_final_layer_conv", "__x0__"],
+    "qwen": ["time_text_embed", "img_in", "norm_out", "proj_out", "txt_in"],
+    "ernie": ["time", "x_embedder", "text_proj", "adaLN"],
+    "anima": ["embed", "llm"],
+    "krea2": ["first", "last", "tmlp", "tproj", "txtfusion", "txtmlp"],
+    "hidream o1": ["embed", "language_model.layers.35.mlp"],
+    "boogu": ["embed", "refine", "norm_out"],
+    "ideogram4": ["embed_image_indicator", "t_embedding", "proj"],
+    "wan": ["patch_embedding", "text_embedding", "time_embedding", "time_projection", "head", "img_emb",
+            "face_adapter", "face_encoder", "motion_encoder", "pose_patch_embedding"],
+    "ltx2": ["adaln", "embedding", "patchify", "to_gate_logits", "proj_out", "model.audio", "model.video",
+             "model.av", "model.patch", "model.proj", "shift"],
+}
+
+
 try:
     from comfy.ops import manual_cast, cast_bias_weight, uncast_bias_weight
     _COMFY_OPS_AVAILABLE = True
@@ -173,12 +234,37 @@ if _COMFY_OPS_AVAILABLE:
 
             _normalize_lora_key = staticmethod(_normalize_lora_key)
 
+            @staticmethod
+            def _is_bias_key(key):
+                return isinstance(key, str) and key.endswith(".bias")
+
+            def _bake_pre_lora(self, tensor, key):
+                """Pre-LoRA patches grouped by the loader, baked into a float
+                weight or bias before quantisation (as Int8TensorwiseOps)."""
+                table = Int4ConvRotOps.lora_patches or {}
+                if tensor is None or tensor.dtype == torch.int8 or not table:
+                    return tensor
+                nk = _normalize_lora_key(key)
+                patches = table.get(nk)
+                if not patches:
+                    return tensor
+                if not hasattr(Int4ConvRotOps, "applied_lora_patches"):
+                    Int4ConvRotOps.applied_lora_patches = set()
+                Int4ConvRotOps.applied_lora_patches.add(nk)
+                import comfy.lora
+                import comfy.model_management
+                formatted = [(p[3] if len(p) == 4 else Int4ConvRotOps.lora_strength, p[0], 1.0, p[1], p[2])
+                             for p in patches]
+                dev = torch.device("cuda") if torch.cuda.is_available() else tensor.device
+                tmp = tensor.to(dev).to(comfy.model_management.lora_compute_dtype(dev))
+                return comfy.lora.calculate_weight(formatted, tmp, key).to(tensor.dtype)
+
             def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
                                       unexpected_keys, error_msgs):
                 self._debug_name = prefix
                 weight_key = prefix + "weight"
-                weight_tensor = state_dict.pop(weight_key, None)
-                bias_tensor = state_dict.pop(prefix + "bias", None)
+                weight_tensor = self._bake_pre_lora(state_dict.pop(weight_key, None), weight_key)
+                bias_tensor = self._bake_pre_lora(state_dict.pop(prefix + "bias", None), prefix + "bias")
                 weight_scale = _pop_metadata(state_dict, prefix, "weight_scale")
                 conf = _parse_comfy_quant(_pop_metadata(state_dict, prefix, "comfy_quant"))
                 state_dict.pop(prefix + "input_scale", None)
@@ -347,3 +433,186 @@ if _COMFY_OPS_AVAILABLE:
             if dims == 3:
                 return cls.Conv3d(*args, **kwargs)
             raise ValueError(f"unsupported dimensions: {dims}")
+
+
+# =============================================================================
+# LoRA on INT4 ConvRot models: low-VRAM patch callable and the model patcher
+# =============================================================================
+
+try:
+    import comfy.model_patcher as _comfy_model_patcher
+    import comfy.lora as _comfy_lora
+    import comfy.utils as _comfy_utils
+    _COMFY_PATCHER_AVAILABLE = _COMFY_OPS_AVAILABLE
+except ImportError:
+    _COMFY_PATCHER_AVAILABLE = False
+
+
+def bake_int4_layer_weight(module, source, delta_fn, stochastic=False, seed=0):
+    """Bake a float-space patch into an INT4 model's quantised layer
+    (int4_quant.py:1165-1195): dequantise (+ un-rotate), apply ``delta_fn``,
+    re-rotate, requantise with the layer's ORIGINAL scale (int4: packed,
+    +-7; int8_tensorwise: +-127)."""
+    group = getattr(module, "_convrot_groupsize", CONVROT_W4A4_GROUP_SIZE)
+    wscale = module.weight_scale.to(source.device)
+    if module._linear_dtype == "int8_tensorwise":
+        use_rot = bool(getattr(module, "_use_convrot", False))
+        w = dequantize_simple_int8_rowwise(source, wscale, source.shape[0], convrot=use_rot, convrot_groupsize=group)
+        w = delta_fn(w)
+        if use_rot:
+            w = ops.rotate(w.float().contiguous(), *rot_for_group(group))
+        return quantize_int8_with_scale(w, wscale)
+    w = dequantize_convrot_w4a4_weight_full(source, wscale, group, dtype=torch.float32)
+    w = ops.rotate(delta_fn(w).float().contiguous(), *rot_for_group(group))
+    if stochastic:
+        return stochastic_round_int4_packed_delta(w, wscale, seed)
+    return quantize_signed_int4_packed_with_scale(w, wscale)
+
+
+if _COMFY_PATCHER_AVAILABLE:
+    from .int8_quant import _dynamic_lora_entries
+
+    def _managed(module):
+        return getattr(module, "_is_quantized", False) and \
+            getattr(module, "_linear_dtype", None) in ("int4", "int8_tensorwise")
+
+    class Int4LowVramPatch:
+        """Low-VRAM LoRA on an INT4 model layer as ComfyUI streams it in
+        (int4_quant.py:1018-1060)."""
+        is_lowvram_patch = True
+
+        def __init__(self, key, patches, module, lora_mode):
+            self.key, self.patches, self.module, self.lora_mode = key, patches, module, lora_mode
+            self.prepared_patches = None
+
+        def memory_required(self):
+            return 0
+
+        def prepare(self, *args, **kwargs):
+            self.prepared_patches = list(self.patches[self.key])
+            return self.prepared_patches
+
+        def clear_prepared(self):
+            self.prepared_patches = None
+
+        def __call__(self, weight):
+            patches = self.prepared_patches if self.prepared_patches is not None else self.patches[self.key]
+            stochastic = self.lora_mode == "Stochastic"
+            return bake_int4_layer_weight(
+                self.module, weight,
+                lambda w: _comfy_lora.calculate_weight(patches, w, self.key, intermediate_dtype=w.dtype),
+                stochastic=stochastic, seed=_comfy_utils.string_to_seed(self.key) if stochastic else 0)
+
+    class Int4ModelPatcher(_comfy_model_patcher.ModelPatcher):
+        """ModelPatcher routing LoRA on INT4 ConvRot (and stray
+        int8_tensorwise) layers through bake-in or dynamic paths
+        (int4_quant.py:1118-1300)."""
+
+        def _managed_module(self, key):
+            try:
+                module = _comfy_utils.get_attr(self.model, key.rsplit(".", 1)[0])
+            except AttributeError:
+                return None
+            return module if _managed(module) else None
+
+        def patch_weight_to_device(self, key, device_to=None, inplace_update=False, return_weight=False,
+                                   force_cast=False):
+            if key not in self.patches and not force_cast:
+                return super().patch_weight_to_device(key, device_to, inplace_update, return_weight, force_cast)
+            module = self._managed_module(key)
+            if module is None:
+                return super().patch_weight_to_device(key, device_to, inplace_update, return_weight, force_cast)
+            if Int4ConvRotOps.Linear._is_bias_key(key):
+                return _comfy_utils.get_attr(self.model, key) if return_weight else None
+            patches = self.patches.get(key, [])
+            if not Int4ConvRotOps.dynamic_lora:
+                current = _comfy_utils.get_attr(self.model, key)
+                if key not in self.backup:
+                    import collections
+                    Backup = collections.namedtuple("Dimension", ["weight", "inplace_update"])
+                    self.backup[key] = Backup(weight=current.to(device=self.offload_device, copy=inplace_update),
+                                              inplace_update=inplace_update)
+                    source = current
+                else:
+                    source = self.backup[key].weight
+                stochastic = getattr(Int4ConvRotOps, "lora_mode", "None") == "Stochastic"
+                patched = bake_int4_layer_weight(
+                    module, source.to("cuda"), lambda w: _comfy_lora.calculate_weight(patches, w, key),
+                    stochastic=stochastic, seed=_comfy_utils.string_to_seed(key) if stochastic else 0)
+                patched = patched.to(current.device)
+                if return_weight:
+                    return patched
+                if inplace_update:
+                    current.data.copy_(patched)
+                else:
+                    _comfy_utils.set_attr(self.model, key, nn.Parameter(patched, requires_grad=False))
+                return None
+            weight = _comfy_utils.get_attr(self.model, key)
+            cache_key = tuple(id(p[1]) for p in patches)
+            if getattr(module, "_lora_cache_key", None) != cache_key:
+                group = getattr(module, "_convrot_groupsize", CONVROT_W4A4_GROUP_SIZE)
+                rotated = bool(getattr(module, "_use_convrot", False)) \
+                    if module._linear_dtype == "int8_tensorwise" else True
+                rot = rot_for_group(group) if rotated else None
+                device = weight.device if weight is not None else self.offload_device
+                entries = _dynamic_lora_entries(module, patches, rot, lambda k: k % group == 0)
+                module.lora_patches = [(d.to(device), u.to(device), s0, sz) for d, u, s0, sz in entries]
+                module._lora_cache_key = cache_key
+            return weight if return_weight else None
+
+        def load(self, *args, **kwargs):
+            if not Int4ConvRotOps.dynamic_lora:
+                for k in list(self.backup):
+                    if k in self.patches and self._managed_module(k) is not None:
+                        bk = self.backup.pop(k)
+                        if bk.inplace_update:
+                            _comfy_utils.get_attr(self.model, k).data.copy_(bk.weight)
+                        else:
+                            _comfy_utils.set_attr(self.model, k, bk.weight)
+            for k in [k for k in self.backup if k not in self.patches]:
+                bk = self.backup.pop(k)
+                if bk.inplace_update:
+                    _comfy_utils.get_attr(self.model, k).data.copy_(bk.weight)
+                else:
+                    _comfy_utils.set_attr(self.model, k, bk.weight)
+            for name, module in self.model.named_modules():
+                if getattr(module, "lora_patches", None):
+                    if not Int4ConvRotOps.dynamic_lora or (name + ".weight") not in self.patches:
+                        module.lora_patches = []
+            res = super().load(*args, **kwargs) if hasattr(super(), "load") else None
+            device_to = kwargs.get("device_to", args[0] if args else None)
+            for name, module in self.model.named_modules():
+                if not _managed(module) or (name + ".weight") not in self.patches:
+                    continue
+                wkey = name + ".weight"
+                if hasattr(module, "weight_function"):
+                    module.weight_function = [f for f in module.weight_function
+                                              if type(f).__name__ != "LowVramPatch"]
+                if Int4ConvRotOps.dynamic_lora:
+                    module.weight_lowvram_function = None
+                    self.patch_weight_to_device(wkey, device_to=device_to)
+                else:
+                    module.weight_lowvram_function = Int4LowVramPatch(
+                        wkey, self.patches, module, getattr(Int4ConvRotOps, "lora_mode", "None"))
+            return res
+
+        def unpatch_model(self, device_to=None, unpatch_weights=True):
+            if unpatch_weights:
+                for module in self.model.modules():
+                    if hasattr(module, "lora_patches"):
+                        module.lora_patches = []
+            return super().unpatch_model(device_to, unpatch_weights)
+
+        def clone(self, *args, **kwargs):
+            """Clone as an INT4-aware patcher (same scheme as INT8ModelPatcher.clone)."""
+            src_cls = self.__class__
+            if src_cls is Int4ModelPatcher:
+                return super().clone(*args, **kwargs)
+            mixed = src_cls if issubclass(src_cls, Int4ModelPatcher) else \
+                type(f"INT4_{src_cls.__name__}", (Int4ModelPatcher, src_cls), {})
+            self.__class__ = mixed
+            try:
+                n = super().clone(*args, **kwargs)
+            finally:
+                self.__class__ = src_cls
+            return n

@@ -212,6 +212,59 @@ if _COMFY_OPS_AVAILABLE:
             def _is_bias_key(key):
                 return isinstance(key, str) and key.endswith(".bias")
 
+            @staticmethod
+            def _format_lora_patches(patches):
+                """Grouped pre-LoRA entries (value, offset, function[, strength])
+                -> the (strength, value, 1.0, offset, function) tuples that
+                comfy.lora.calculate_weight consumes (int8_quant.py:256-265)."""
+                formatted = []
+                for patch in patches or []:
+                    if len(patch) == 4:
+                        v, offset, function, strength = patch
+                    else:
+                        v, offset, function = patch
+                        strength = getattr(Int8TensorwiseOps, "lora_strength", 1.0)
+                    formatted.append((strength, v, 1.0, offset, function))
+                return formatted
+
+            def _apply_int8_lora_patches(self, tensor, key, patches, device):
+                """Bake pre-LoRA patches into a float weight in ComfyUI's LoRA
+                compute dtype (int8_quant.py:268-274)."""
+                if not patches or tensor.dtype == torch.int8:
+                    return tensor
+                import comfy.lora
+                import comfy.model_management
+                temp_dtype = comfy.model_management.lora_compute_dtype(device)
+                tensor_temp = tensor.to(device, non_blocking=True).to(dtype=temp_dtype)
+                return comfy.lora.calculate_weight(self._format_lora_patches(patches), tensor_temp, key)
+
+            def finalize_pending_int8(self):
+                """Deferred load work (pre-LoRA bake and/or on-the-fly quant)
+                recorded while a dynamic load device was set; run by
+                INT8ModelPatcher at model load (int8_quant.py:276-325)."""
+                pending = getattr(self, "_pending_int8_finalize", None)
+                if pending is None:
+                    return False
+                device = pending.get("device") or torch.device("cuda")
+                weight_tensor = self._apply_int8_lora_patches(
+                    self.weight.detach(), pending["weight_key"], pending.get("lora_patches"), device)
+                if pending["quantize"]:
+                    saved = Int8TensorwiseOps.enable_convrot
+                    Int8TensorwiseOps.enable_convrot = pending.get("enable_convrot", False)
+                    try:
+                        self._otf_quantize(weight_tensor.to(device))
+                    finally:
+                        Int8TensorwiseOps.enable_convrot = saved
+                else:
+                    self.weight = nn.Parameter(weight_tensor.cpu(), requires_grad=False)
+                self.weight_comfy_model_dtype = self.weight.dtype
+                if self.weight_scale is not None:
+                    self.weight_scale_comfy_model_dtype = self.weight_scale.dtype
+                if self.bias is not None:
+                    self.bias_comfy_model_dtype = self.bias.dtype
+                del self._pending_int8_finalize
+                return True
+
             # -- loading ----------------------------------------------------
             def _otf_quantize(self, weight_tensor):
                 """On-the-fly quant (int8_quant.py:517-554): float32 weight ->
@@ -241,6 +294,35 @@ if _COMFY_OPS_AVAILABLE:
                 weight_tensor = state_dict.pop(weight_key, None)
                 bias_tensor = state_dict.pop(bias_key, None)
                 state_dict.pop(prefix + "input_scale", None)
+
+                # pre-LoRA patches grouped by the loader (int8_quant.py:335-453):
+                # baked into float weights/biases before any quantisation;
+                # deferred to model load when a dynamic load device is set
+                lora_table = Int8TensorwiseOps.lora_patches or {}
+
+                def _note_applied(key):
+                    if not hasattr(Int8TensorwiseOps, "applied_lora_patches"):
+                        Int8TensorwiseOps.applied_lora_patches = set()
+                    Int8TensorwiseOps.applied_lora_patches.add(key)
+
+                def _bake(tensor, key):
+                    if tensor is None or tensor.dtype == torch.int8 or not lora_table:
+                        return tensor
+                    patches = lora_table.get(_normalize_lora_key(key))
+                    if not patches:
+                        return tensor
+                    _note_applied(_normalize_lora_key(key))
+                    device = getattr(Int8TensorwiseOps, "dynamic_load_device", None) or tensor.device
+                    return self._apply_int8_lora_patches(tensor, key, patches, device).to(tensor.dtype)
+
+                pending_weight_lora = None
+                if weight_tensor is not None and weight_tensor.dtype != torch.int8 and lora_table:
+                    pending_weight_lora = lora_table.get(_normalize_lora_key(weight_key))
+                defer_weight_lora = (getattr(Int8TensorwiseOps, "dynamic_load_device", None) is not None
+                                     and bool(pending_weight_lora))
+                if not defer_weight_lora:
+                    weight_tensor = _bake(weight_tensor, weight_key)
+                bias_tensor = _bake(bias_tensor, bias_key)
 
                 if isinstance(conf, dict) and conf.get("convrot", False):
                     self._use_convrot = True
@@ -293,7 +375,22 @@ if _COMFY_OPS_AVAILABLE:
                     elif weight_tensor.dtype in (torch.float16, torch.bfloat16, torch.float32):
                         is_excluded = any(ex in prefix for ex in Int8TensorwiseOps.excluded_names)
                         is_dim1 = self.in_features == 1 or self.out_features == 1 or weight_tensor.ndim == 1
-                        if Int8TensorwiseOps.dynamic_quantize and not is_excluded and not is_dim1:
+                        should_quantize = Int8TensorwiseOps.dynamic_quantize and not is_excluded and not is_dim1
+                        load_dev = getattr(Int8TensorwiseOps, "dynamic_load_device", None)
+                        if load_dev is not None and (should_quantize or pending_weight_lora):
+                            # per-layer bake/quant deferred to model load
+                            self._is_quantized = False
+                            self.weight = nn.Parameter(weight_tensor, requires_grad=False)
+                            self._pending_int8_finalize = {
+                                "weight_key": weight_key,
+                                "quantize": should_quantize,
+                                "lora_patches": pending_weight_lora,
+                                "device": load_dev,
+                                "enable_convrot": getattr(Int8TensorwiseOps, "enable_convrot", False),
+                            }
+                            if pending_weight_lora:
+                                _note_applied(_normalize_lora_key(weight_key))
+                        elif should_quantize:
                             if not hasattr(Int8TensorwiseOps, "_logged_otf"):
                                 logging.info(
                                     f"INT8 Fast: Quantizing on-the-fly (ConvRot: {Int8TensorwiseOps.enable_convrot})")
@@ -448,3 +545,241 @@ if _COMFY_OPS_AVAILABLE:
             if dims == 3:
                 return cls.Conv3d(*args, **kwargs)
             raise ValueError(f"unsupported dimensions: {dims}")
+
+
+# =============================================================================
+# LoRA on INT8 layers: low-VRAM patch callable and the model patcher
+# =============================================================================
+
+try:
+    import comfy.model_patcher as _comfy_model_patcher
+    import comfy.lora as _comfy_lora
+    import comfy.utils as _comfy_utils
+    _COMFY_PATCHER_AVAILABLE = _COMFY_OPS_AVAILABLE
+except ImportError:
+    _COMFY_PATCHER_AVAILABLE = False
+
+
+def _int8_module_rot(module):
+    """The (kind, group) rotation of an INT8 layer, or None."""
+    if getattr(module, "_use_convrot", False):
+        return rot_for_group(getattr(module, "_convrot_groupsize", CONVROT_GROUP_SIZE))
+    return None
+
+
+def _dynamic_lora_entries(module, patches, rot, group_ok):
+    """Dynamic-LoRA (down_scaled, up, start, size) entries for one layer
+    (int8_quant.py:969-1008): the LoRA down projection is scaled by
+    alpha/rank * strength and, for a ConvRot layer, rotated like the weight
+    (W_rot = W H^T  =>  dW_rot = up (down H^T))."""
+    entries = []
+    for p in patches:
+        strength_patch, adapter, strength_model = p[0], p[1], p[2]
+        offset = p[3] if len(p) > 3 else None
+        if not hasattr(adapter, "weights"):
+            continue
+        weights = adapter.weights
+        if len(weights) != 6:
+            continue
+        up, down, alpha, mid, _dora, _reshape = weights
+        strength = strength_patch * strength_model
+        rank = down.shape[0] if down.ndim >= 2 else 1
+        scale = (alpha / rank) * strength if alpha is not None else strength
+        down_scaled = down.flatten(1) * scale
+        if mid is not None:
+            down_scaled = torch.mm(mid.flatten(1), down.flatten(1)) * scale
+        if rot is not None and group_ok(down_scaled.shape[1]):
+            down_scaled = ops.rotate(down_scaled.to(torch.float32).cuda(), *rot).to(down_scaled.dtype)
+        start = size = None
+        if offset is not None:
+            _dim, start, size = offset
+        entries.append((down_scaled, up.flatten(1), start, size))
+    return entries
+
+
+if _COMFY_PATCHER_AVAILABLE:
+
+    class INT8LowVramPatch:
+        """Low-VRAM LoRA on an INT8 layer as ComfyUI streams the weight in
+        (int8_quant.py:761-843): dequant (+ un-rotate) -> patch in float ->
+        re-rotate -> requantise with the layer's original scale."""
+        is_lowvram_patch = True
+
+        def __init__(self, key, patches, module, lora_mode):
+            self.key = key
+            self.patches = patches
+            self.module = module
+            self.lora_mode = lora_mode
+            self.prepared_patches = None
+
+        def memory_required(self):
+            return 0
+
+        def prepare(self, *args, **kwargs):
+            self.prepared_patches = list(self.patches[self.key])
+            return self.prepared_patches
+
+        def clear_prepared(self):
+            self.prepared_patches = None
+
+        def __call__(self, weight):
+            patches = self.prepared_patches if self.prepared_patches is not None else self.patches[self.key]
+            scale = self.module._get_weight_scale()
+            if isinstance(scale, torch.Tensor):
+                scale = scale.to(weight.device)
+            group = getattr(self.module, "_convrot_groupsize", CONVROT_GROUP_SIZE) \
+                if getattr(self.module, "_use_convrot", False) else 0
+            return lowvram_patch_int8(
+                weight, scale, group,
+                lambda w: _comfy_lora.calculate_weight(patches, w, self.key, intermediate_dtype=w.dtype),
+                stochastic=self.lora_mode == "Stochastic",
+                seed=_comfy_utils.string_to_seed(self.key) if self.lora_mode == "Stochastic" else 0)
+
+    class INT8ModelPatcher(_comfy_model_patcher.ModelPatcher):
+        """ModelPatcher that routes LoRA patches on INT8 layers through the
+        bake-in path (dequant -> patch -> requant, on the kernels) or the
+        dynamic path (low-rank branch in the forward), per
+        ``Int8TensorwiseOps.dynamic_lora`` (int8_quant.py:846-1110)."""
+
+        def finalize_pending_int8(self):
+            finalized = 0
+            for module in self.model.modules():
+                fn = getattr(module, "finalize_pending_int8", None)
+                if fn is not None and fn():
+                    finalized += 1
+            if finalized:
+                self.size = 0
+                torch.cuda.empty_cache()
+            return finalized
+
+        def _int8_module(self, key):
+            try:
+                module = _comfy_utils.get_attr(self.model, key.rsplit(".", 1)[0])
+            except AttributeError:
+                return None
+            return module if getattr(module, "_is_quantized", False) else None
+
+        def patch_weight_to_device(self, key, device_to=None, inplace_update=False, return_weight=False,
+                                   force_cast=False):
+            if key not in self.patches and not force_cast:
+                return super().patch_weight_to_device(key, device_to, inplace_update, return_weight, force_cast)
+            module = self._int8_module(key)
+            if module is None:
+                return super().patch_weight_to_device(key, device_to, inplace_update, return_weight, force_cast)
+            if Int8TensorwiseOps.Linear._is_bias_key(key):
+                return _comfy_utils.get_attr(self.model, key) if return_weight else None
+            patches = self.patches.get(key, [])
+
+            if not Int8TensorwiseOps.dynamic_lora:
+                # bake: always from the backed-up base weight (no stacking)
+                current = _comfy_utils.get_attr(self.model, key)
+                if device_to is None:
+                    device_to = current.device
+                if key not in self.backup:
+                    import collections
+                    Backup = collections.namedtuple("Dimension", ["weight", "inplace_update"])
+                    self.backup[key] = Backup(weight=current.to(device=self.offload_device, copy=inplace_update),
+                                              inplace_update=inplace_update)
+                    source = current
+                else:
+                    source = self.backup[key].weight
+                dev = device_to if torch.device(device_to).type == "cuda" else torch.device("cuda")
+                scale = module._get_weight_scale()
+                if isinstance(scale, torch.Tensor):
+                    scale = scale.to(dev)
+                group = getattr(module, "_convrot_groupsize", CONVROT_GROUP_SIZE) \
+                    if getattr(module, "_use_convrot", False) else 0
+                stochastic = getattr(Int8TensorwiseOps, "lora_mode", "None") == "Stochastic"
+                patched = lowvram_patch_int8(
+                    source.to(dev), scale, group,
+                    lambda w: _comfy_lora.calculate_weight(patches, w, key),
+                    stochastic=stochastic, seed=_comfy_utils.string_to_seed(key) if stochastic else 0)
+                patched = patched.to(current.device)
+                if return_weight:
+                    return patched
+                if inplace_update:
+                    current.data.copy_(patched)
+                else:
+                    _comfy_utils.set_attr(self.model, key, nn.Parameter(patched, requires_grad=False))
+                return None
+
+            # dynamic: low-rank branch evaluated in Linear.forward
+            weight = _comfy_utils.get_attr(self.model, key)
+            cache_key = tuple(id(p[1]) for p in patches)
+            if getattr(module, "_lora_cache_key", None) != cache_key:
+                device = weight.device if weight is not None else self.offload_device
+                rot = _int8_module_rot(module)
+                entries = _dynamic_lora_entries(module, patches, rot, lambda k: k % rot[1] == 0 if rot else False)
+                module.lora_patches = [(d.to(device), u.to(device), s0, sz) for d, u, s0, sz in entries]
+                module._lora_cache_key = cache_key
+            return weight if return_weight else None
+
+        def load(self, *args, **kwargs):
+            self.finalize_pending_int8()
+            if not Int8TensorwiseOps.dynamic_lora:
+                # restore the base INT8 weights so the bake starts from them
+                for k in list(self.backup):
+                    if k in self.patches and self._int8_module(k) is not None:
+                        bk = self.backup.pop(k)
+                        if bk.inplace_update:
+                            _comfy_utils.get_attr(self.model, k).data.copy_(bk.weight)
+                        else:
+                            _comfy_utils.set_attr(self.model, k, bk.weight)
+            for k in [k for k in self.backup if k not in self.patches]:  # stale patches
+                bk = self.backup.pop(k)
+                if bk.inplace_update:
+                    _comfy_utils.get_attr(self.model, k).data.copy_(bk.weight)
+                else:
+                    _comfy_utils.set_attr(self.model, k, bk.weight)
+            for name, module in self.model.named_modules():
+                if getattr(module, "lora_patches", None):
+                    if not Int8TensorwiseOps.dynamic_lora or (name + ".weight") not in self.patches:
+                        module.lora_patches = []
+            res = super().load(*args, **kwargs) if hasattr(super(), "load") else None
+            device_to = kwargs.get("device_to", args[0] if args else None)
+            for name, module in self.model.named_modules():
+                if not getattr(module, "_is_quantized", False):
+                    continue
+                wkey = name + ".weight"
+                if wkey not in self.patches:
+                    continue
+                if hasattr(module, "weight_function"):
+                    module.weight_function = [f for f in module.weight_function
+                                              if type(f).__name__ != "LowVramPatch"]
+                if Int8TensorwiseOps.dynamic_lora:
+                    module.weight_lowvram_function = None
+                    self.patch_weight_to_device(wkey, device_to=device_to)
+                else:
+                    module.weight_lowvram_function = INT8LowVramPatch(
+                        wkey, self.patches, module, getattr(Int8TensorwiseOps, "lora_mode", "None"))
+            return res
+
+        def unpatch_model(self, device_to=None, unpatch_weights=True):
+            if unpatch_weights:
+                for module in self.model.modules():
+                    if hasattr(module, "lora_patches"):
+                        module.lora_patches = []
+            return super().unpatch_model(device_to, unpatch_weights)
+
+        def clone(self, *args, **kwargs):
+            """Clone as an INT8-aware patcher: a patcher of another class is
+            re-typed to a subclass mixing this one in for the duration of the
+            base clone, so the copy keeps the INT8 LoRA routing
+            (int8_quant.py:1103-1135)."""
+            src_cls = self.__class__
+            if src_cls is INT8ModelPatcher:
+                return super().clone(*args, **kwargs)
+            mixed = src_cls if issubclass(src_cls, INT8ModelPatcher) else \
+                type(f"INT8_{src_cls.__name__}", (INT8ModelPatcher, src_cls), {})
+            self.__class__ = mixed
+            try:
+                if (hasattr(self, "is_dynamic") and not self.is_dynamic()
+                        and getattr(self, "cached_patcher_init", None) is None):
+                    self.cached_patcher_init = (lambda *a, **kw: self, ())
+                n = super().clone(*args, **kwargs)
+            finally:
+                self.__class__ = src_cls
+            disable_dynamic = args[0] if args else kwargs.get("disable_dynamic", False)
+            if disable_dynamic and not isinstance(n, INT8ModelPatcher):
+                n.__class__ = type(f"INT8_{n.__class__.__name__}", (INT8ModelPatcher, n.__class__), {})
+            return n
