@@ -162,6 +162,214 @@ def cpu_baseline(min_seconds=10.0, max_runs=60):
                       f"torch._int_mm, two-rounding epilogue)"}
 
 
+# ---------------------------------------------------------------------------
+# Flux-style MMDiT step with W8A8 + ConvRot on every linear
+# ---------------------------------------------------------------------------
+# hidden 3072, 24 heads x 128, 19 double-stream + 38 single-stream blocks,
+# MLP ratio 4, 4096 image + 512 text tokens, bf16 activations, attention and
+# RoPE in bf16 (torch SDPA), random-init weights, batch 8 with CFG = 16
+# forward samples per step, split evenly across ranks; seed 4.  ConvRot uses
+# the loaders' default block (regular, 256).
+DIT = dict(hidden=3072, heads=24, head_dim=128, mlp=4, double=19, single=38, img=4096, txt=512, samples=16,
+           seed=4, group=256, kind="regular")
+DIT_WARMUP, DIT_STEPS = 3, 3
+
+
+class _QLin:
+    """One quantised linear: int8 [N, K] rotated + per-channel scales, bf16 bias."""
+
+    def __init__(self, n, k, gen, dev, quant):
+        w = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32) * 0.02
+        self.wq, self.ws = quant(w)
+        self.b = (torch.randn((n,), generator=gen, device=dev) * 0.01).to(torch.bfloat16)
+        self.n, self.k = n, k
+        del w
+
+
+def _dit_params(dev, quant, n_double, n_single):
+    D, F_ = DIT["hidden"], DIT["hidden"] * DIT["mlp"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(DIT["seed"])
+    ones = torch.ones(DIT["head_dim"], device=dev, dtype=torch.bfloat16)
+    dbl = []
+    for _ in range(n_double):
+        blk = {}
+        for s in ("img", "txt"):
+            blk[s + "_mod"] = _QLin(6 * D, D, gen, dev, quant)
+            blk[s + "_qkv"] = _QLin(3 * D, D, gen, dev, quant)
+            blk[s + "_proj"] = _QLin(D, D, gen, dev, quant)
+            blk[s + "_mlp0"] = _QLin(F_, D, gen, dev, quant)
+            blk[s + "_mlp1"] = _QLin(D, F_, gen, dev, quant)
+        blk["qn"], blk["kn"] = ones, ones
+        dbl.append(blk)
+    sgl = []
+    for _ in range(n_single):
+        sgl.append({"mod": _QLin(3 * D, D, gen, dev, quant), "linear1": _QLin(3 * D + F_, D, gen, dev, quant),
+                    "linear2": _QLin(D, D + F_, gen, dev, quant), "qn": ones, "kn": ones})
+    return dbl, sgl
+
+
+def _rope_tables(L, dev):
+    hd = DIT["head_dim"]
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
+    ang = torch.arange(L, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+    return torch.cos(ang).to(torch.bfloat16), torch.sin(ang).to(torch.bfloat16)
+
+
+def _rope(x, cos, sin):
+    x1, x2 = x[..., 0::2], x[..., 1::2]
+    return torch.stack((x1 * cos - x2 * sin, x1 * sin + x2 * cos), dim=-1).flatten(-2)
+
+
+def _attention(qkv, blk, cos, sin):
+    B, L, _ = qkv.shape
+    H, hd = DIT["heads"], DIT["head_dim"]
+    q, k, v = qkv.view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
+    q = _rope(torch.nn.functional.rms_norm(q, (hd,), blk["qn"], 1e-6), cos, sin)
+    k = _rope(torch.nn.functional.rms_norm(k, (hd,), blk["kn"], 1e-6), cos, sin)
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    return o.transpose(1, 2).reshape(B, L, H * hd)
+
+
+def dit_forward(params, img, txt, vec, lin):
+    """One forward of the MMDiT over a batch; ``lin(x, layer)`` is the
+    quantised linear (the product op on the GPU, the reference's PyTorch
+    path on the CPU)."""
+    F = torch.nn.functional
+    D = DIT["hidden"]
+    dbl, sgl = params
+    Lt = txt.shape[1]
+    cos, sin = _rope_tables(Lt + img.shape[1], img.device)
+    svec = F.silu(vec)
+
+    def mod(x, shift, scale):
+        return F.layer_norm(x, (D,), eps=1e-6) * (1 + scale[:, None]) + shift[:, None]
+
+    for blk in dbl:
+        mi = lin(svec, blk["img_mod"]).chunk(6, dim=-1)
+        mt = lin(svec, blk["txt_mod"]).chunk(6, dim=-1)
+        qkv = torch.cat((lin(mod(txt, mt[0], mt[1]), blk["txt_qkv"]), lin(mod(img, mi[0], mi[1]), blk["img_qkv"])), 1)
+        o = _attention(qkv, blk, cos, sin)
+        txt = txt + mt[2][:, None] * lin(o[:, :Lt], blk["txt_proj"])
+        img = img + mi[2][:, None] * lin(o[:, Lt:], blk["img_proj"])
+        img = img + mi[5][:, None] * lin(F.gelu(lin(mod(img, mi[3], mi[4]), blk["img_mlp0"]), approximate="tanh"),
+                                         blk["img_mlp1"])
+        txt = txt + mt[5][:, None] * lin(F.gelu(lin(mod(txt, mt[3], mt[4]), blk["txt_mlp0"]), approximate="tanh"),
+                                         blk["txt_mlp1"])
+    x = torch.cat((txt, img), 1)
+    for blk in sgl:
+        m = lin(svec, blk["mod"]).chunk(3, dim=-1)
+        h = lin(mod(x, m[0], m[1]), blk["linear1"])
+        qkv, mlp = h.split((3 * D, DIT["mlp"] * D), dim=-1)
+        o = _attention(qkv.contiguous(), blk, cos, sin)
+        x = x + m[2][:, None] * lin(torch.cat((o, F.gelu(mlp, approximate="tanh")), -1), blk["linear2"])
+    return x[:, Lt:]
+
+
+def dit_int8_ops(samples, n_double, n_single):
+    """2*M*N*K over every quantised linear of one forward of ``samples``."""
+    D, F_, Li, Lt = DIT["hidden"], DIT["hidden"] * DIT["mlp"], DIT["img"], DIT["txt"]
+    per = 0
+    for L in (Li, Lt):
+        per += n_double * L * (3 * D * D + D * D + 2 * D * F_)
+    per += n_single * (Li + Lt) * ((3 * D + F_) * D + (D + F_) * D)
+    per += n_double * 2 * 6 * D * D + n_single * 3 * D * D  # modulation (one row per sample)
+    return 2.0 * samples * per
+
+
+def dit_inputs(samples, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    D = DIT["hidden"]
+    mk = lambda *shape: torch.randn(shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    return mk(samples, DIT["img"], D), mk(samples, DIT["txt"], D), mk(samples, D)
+
+
+def run_dit(pkg, dev, world, rank):
+    """DiT steps/s with the 16 samples split across ranks (strong scaling, no
+    collective), max step time over ranks; plus the CPU extrapolation."""
+    ops = pkg.ops
+    pub = pkg.int8_quant
+    rot = (DIT["kind"], DIT["group"])
+    per_rank = DIT["samples"] // world
+    if per_rank * world != DIT["samples"]:
+        return {"skipped": f"{DIT['samples']} samples do not split over {world} ranks"}
+    params = _dit_params(dev, lambda w: ops.quant_weight_int8(w, rot), DIT["double"], DIT["single"])
+
+    def lin(x, layer):
+        shp = x.shape
+        y = pub.int8_forward_dynamic_per_row(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16,
+                                             rot)
+        return y.reshape(*shp[:-1], layer.n)
+
+    img, txt, vec = dit_inputs(per_rank, dev, DIT["seed"] + 100 * rank)
+    with torch.no_grad():
+        for _ in range(DIT_WARMUP):
+            dit_forward(params, img, txt, vec, lin)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(DIT_STEPS):
+            out = dit_forward(params, img, txt, vec, lin)
+        e1.record(s)
+        torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / DIT_STEPS], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms.item())
+    finite = bool(torch.isfinite(out).all().item())
+    del params, img, txt, vec, out
+    torch.cuda.empty_cache()
+    ops_step = dit_int8_ops(DIT["samples"], DIT["double"], DIT["single"])
+    res = {"config": f"Flux-style MMDiT D={DIT['hidden']} heads={DIT['heads']}x{DIT['head_dim']} "
+                     f"{DIT['double']} double + {DIT['single']} single blocks, {DIT['img']}+{DIT['txt']} tokens, "
+                     f"{DIT['samples']} samples per step (batch 8 x CFG), W8A8 + ConvRot "
+                     f"{DIT['kind']}{DIT['group']} on every linear, bf16 SDPA attention, random init",
+           "steps_per_s": round(1000.0 / ms, 4), "ms_per_step": round(ms, 2), "n_gpus": world,
+           "samples_per_rank": per_rank, "scaling": "strong", "steps": DIT_STEPS, "warmup": DIT_WARMUP,
+           "int8_tops_in_step": round(ops_step / (ms * 1e-3) / 1e12, 1), "finite_output": finite}
+    return res
+
+
+def dit_cpu_baseline():
+    """One double and one single block for one sample through the
+    reference's PyTorch CPU linear, extrapolated to the full model and the
+    16-sample step."""
+    from oracle import torch_cpu_path as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    H = R.hadamard(DIT["group"], DIT["kind"])
+
+    def quant(w):
+        return R.quantize_int8_axiswise(R.rotate_activation(w, H, DIT["group"]), dim=1)
+
+    dev = torch.device("cpu")
+    timings = {}
+    for name, nd, ns in (("double", 1, 0), ("single", 0, 1)):
+        params = _dit_params(dev, quant, nd, ns)
+
+        def lin(x, layer):
+            shp = x.shape
+            y = R.convrot_w8a8_linear(x.reshape(-1, shp[-1]), H, DIT["group"], layer.wq, layer.ws, layer.b,
+                                      torch.bfloat16)
+            return y.reshape(*shp[:-1], layer.n)
+
+        img, txt, vec = dit_inputs(1, dev, DIT["seed"])
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            dit_forward(params, img, txt, vec, lin)
+            timings[name] = time.perf_counter() - t0
+        del params
+    t_step = DIT["samples"] * (DIT["double"] * timings["double"] + DIT["single"] * timings["single"])
+    return {"steps_per_s": round(1.0 / t_step, 6), "s_per_step": round(t_step, 1), "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"one double block ({timings['double']:.2f} s) and one single block "
+                                      f"({timings['single']:.2f} s) for one sample on the reference's PyTorch CPU "
+                                      f"path, extrapolated x{DIT['double']}/x{DIT['single']} blocks x{DIT['samples']} "
+                                      f"samples"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -279,6 +487,11 @@ def run_ours(args):
     quant_bytes = M * K * 2 + M * K + M * 4
     quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
+    del x, b, wq, ws, xq, xs, y, flush, x_host, y_host, xd
+    torch.cuda.empty_cache()
+    dit = run_dit(pkg, dev, world, rank) if not args.no_dit else {"skipped": "--no-dit"}
+    if rank == 0 and world == 1 and not args.no_dit:
+        dit["cpu_baseline"] = dit_cpu_baseline()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
@@ -302,6 +515,7 @@ def run_ours(args):
                     "api": "int8_quant.int8_forward_dynamic_per_row, pinned host x in, y out"},
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
+            "dit": dit,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -315,6 +529,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-dit", action="store_true", help="skip the MMDiT step measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
