@@ -505,7 +505,7 @@ def run_ours(args):
                          "achieved": round(gemm_tops, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                          "frac": round(gemm_tops / int8_peak, 4), "traffic": GEMM_TRAFFIC_BYTES,
                          "peak_source": f"2 x {src} dense bf16 ({bf16_tf} TFLOP/s) = dense int8"},
-            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_pair_kernel (fused Hadamard-128 + int8)",
+            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_x2_kernel (fused Hadamard-128 + int8, bulk-copy row ring)",
                                "achieved": round(quant_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
                                "frac": round(quant_gbs / hbm_gbs, 4), "bytes": quant_bytes,
                                "us": round(quant_ms * 1e3, 2)},

@@ -120,7 +120,11 @@ QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits) {
   if (!error_bits) return fail(QLIN_ERR_INVALID_ARG, "error_bits is null");
   int rc = check_device();
   if (rc) return rc;
-  return read_device_error(static_cast<cudaStream_t>(stream), error_bits);
+  uint32_t gemm_bits = 0, row_bits = 0;
+  if ((rc = read_device_error(static_cast<cudaStream_t>(stream), &gemm_bits))) return rc;
+  if ((rc = read_rowquant_error(static_cast<cudaStream_t>(stream), &row_bits))) return rc;
+  *error_bits = gemm_bits | row_bits;
+  return QLIN_OK;
 }
 
 QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,

@@ -52,5 +52,6 @@ int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const
 int launch_situ(int dt, const void* x, int64_t ldx, int64_t M, int64_t K, void* y, cudaStream_t stream);
 
 int read_device_error(cudaStream_t stream, uint32_t* bits);
+int read_rowquant_error(cudaStream_t stream, uint32_t* bits);
 
 }  // namespace qlin

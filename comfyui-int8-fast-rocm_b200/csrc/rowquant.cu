@@ -117,26 +117,41 @@ int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s,
   return fail(QLIN_ERR_UNSUPPORTED, "unsupported dtype/mode combination");
 }
 
-// Activation int8 quantisation, two chunks per thread (rowquant_pair_kernel).
-template <int DT, int KIND, int R>
-int launch_pair(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
-  auto kern = rowquant_pair_kernel<DT, KIND, R>;
-  const int per = (nchunks + 1) / 2;
+// Activation int8 quantisation (rowquant_x2_kernel): rows stream through a
+// shared-memory ring filled by bulk copies.  Returns QLIN_ERR_UNSUPPORTED
+// (without launching) when two ring slots do not fit in shared memory; the
+// caller then uses the register-prefetch kernel.
+constexpr size_t kX2SmemBudget = 200 * 1024;  // hard limit (one CTA)
+constexpr size_t kX2SmemTarget = 72 * 1024;   // keeps three CTAs per SM
+
+template <int DT, int KIND, int R, int CHUNKS>
+int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
+  auto kern = rowquant_x2_kernel<DT, KIND, R, CHUNKS>;
+  constexpr int EB = DT == DT_F32 ? 4 : 2;
+  const int per = (nchunks + CHUNKS - 1) / CHUNKS;
   const int tpr = ((per + 31) / 32) * 32;
   int rpc = 256 / tpr;
   if (rpc < 1) rpc = 1;
-  const size_t smem = (KIND != ROT_NONE && R > 1) ? (size_t)(rpc * tpr / 32) * 1024 * sizeof(float) : 0;
+  if (rpc > 32) rpc = 32;
+  const size_t row_bytes = (size_t)p.K * EB;
+  const int slot_bytes = (int)(((size_t)rpc * row_bytes + 127) / 128 * 128);
+  const size_t tbuf = (KIND != ROT_NONE && R > 1) ? (size_t)(rpc * tpr / 32) * 512 * sizeof(float) : 0;
+  int stages = 4;
+  while (stages > 2 && (size_t)stages * slot_bytes + tbuf + stages * 8 > kX2SmemTarget) --stages;
+  const size_t smem = (size_t)stages * slot_bytes + tbuf + stages * 8;
+  if (smem > kX2SmemBudget) return QLIN_ERR_UNSUPPORTED;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> attr_devices{0};
   const uint64_t bit = 1ull << (dev & 63);
-  if (smem > 0 && !(attr_devices.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant pair)");
+  if (!(attr_devices.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kX2SmemBudget);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant x2)");
     attr_devices.fetch_or(bit);
   }
-  static std::atomic<int> occ_key{-1}, occ_val{1};
-  const int key = tpr * rpc * 4 + (int)(smem >> 10);
+  static std::atomic<int64_t> occ_key{-1};
+  static std::atomic<int> occ_val{1};
+  const int64_t key = ((int64_t)tpr * rpc << 32) | (int64_t)smem;
   int per_sm = occ_val.load();
   if (occ_key.load() != key) {
     int nb = 0;
@@ -148,23 +163,34 @@ int launch_pair(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
   }
   const int64_t groups = (p.M + rpc - 1) / rpc;
   const int64_t cap = (int64_t)device_sm_count() * per_sm;
-  kern<<<dim3((unsigned)(groups < cap ? groups : cap)), dim3(tpr, rpc), smem, stream>>>(p);
+  kern<<<dim3((unsigned)(groups < cap ? groups : cap)), dim3(tpr, rpc), smem, stream>>>(p, stages, slot_bytes);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "rowquant pair launch");
+  if (e != cudaSuccess) return cuda_fail(e, "rowquant x2 launch");
   return QLIN_OK;
 }
 
-template <int DT>
-int pair_by_rot(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
+template <int DT, int CHUNKS>
+int x2_by_rot(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
   switch (rc) {
-    case RC_NONE: return launch_pair<DT, ROT_NONE, 1>(p, nchunks, s);
-    case RC_REG16: return launch_pair<DT, ROT_REGULAR, 1>(p, nchunks, s);
-    case RC_REG64: return launch_pair<DT, ROT_REGULAR, 4>(p, nchunks, s);
-    case RC_REG256: return launch_pair<DT, ROT_REGULAR, 16>(p, nchunks, s);
-    case RC_SYL32: return launch_pair<DT, ROT_SYLVESTER, 2>(p, nchunks, s);
-    case RC_SYL128: return launch_pair<DT, ROT_SYLVESTER, 8>(p, nchunks, s);
+    case RC_NONE: return launch_x2<DT, ROT_NONE, 1, CHUNKS>(p, nchunks, s);
+    case RC_REG16: return launch_x2<DT, ROT_REGULAR, 1, CHUNKS>(p, nchunks, s);
+    case RC_REG64: return launch_x2<DT, ROT_REGULAR, 4, CHUNKS>(p, nchunks, s);
+    case RC_REG256: return launch_x2<DT, ROT_REGULAR, 16, CHUNKS>(p, nchunks, s);
+    case RC_SYL32: return launch_x2<DT, ROT_SYLVESTER, 2, CHUNKS>(p, nchunks, s);
+    case RC_SYL128: return launch_x2<DT, ROT_SYLVESTER, 8, CHUNKS>(p, nchunks, s);
     default: return fail(QLIN_ERR_UNSUPPORTED, "unsupported rotation");
   }
+}
+
+// Chunks per thread: per-row work is amortised over more elements for long
+// rows, while short rows keep a full warp per row.
+template <int DT>
+int x2_by_chunks(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
+  if constexpr (DT != DT_F32) {  // float32 rows would need twice the prefetch registers
+    if (nchunks >= 512) return x2_by_rot<DT, 4>(rc, p, nchunks, s);
+  }
+  if (nchunks >= 64) return x2_by_rot<DT, 2>(rc, p, nchunks, s);
+  return x2_by_rot<DT, 1>(rc, p, nchunks, s);
 }
 
 }  // namespace
@@ -193,12 +219,15 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
 
   const int64_t nchunks = K / 16;
   if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
-  // Activation int8 hot path (1024 <= K <= 16384): two chunks per thread in
-  // packed f32x2 lanes.
-  if (L.mode == MODE_INT8 && L.dt_in == L.dt_q && nchunks >= 64 && nchunks <= 1024) {
-    if (L.dt_in == DT_BF16) return pair_by_rot<DT_BF16>(rc, p, (int)nchunks, stream);
-    if (L.dt_in == DT_F16) return pair_by_rot<DT_F16>(rc, p, (int)nchunks, stream);
-    if (L.dt_in == DT_F32) return pair_by_rot<DT_F32>(rc, p, (int)nchunks, stream);
+  // Activation int8 hot path: packed float32x2 kernel fed by a bulk-copy
+  // ring (falls through to the register-prefetch kernel when two ring slots
+  // do not fit in shared memory).
+  if (L.mode == MODE_INT8 && L.dt_in == L.dt_q) {
+    int rc2 = QLIN_ERR_UNSUPPORTED;
+    if (L.dt_in == DT_BF16) rc2 = x2_by_chunks<DT_BF16>(rc, p, (int)nchunks, stream);
+    if (L.dt_in == DT_F16) rc2 = x2_by_chunks<DT_F16>(rc, p, (int)nchunks, stream);
+    if (L.dt_in == DT_F32) rc2 = x2_by_chunks<DT_F32>(rc, p, (int)nchunks, stream);
+    if (rc2 != QLIN_ERR_UNSUPPORTED) return rc2;
   }
   LaunchShape s;
   s.chunks = nchunks <= 1024 ? 1 : 2;
@@ -228,6 +257,21 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
     default: break;
   }
   return fail(QLIN_ERR_UNSUPPORTED, "unsupported input/compute dtype pair");
+}
+
+// Error word of the row kernels: read and clear (bit 1: a bulk-copy wait
+// timed out).
+int read_rowquant_error(cudaStream_t stream, uint32_t* bits) {
+  uint32_t h = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_rq_error_bits, sizeof(uint32_t), 0, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "read row-kernel error word");
+  const uint32_t zero = 0;
+  e = cudaMemcpyToSymbolAsync(g_rq_error_bits, &zero, sizeof(uint32_t), 0, cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clear row-kernel error word");
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "sync");
+  *bits = h;
+  return QLIN_OK;
 }
 
 // Unaligned rows (no rotation): generic kernel.

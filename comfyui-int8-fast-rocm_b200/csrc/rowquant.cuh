@@ -475,29 +475,118 @@ __device__ __forceinline__ void xform_regs2(float2* v) {
   }
 }
 
-template <int DT, int KIND, int R>
-__global__ void __launch_bounds__(512) rowquant_pair_kernel(RowQuantParams p) {
-  extern __shared__ float stage_smem[];  // [warps][2][512] when R > 1
+// One 16-element chunk held as 8 float2 of adjacent elements (2i, 2i+1).
+// The within-chunk transform: the stride-1 digit inside each pair (scalar),
+// the higher digits on whole pairs (packed); same float32 expressions and
+// order as xform_regs<KIND, 16>.
+template <int KIND>
+__device__ __forceinline__ void xform16_x2(float2 (&v)[8]) {
+  if constexpr (KIND == ROT_SYLVESTER) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = v[i].x, b = v[i].y;
+      v[i] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
+    }
+#pragma unroll
+    for (int ps = 1; ps < 8; ps *= 2)
+#pragma unroll
+      for (int base = 0; base < 8; base += 2 * ps)
+#pragma unroll
+        for (int o = 0; o < ps; ++o) h2_sylvester2(v[base + o], v[base + o + ps]);
+  } else if constexpr (KIND == ROT_REGULAR) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float a0 = v[2 * q].x, a1 = v[2 * q].y, a2 = v[2 * q + 1].x, a3 = v[2 * q + 1].y;
+      h4_regular(a0, a1, a2, a3);
+      v[2 * q] = make_float2(a0, a1);
+      v[2 * q + 1] = make_float2(a2, a3);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) h4_regular2(v[j], v[j + 2], v[j + 4], v[j + 6]);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack_raw2(const RawChunk<DT>& r, float2 (&v)[8]) {
+  if constexpr (DT == DT_F32) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = make_float2(__uint_as_float(r.w[2 * i]), __uint_as_float(r.w[2 * i + 1]));
+  } else if constexpr (DT == DT_BF16) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = make_float2(__uint_as_float(r.w[i] << 16), __uint_as_float(r.w[i] & 0xFFFF0000u));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __half22float2(*reinterpret_cast<const __half2*>(&r.w[i]));
+  }
+}
+
+// max of three floats, NaN if any is NaN (sm_100 three-input form).
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Device error word of the row kernels (bit 1: a bulk-copy wait timed out);
+// one copy per translation unit, read through rowquant.cu.
+static __device__ uint32_t g_rq_error_bits = 0;
+constexpr uint64_t kRqWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ bool rq_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t iter = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++iter & 63u) == 0 && globaltimer_ns() - t0 > kRqWaitLimitNs) {
+      atomicOr(&g_rq_error_bits, 2u);
+      return false;
+    }
+  }
+}
+
+// Per-token int8 quantisation of activations (optionally ConvRot-rotated).
+// Rows stream through a ring of `stages` shared-memory slots filled by 1-D
+// bulk copies (one thread issues them, completion counted on an mbarrier per
+// slot), so several rows per CTA are in flight without costing registers.
+// Each thread owns CHUNKS 16-element chunks of its row (chunk t + i*TPR),
+// each kept as 8 float2 of adjacent elements: the packed float32x2 math, the
+// 128-bit shared-memory transposes and the pair-wise bf16 rounding use
+// register pairs directly; per-row work (reduction, scale) is shared by
+// 16*CHUNKS elements.  The per-row CTA barrier (absmax exchange) also
+// releases the row's slot for the next bulk copy.
+//
+// Dynamic shared memory: [stages x slot_bytes ring][warps x 512 floats
+// transpose buffers (rotations with R > 1)][stages mbarriers].
+template <int DT, int KIND, int R, int CHUNKS>
+__global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int stages, int slot_bytes) {
+  extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float red[2][32][33];
+  constexpr int EB = DT == DT_F32 ? 4 : 2;  // element bytes
+  constexpr bool STAGED = KIND != ROT_NONE && R > 1;
 
   const int tpr = blockDim.x;
+  const int rpc = blockDim.y;
   const int t = threadIdx.x;
+  const int tid = threadIdx.y * tpr + t;
   const int lane = t & 31;
   const int warp_in_row = t >> 5;
   const int nchunks = p.K >> 4;
-  const int ciA = t, ciB = t + tpr;
-  const bool hasA = ciA < nchunks, hasB = ciB < nchunks;
+  const int nwarps = (tpr >> 5) * rpc;
   const int warp_lin = threadIdx.y * (tpr >> 5) + warp_in_row;
-  float* bufA = stage_smem + warp_lin * 1024;
-  float* bufB = bufA + 512;
-  (void)bufA; (void)bufB;
+  const int row_bytes = p.K * EB;
+  uint8_t* ring = dsm;
+  float* wbuf = reinterpret_cast<float*>(dsm + (size_t)stages * slot_bytes) + warp_lin * 512;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)stages * slot_bytes +
+                                               (STAGED ? (size_t)nwarps * 512 * sizeof(float) : 0));
+  (void)wbuf;
 
   constexpr int J = 16 / R;
   constexpr int J2 = J < 4 ? J : 4;
   constexpr int NQ = J / J2;
   int nat[4];
   int s2[R > 1 ? R : 1][NQ];
-  if constexpr (KIND != ROT_NONE && R > 1) {
+  if constexpr (STAGED) {
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4) nat[q4] = swz<R>(lane * 16 + 4 * q4);
     const int g0 = (lane / R) * (16 * R);
@@ -509,176 +598,190 @@ __global__ void __launch_bounds__(512) rowquant_pair_kernel(RowQuantParams p) {
   }
   const float2 c2 = make_float2(p.rot_c, p.rot_c);
 
-  const int rows_per_cta = blockDim.y;
-  const int stride_rows = gridDim.x * rows_per_cta;
-  RawChunk<DT> rawA, rawB;
-  int first = blockIdx.x * rows_per_cta;
-  {
-    const int row = first + threadIdx.y;
-    if (row < p.M && hasA) load_raw<DT>(p.x, (int64_t)row * p.ldx + (int64_t)ciA * 16, rawA);
-    if (row < p.M && hasB) load_raw<DT>(p.x, (int64_t)row * p.ldx + (int64_t)ciB * 16, rawB);
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
   }
+  __syncthreads();
 
-  for (int it = 0; first < p.M; ++it, first += stride_rows) {
-    const int row = first + threadIdx.y;
-    const bool row_ok = row < p.M;
-    float2 v[16];
-    {
-      float va[16], vb[16];
-      if (row_ok && hasA) {
-        unpack_raw<DT>(rawA, va, 1.0f);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) va[j] = 0.0f;
-      }
-      if (row_ok && hasB) {
-        unpack_raw<DT>(rawB, vb, 1.0f);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) vb[j] = 0.0f;
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = make_float2(va[j], vb[j]);
+  // fill slot s with the rows of iteration `it` (thread 0 only)
+  const bool dense = (int64_t)p.ldx * EB == row_bytes;
+  auto issue = [&](int it, int s) {
+    const int64_t f = ((int64_t)blockIdx.x + (int64_t)it * gridDim.x) * rpc;
+    if (f >= p.M) return;
+    const int nrows = (int)min((int64_t)rpc, (int64_t)p.M - f);
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(nrows * row_bytes));
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x);
+    uint8_t* dst = ring + (size_t)s * slot_bytes;
+    if (dense) {
+      bulk_load(dst, src + f * row_bytes, (uint32_t)(nrows * row_bytes), &full[s]);
+    } else {
+      for (int r = 0; r < nrows; ++r)
+        bulk_load(dst + (size_t)r * row_bytes, src + (f + r) * (int64_t)p.ldx * EB, (uint32_t)row_bytes, &full[s]);
     }
-    {
-      const int nrow = row + stride_rows;
-      if (nrow < p.M && hasA) load_raw<DT>(p.x, (int64_t)nrow * p.ldx + (int64_t)ciA * 16, rawA);
-      if (nrow < p.M && hasB) load_raw<DT>(p.x, (int64_t)nrow * p.ldx + (int64_t)ciB * 16, rawB);
+  };
+  if (tid == 0)
+    for (int s = 0; s < stages; ++s) issue(s, s);
+
+  int s = 0;
+  uint32_t parity = 0;
+  for (int it = 0;; ++it) {
+    const int64_t first = ((int64_t)blockIdx.x + (int64_t)it * gridDim.x) * rpc;
+    if (first >= p.M) break;
+    const bool ok = rq_wait_bounded(&full[s], parity);
+    const int64_t row = first + threadIdx.y;
+    const bool row_ok = row < p.M && ok;
+    const uint8_t* rsrc = ring + (size_t)s * slot_bytes + (size_t)threadIdx.y * row_bytes;
+    float2 v[CHUNKS][8];
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int ci = t + i * tpr;
+      if (row_ok && ci < nchunks) {
+        RawChunk<DT> raw;
+        const uint4* q = reinterpret_cast<const uint4*>(rsrc + (size_t)ci * 16 * EB);
+#pragma unroll
+        for (int k = 0; k < RawChunk<DT>::WORDS / 4; ++k) {
+          const uint4 w = q[k];
+          raw.w[4 * k] = w.x; raw.w[4 * k + 1] = w.y; raw.w[4 * k + 2] = w.z; raw.w[4 * k + 3] = w.w;
+        }
+        unpack_raw2<DT>(raw, v[i]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = make_float2(0.0f, 0.0f);
+      }
     }
 
     if constexpr (KIND != ROT_NONE) {
-      xform_regs2<KIND, 16>(v);
-      if constexpr (R > 1) {
-        // stage 2 for both chunks: same swizzled transpose as rowquant_kernel,
-        // one 512-float region per chunk
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          *reinterpret_cast<float4*>(bufA + nat[q4]) =
-              make_float4(v[4 * q4].x, v[4 * q4 + 1].x, v[4 * q4 + 2].x, v[4 * q4 + 3].x);
-          *reinterpret_cast<float4*>(bufB + nat[q4]) =
-              make_float4(v[4 * q4].y, v[4 * q4 + 1].y, v[4 * q4 + 2].y, v[4 * q4 + 3].y);
-        }
-        __syncwarp();
-        float2 w[J][R];
+      for (int i = 0; i < CHUNKS; ++i) {
+        xform16_x2<KIND>(v[i]);
+        if constexpr (STAGED) {
+          // stage 2: transform over the chunk index within each group of R chunks
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
+          for (int q4 = 0; q4 < 4; ++q4)
+            *reinterpret_cast<float4*>(wbuf + nat[q4]) =
+                make_float4(v[i][2 * q4].x, v[i][2 * q4].y, v[i][2 * q4 + 1].x, v[i][2 * q4 + 1].y);
+          __syncwarp();
+          if constexpr (J >= 2) {
+            float2 w[J / 2][R];
 #pragma unroll
-          for (int q = 0; q < NQ; ++q) {
-            if constexpr (J2 == 4) {
-              const float4 fa = *reinterpret_cast<const float4*>(bufA + s2[r][q]);
-              const float4 fb = *reinterpret_cast<const float4*>(bufB + s2[r][q]);
-              w[4 * q][r] = make_float2(fa.x, fb.x); w[4 * q + 1][r] = make_float2(fa.y, fb.y);
-              w[4 * q + 2][r] = make_float2(fa.z, fb.z); w[4 * q + 3][r] = make_float2(fa.w, fb.w);
-            } else if constexpr (J2 == 2) {
-              const float2 fa = *reinterpret_cast<const float2*>(bufA + s2[r][q]);
-              const float2 fb = *reinterpret_cast<const float2*>(bufB + s2[r][q]);
-              w[0][r] = make_float2(fa.x, fb.x); w[1][r] = make_float2(fa.y, fb.y);
-            } else {
-              w[0][r] = make_float2(bufA[s2[r][q]], bufB[s2[r][q]]);
+            for (int r = 0; r < R; ++r) {
+#pragma unroll
+              for (int q = 0; q < NQ; ++q) {
+                if constexpr (J2 == 4) {
+                  const float4 f = *reinterpret_cast<const float4*>(wbuf + s2[r][q]);
+                  w[2 * q][r] = make_float2(f.x, f.y);
+                  w[2 * q + 1][r] = make_float2(f.z, f.w);
+                } else {
+                  w[0][r] = *reinterpret_cast<const float2*>(wbuf + s2[r][q]);
+                }
+              }
             }
-          }
-        }
 #pragma unroll
-        for (int jj = 0; jj < J; ++jj) xform_regs2<KIND, R>(w[jj]);
+            for (int jj = 0; jj < J / 2; ++jj) xform_regs2<KIND, R>(w[jj]);
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
+            for (int r = 0; r < R; ++r) {
 #pragma unroll
-          for (int q = 0; q < NQ; ++q) {
-            if constexpr (J2 == 4) {
-              *reinterpret_cast<float4*>(bufA + s2[r][q]) =
-                  make_float4(w[4 * q][r].x, w[4 * q + 1][r].x, w[4 * q + 2][r].x, w[4 * q + 3][r].x);
-              *reinterpret_cast<float4*>(bufB + s2[r][q]) =
-                  make_float4(w[4 * q][r].y, w[4 * q + 1][r].y, w[4 * q + 2][r].y, w[4 * q + 3][r].y);
-            } else if constexpr (J2 == 2) {
-              *reinterpret_cast<float2*>(bufA + s2[r][q]) = make_float2(w[0][r].x, w[1][r].x);
-              *reinterpret_cast<float2*>(bufB + s2[r][q]) = make_float2(w[0][r].y, w[1][r].y);
-            } else {
-              bufA[s2[r][q]] = w[0][r].x;
-              bufB[s2[r][q]] = w[0][r].y;
+              for (int q = 0; q < NQ; ++q) {
+                if constexpr (J2 == 4) {
+                  *reinterpret_cast<float4*>(wbuf + s2[r][q]) =
+                      make_float4(w[2 * q][r].x, w[2 * q][r].y, w[2 * q + 1][r].x, w[2 * q + 1][r].y);
+                } else {
+                  *reinterpret_cast<float2*>(wbuf + s2[r][q]) = w[0][r];
+                }
+              }
             }
+          } else {
+            float w[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) w[r] = wbuf[s2[r][0]];
+            xform_regs<KIND, R>(w);
+#pragma unroll
+            for (int r = 0; r < R; ++r) wbuf[s2[r][0]] = w[r];
           }
-        }
-        __syncwarp();
+          __syncwarp();
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 fa = *reinterpret_cast<const float4*>(bufA + nat[q4]);
-          const float4 fb = *reinterpret_cast<const float4*>(bufB + nat[q4]);
-          v[4 * q4] = make_float2(fa.x, fb.x); v[4 * q4 + 1] = make_float2(fa.y, fb.y);
-          v[4 * q4 + 2] = make_float2(fa.z, fb.z); v[4 * q4 + 3] = make_float2(fa.w, fb.w);
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 f = *reinterpret_cast<const float4*>(wbuf + nat[q4]);
+            v[i][2 * q4] = make_float2(f.x, f.y);
+            v[i][2 * q4 + 1] = make_float2(f.z, f.w);
+          }
+          __syncwarp();
         }
-        __syncwarp();
-      }
+        // normalise with the dtype-rounded constant, round to the compute dtype
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        v[j] = f2_mul(v[j], c2);
-        if constexpr (DT == DT_BF16) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(v[j].x, v[j].y);
-          const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
-          v[j] = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
-        } else if constexpr (DT == DT_F16) {
-          v[j] = __half22float2(__floats2half2_rn(v[j].x, v[j].y));
+        for (int j = 0; j < 8; ++j) {
+          v[i][j] = f2_mul(v[i][j], c2);
+          if constexpr (DT == DT_BF16) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(v[i][j].x, v[i][j].y);
+            const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+            v[i][j] = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+          } else if constexpr (DT == DT_F16) {
+            v[i][j] = __half22float2(__floats2half2_rn(v[i][j].x, v[i][j].y));
+          }
         }
       }
     }
 
-    // per-row absmax (NaN-propagating)
+    // per-row absmax (NaN-propagating); the CTA barrier also frees slot s
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) amax = fmax_nan(fmax_nan(amax, fabsf(v[j].x)), fabsf(v[j].y));
+    for (int i = 0; i < CHUNKS; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmax3_nan(amax, fabsf(v[i][j].x), fabsf(v[i][j].y));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    {
-      const int nw = tpr >> 5;
-      float (*rb)[33] = red[it & 1];
-      if (lane == 0) rb[threadIdx.y][warp_in_row] = amax;
-      __syncthreads();
-      amax = rb[threadIdx.y][0];
-      for (int w2 = 1; w2 < nw; ++w2) amax = fmax_nan(amax, rb[threadIdx.y][w2]);
+    const int nw = tpr >> 5;
+    float (*rb)[33] = red[it & 1];
+    if (lane == 0) rb[threadIdx.y][warp_in_row] = amax;
+    if (__syncthreads_or(!ok)) break;  // a bulk copy never arrived: leave together
+    if (tid == 0) {
+      fence_proxy_async_smem();  // this iteration's reads of slot s before the next copy into it
+      issue(it + stages, s);
     }
+    if (++s == stages) { s = 0; parity ^= 1; }
+    amax = rb[threadIdx.y][0];
+    for (int w2 = 1; w2 < nw; ++w2) amax = fmax_nan(amax, rb[threadIdx.y][w2]);
     if (!row_ok) continue;
-    int8_t* qrow = p.q + (int64_t)row * p.K;
+    int8_t* qrow = p.q + row * p.K;
     if (!(amax < __uint_as_float(0x7F800000u))) {
       // Inf or NaN in the row: scale Inf / NaN and every code 0 (torch's result)
       if (t == 0) p.scale[row] = amax;
-      if (hasA) *reinterpret_cast<int4*>(qrow + (int64_t)ciA * 16) = make_int4(0, 0, 0, 0);
-      if (hasB) *reinterpret_cast<int4*>(qrow + (int64_t)ciB * 16) = make_int4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        const int ci = t + i * tpr;
+        if (ci < nchunks) *reinterpret_cast<int4*>(qrow + (int64_t)ci * 16) = make_int4(0, 0, 0, 0);
+      }
       continue;
     }
     const float s_row = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);  // (absmax.float()/127).clamp(1e-30)
     const float inv = __frcp_rn(s_row);                          // 1.0 / scale
     if (t == 0) p.scale[row] = s_row;
     // |v| <= absmax: the round-half-even code of v * (1/scale) is already in
-    // [-127, 127]; the low byte of y + 1.5*2^23 is its two's complement.
-    // The product must be rounded before the add (torch rounds x * (1/s),
-    // then rounds to an integer).  The assembler has been seen to fuse a
-    // packed multiply with a following packed add even when both carry
-    // .rn, so the add is written as fma(product, one, magic) with `one` a
-    // kernel parameter equal to 1.0f: no single fused operation computes it.
+    // [-127, 127]; the low byte of y + 1.5*2^23 is its two's complement.  The
+    // product is rounded before the add (torch rounds x * (1/s), then to an
+    // integer); the add is an FMA with a run-time 1.0 so that the assembler
+    // cannot fuse it with the packed multiply (it did fuse a plain packed add).
     const float2 inv2 = make_float2(inv, inv);
     const float2 one2 = make_float2(p.one, p.one);
     const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    uint32_t ua[16], ub[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float2 y = f2_fma(f2_mul(v[j], inv2), one2, magic);
-      ua[j] = __float_as_uint(y.x);
-      ub[j] = __float_as_uint(y.y);
-    }
-    if (hasA) {
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int ci = t + i * tpr;
+      if (ci >= nchunks) continue;
+      uint32_t u[16];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 y = f2_fma(f2_mul(v[i][j], inv2), one2, magic);
+        u[2 * j] = __float_as_uint(y.x);
+        u[2 * j + 1] = __float_as_uint(y.y);
+      }
       int4 o;
-      o.x = (int)pack4((int)ua[0], (int)ua[1], (int)ua[2], (int)ua[3]);
-      o.y = (int)pack4((int)ua[4], (int)ua[5], (int)ua[6], (int)ua[7]);
-      o.z = (int)pack4((int)ua[8], (int)ua[9], (int)ua[10], (int)ua[11]);
-      o.w = (int)pack4((int)ua[12], (int)ua[13], (int)ua[14], (int)ua[15]);
-      *reinterpret_cast<int4*>(qrow + (int64_t)ciA * 16) = o;
-    }
-    if (hasB) {
-      int4 o;
-      o.x = (int)pack4((int)ub[0], (int)ub[1], (int)ub[2], (int)ub[3]);
-      o.y = (int)pack4((int)ub[4], (int)ub[5], (int)ub[6], (int)ub[7]);
-      o.z = (int)pack4((int)ub[8], (int)ub[9], (int)ub[10], (int)ub[11]);
-      o.w = (int)pack4((int)ub[12], (int)ub[13], (int)ub[14], (int)ub[15]);
-      *reinterpret_cast<int4*>(qrow + (int64_t)ciB * 16) = o;
+      o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
+      o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
+      o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
+      o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
+      *reinterpret_cast<int4*>(qrow + (int64_t)ci * 16) = o;
     }
   }
 }

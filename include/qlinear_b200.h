@@ -68,8 +68,9 @@ QLIN_API int qlin_version(void);
  * on the current device; callers that switch devices call this first). */
 QLIN_API int qlin_set_device(int device);
 QLIN_API const char* qlin_last_error(void);
-/* Reads and clears the device-side error word of the current device (bit 0:
- * a pipeline wait inside a GEMM kernel timed out).  Synchronises `stream`. */
+/* Reads and clears the device-side error words of the current device (bit 0:
+ * a pipeline wait inside a GEMM kernel timed out; bit 1: a row kernel's
+ * bulk-copy wait timed out).  Synchronises `stream`. */
 QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits);
 
 /* ---- (a) activation quantisation, fused with the ConvRot rotation -------- */

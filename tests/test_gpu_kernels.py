@@ -125,7 +125,7 @@ def test_fused_rotate_quant_long_rows(P):
     np.testing.assert_array_equal(s.cpu().numpy(), so)
 
 
-# Row lengths 1024..16384 run the two-chunks-per-thread kernel: 64 chunks
+# Row lengths 1024..16384 exercise the activation kernel's one-, two- and four-chunk forms: 64 chunks
 # (smallest), 65 (odd: the last thread has one chunk), 193, 1024 (largest).
 PAIR_CASES = [(1024, None), (1040, None), (3088, ("regular", 16)), (16384, None), (1024, ("sylvester", 32)),
               (1024, ("regular", 64)), (16384, ("regular", 256)), (16384, ("sylvester", 128)), (1040, ("regular", 16))]
