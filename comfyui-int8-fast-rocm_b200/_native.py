@@ -37,6 +37,7 @@ SIGNATURES = {
     "qlin_rotate": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P],
     "qlin_situ": [_P, _I, _L, _L, _L, _P, _P],
     "qlin_gemm_w8a8": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _P],
+    "qlin_gemm_w8a8_allgather": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _I, _L, _L, _L, _P],
     "qlin_int_mm": [_P, _P, _P, _L, _L, _L, _P],
     "qlin_int4_mm": [_P, _P, _P, _L, _L, _L, _P],
     "qlin_gemm_w4a4": [_P, _P, _P, _P, _P, _P, _I, _L, _L, _L, _P],

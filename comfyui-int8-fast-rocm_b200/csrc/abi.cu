@@ -201,6 +201,35 @@ QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t*
                      w_scale, bias, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream));
 }
 
+QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, const int8_t* w_shard,
+                                      const float* w_scale_shard, int wscale_mode, const void* bias_shard,
+                                      void* const* out_bufs, int n_out, int64_t col_off, int64_t ldo, int out_dtype,
+                                      int64_t M, int64_t N_shard, int64_t K, void* stream) {
+  int rc = gemm_common_checks(a, w_shard, M, N_shard, K, 16);
+  if (rc || M == 0 || N_shard == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_scale || !w_scale_shard || !out_bufs) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (wscale_mode != QLIN_WSCALE_ROW && wscale_mode != QLIN_WSCALE_TENSOR)
+    return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
+  if (n_out < 1 || n_out > 8) return fail(QLIN_ERR_INVALID_ARG, "n_out must be between 1 and 8");
+  if (col_off < 0 || ldo < col_off + N_shard) return fail(QLIN_ERR_INVALID_ARG, "col_off + N_shard > ldo");
+  const int es = esize(out_dtype);
+  if ((col_off * es) % 16 || (ldo * es) % 16) return fail(QLIN_ERR_ALIGNMENT, "col_off and ldo must be 16-byte aligned");
+  OutSpec o;
+  o.nout = n_out;
+  o.col_off = col_off;
+  o.ldo = ldo;
+  for (int i = 0; i < 8; ++i) o.outs[i] = nullptr;
+  for (int i = 0; i < n_out; ++i) {
+    if (!out_bufs[i]) return fail(QLIN_ERR_INVALID_ARG, "null output buffer");
+    if (!aligned16(out_bufs[i])) return fail(QLIN_ERR_ALIGNMENT, "output buffers must be 16-byte aligned");
+    o.outs[i] = out_bufs[i];
+  }
+  return launch_gemm_to(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, false, a, w_shard,
+                        a_scale, w_scale_shard, bias_shard, o, out_dtype, M, N_shard, K,
+                        static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c, int64_t M, int64_t N, int64_t K,
                          void* stream) {
   int rc = gemm_common_checks(a, w, M, N, K, 16);

@@ -140,12 +140,42 @@ bool pair_disabled() {
   return off;
 }
 
+GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale, const float* w_scale, const void* bias,
+                       const OutSpec& o, int sms) {
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.a_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = o.outs[0];
+  p.ldo = o.ldo;
+  p.num_sms = sms;
+  p.nout = o.nout;
+  p.col_off = o.col_off;
+  for (int i = 0; i < kMaxOutputs; ++i) p.outs[i] = i < o.nout ? o.outs[i] : nullptr;
+  return p;
+}
+
 }  // namespace
 
 int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
                 const float* w_scale, const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K,
                 cudaStream_t stream) {
+  OutSpec o;
+  o.outs[0] = out;
+  o.nout = 1;
+  o.col_off = 0;
+  o.ldo = N;
+  return launch_gemm_to(kind, b_int4, a, b, a_scale, w_scale, bias, o, out_dt, M, N, K, stream);
+}
+
+int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
+                   const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
+                   int64_t K, cudaStream_t stream) {
   if (M == 0 || N == 0) return QLIN_OK;
+  if (o.nout < 1 || o.nout > kMaxOutputs) return fail(QLIN_ERR_INVALID_ARG, "between 1 and 8 outputs");
   const int sms = device_sm_count();
   if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
   CUtensorMap ta, tb;
@@ -155,7 +185,7 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
     if (rc) return rc;
     rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    GemmParams p{(int)M, (int)N, (int)K, a_scale, w_scale, bias, out, N, sms};
+    GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
     return dispatch_pair(kind, out_dt, ta, tb, p, stream);
   }
   // Narrow outputs waste half a 256-wide tile; use 128 columns there.
@@ -169,16 +199,7 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
     rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B);
   }
   if (rc) return rc;
-  GemmParams p;
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)K;
-  p.a_scale = a_scale;
-  p.w_scale = w_scale;
-  p.bias = bias;
-  p.out = out;
-  p.ldo = N;
-  p.num_sms = sms;
+  GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
   if (b_int4) {
     if (BN == 128) return dispatch_epi<128, true>(kind, out_dt, ta, tb, p, stream);
     return dispatch_epi<256, true>(kind, out_dt, ta, tb, p, stream);

@@ -59,14 +59,19 @@ enum : int {
   EPI_I32 = 3,          // raw int32
 };
 
+constexpr int kMaxOutputs = 8;  // destinations of one GEMM (tensor-parallel gather)
+
 struct GemmParams {
   int M, N, K;
   const float* a_scale;  // [M]
   const float* w_scale;  // [N] or [1]
   const void* bias;      // [N] in the output dtype, or null
-  void* out;             // [M, N]
+  void* out;             // [M, ldo] output (the only destination when nout == 1)
   int64_t ldo;           // output row stride (elements)
   int num_sms;
+  int nout;              // number of destinations
+  int64_t col_off;       // column of this GEMM's column 0 in every destination
+  void* outs[kMaxOutputs];  // destinations when nout > 1 (peer buffers)
 };
 
 constexpr int GEMM_BM = 128;
@@ -201,7 +206,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
   constexpr int CPW = CHUNKS / 2;  // chunks per warp
   const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
   const int vec_n = out16 ? 8 : 4;
-  const bool vec_ok = (p.ldo % vec_n) == 0 && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
+  // (every destination base is 16-byte aligned when nout > 1: checked on the host)
+  const bool vec_ok = (p.ldo % vec_n) == 0 && (p.col_off % vec_n) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
   const bool has_bias = p.bias != nullptr;
   const int row = row0 + quarter * 32 + lane;
   const bool row_ok = row < p.M;
@@ -223,7 +230,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = (uint32_t)((int32_t)r[j] >> ISHIFT);
       }
-      int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+      int32_t* dst = reinterpret_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + p.col_off + col0;
       if (full_chunk) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -272,8 +279,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
 #pragma unroll
         for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
       }
-      auto* dst = reinterpret_cast<typename EO::T*>(p.out) + (int64_t)row * p.ldo + col0;
-      store_out_chunk<OUT_DT>(dst, y, full_chunk, ncols);
+      const int64_t off = (int64_t)row * p.ldo + p.col_off + col0;
+      if (p.nout == 1) {
+        store_out_chunk<OUT_DT>(reinterpret_cast<typename EO::T*>(p.out) + off, y, full_chunk, ncols);
+      } else {
+        // tensor-parallel gather: the same chunk into every rank's buffer
+        for (int o = 0; o < p.nout; ++o)
+          store_out_chunk<OUT_DT>(reinterpret_cast<typename EO::T*>(p.outs[o]) + off, y, full_chunk, ncols);
+      }
     }
   }
 }
@@ -335,6 +348,9 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
     acc ^= 1;
     if (acc == 0) acc_phase ^= 1;
   }
+  // peer stores are made visible system-wide before the kernel ends (the
+  // caller's cross-GPU barrier orders them with the peers' reads)
+  if (p.nout > 1) __threadfence_system();
 }
 
 template <int BN, int EPI, int OUT_DT, bool B_INT4>

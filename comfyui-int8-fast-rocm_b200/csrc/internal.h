@@ -41,6 +41,19 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
                 const float* w_scale, const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K,
                 cudaStream_t stream);
 
+// Output destinations of a GEMM: one buffer, or the same [M, ldo] buffer on
+// every rank of a tensor-parallel group (peer pointers), written at column
+// col_off.
+struct OutSpec {
+  void* outs[8];
+  int nout;
+  int64_t col_off;
+  int64_t ldo;
+};
+int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
+                   const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
+                   int64_t K, cudaStream_t stream);
+
 int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
                      int64_t K, cudaStream_t stream);

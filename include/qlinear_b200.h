@@ -124,6 +124,23 @@ QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t*
                             int wscale_mode, const void* bias, void* out, int out_dtype,
                             int64_t M, int64_t N, int64_t K, void* stream);
 
+/* Tensor-parallel W8A8 linear fused with its all-gather: this rank's column
+ * shard, out[:, col_off : col_off + N_shard] = the qlin_gemm_w8a8 result for
+ * (a, a_scale, w_shard, w_scale_shard, bias_shard), is stored into each of
+ * the n_out buffers out_bufs[0..n_out) -- [M, ldo] row-major in out_dtype,
+ * typically the peer mappings of one symmetric allocation, so every rank
+ * ends up with the whole [M, ldo] output without a separate collective.
+ * out_bufs is a host array; 1 <= n_out <= 8; col_off + N_shard <= ldo;
+ * every buffer, col_off and ldo 16-byte aligned in bytes.  The kernel ends
+ * with a system-scope fence; the caller orders the peers' reads after the
+ * stores with a cross-GPU barrier, and their previous reads of the buffers
+ * before the call.  No counterpart in the reference, which runs on one
+ * device: this is the column-split latency mode of a multi-GPU linear. */
+QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, const int8_t* w_shard,
+                                      const float* w_scale_shard, int wscale_mode, const void* bias_shard,
+                                      void* const* out_bufs, int n_out, int64_t col_off, int64_t ldo, int out_dtype,
+                                      int64_t M, int64_t N_shard, int64_t K, void* stream);
+
 /* c[M,N] int32 = a[M,K] . w[N,K]^T (torch._int_mm(a, w.T), int8_quant.py:124,152). */
 QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c,
                          int64_t M, int64_t N, int64_t K, void* stream);
