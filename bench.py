@@ -370,6 +370,56 @@ def dit_cpu_baseline():
                                       f"samples"}
 
 
+# ---------------------------------------------------------------------------
+# Tensor-parallel latency mode (N > 1): one column-parallel ConvRot W8A8
+# linear over a single sample's tokens, fused GEMM + all-gather vs the GEMM
+# followed by an NCCL all-gather.
+# ---------------------------------------------------------------------------
+TP = dict(M=4608, N=12288, K=3072, group=256, kind="regular", iters=20, warmup=5)
+
+
+def run_tp(pkg, dev, world, rank):
+    tp = pkg.tensor_parallel
+    ops = pkg.ops
+    rot = (TP["kind"], TP["group"])
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    w = torch.randn((TP["N"], TP["K"]), generator=g, device=dev) * 0.02
+    wq, ws = ops.quant_weight_int8(w, rot)
+    del w
+    b = (torch.randn((TP["N"],), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+    x = torch.randn((TP["M"], TP["K"]), generator=g, device=dev).to(torch.bfloat16)
+    res = {}
+    for mode in ("fused", "nccl"):
+        layer = tp.ColumnParallelInt8Linear(wq, ws, b, rot=rot, mode=mode)
+        for _ in range(TP["warmup"]):
+            layer(x)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(TP["iters"]):
+            layer(x)
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = torch.tensor([e0.elapsed_time(e1) * 1e3 / TP["iters"]], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(us, op=torch.distributed.ReduceOp.MAX)
+        res[mode + "_us"] = round(float(us.item()), 2)
+        del layer
+    shard = -(-TP["N"] // world)
+    link_bytes = TP["M"] * shard * 2 * (world - 1)  # bf16 shard pushed to every peer
+    flops = 2.0 * TP["M"] * shard * TP["K"]
+    _, bf16_tf, _ = peaks()
+    t_roof = max(flops / (2.0 * bf16_tf * 1e12), link_bytes / 770e9) * 1e6
+    res.update({"config": f"column-parallel ConvRot W8A8 linear, M={TP['M']} tokens (one sample) N={TP['N']} "
+                          f"K={TP['K']} over {world} GPUs, bf16 out gathered on every rank",
+                "roofline_us": round(t_roof, 2), "link_bytes_per_rank": link_bytes,
+                "roofline_note": "max(int8 ops / (2 x dense bf16 peak), NVLink bytes / 770 GB/s per direction)",
+                "frac_fused": round(t_roof / res["fused_us"], 3)})
+    return res
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -490,6 +540,7 @@ def run_ours(args):
     del x, b, wq, ws, xq, xs, y, flush, x_host, y_host, xd
     torch.cuda.empty_cache()
     dit = run_dit(pkg, dev, world, rank) if not args.no_dit else {"skipped": "--no-dit"}
+    tpres = run_tp(pkg, dev, world, rank) if world > 1 else None
     if rank == 0 and world == 1 and not args.no_dit:
         dit["cpu_baseline"] = dit_cpu_baseline()
     if rank == 0:
@@ -516,6 +567,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
             "dit": dit,
+            "tensor_parallel": tpres,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -29,16 +29,18 @@ PFN_encodeTiled_t get_encode_fn() {
   return fn;
 }
 
-// 2-D uint8 tensor map: `outer` rows of `inner` bytes, row pitch `pitch` bytes.
+// 2-D tensor map: `outer` rows of `inner` elements, row pitch `pitch` bytes
+// (uint8 elements unless `dtype` says otherwise).
 int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_inner,
-              uint32_t box_outer, CUtensorMapSwizzle swz) {
+              uint32_t box_outer, CUtensorMapSwizzle swz,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
   PFN_encodeTiled_t enc = get_encode_fn();
   if (!enc) return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {pitch};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = enc(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -72,6 +74,16 @@ template <int EPI, int OUT_DT>
 int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   using Cfg = PairCfg<EPI, OUT_DT>;
   auto kern = gemm_i8_pair_kernel<EPI, OUT_DT>;
+  // 16-bit output through TMA stores: one destination, 16-byte aligned rows
+  CUtensorMap tc = ta;
+  int use_tma_store = 0;
+  if (Cfg::TMA_ST && p.nout == 1 && (p.ldo * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+      (p.col_off * 2) % 16 == 0) {
+    const int rc = make_tmap(&tc, p.out, (uint64_t)(p.col_off + p.N), (uint64_t)p.M, (uint64_t)p.ldo * 2, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    if (rc) return rc;
+    use_tma_store = 1;
+  }
   static std::atomic<uint64_t> attr_devices{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -84,7 +96,7 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
   }
   const int num_tiles = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN);
   const int clusters = num_tiles < p.num_sms / 2 ? num_tiles : p.num_sms / 2;
-  kern<<<2 * clusters, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  kern<<<2 * clusters, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p, use_tma_store);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return QLIN_OK;

@@ -198,9 +198,16 @@ __device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, 
 // [tmem_acc, tmem_acc + BN): this warp converts TMEM lane quarter `quarter`
 // (rows row0 + 32*quarter + lane) and column half `half` (EPI_WARPS == 8),
 // with the tile's per-column parameters in shared memory (s_ws, s_b).
+// Stores through shared memory: each epilogue warp stages its 32 x 32 chunk
+// of 16-bit outputs in a 2 KB buffer laid out with the 64-byte TMA swizzle
+// (16-byte chunk k of row r at k ^ ((r >> 1) & 3): conflict-free row writes)
+// and one lane issues a TMA tensor store of the box.
+constexpr int EPI_STAGE_BYTES = 32 * 64;
+
 template <int BN, int EPI, int OUT_DT, int ISHIFT>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int row0, int colt0, int quarter,
-                                              int half, int lane, const float* s_ws, const float* s_b, float xs) {
+                                              int half, int lane, const float* s_ws, const float* s_b, float xs,
+                                              const CUtensorMap* tmC = nullptr, uint8_t* stage = nullptr) {
   using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
   constexpr int CHUNKS = BN / 32;
   constexpr int CPW = CHUNKS / 2;  // chunks per warp
@@ -223,7 +230,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
     uint32_t r[32];
     tmem_ld_32x32b_x32(tmem_acc + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
     tmem_ld_wait();
-    if (!row_ok || col0 >= p.N) continue;
+    const bool tma_st = tmC != nullptr;  // warp-uniform
+    if (tma_st ? (col0 >= p.N || row0 + quarter * 32 >= p.M) : (!row_ok || col0 >= p.N)) continue;
     if constexpr (EPI == EPI_I32) {
       if constexpr (ISHIFT > 0) {
         // 16*q weights: the accumulator is 16x the product, exactly
@@ -279,6 +287,34 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
 #pragma unroll
         for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
       }
+      if constexpr (OUT_DT == DT_BF16 || OUT_DT == DT_F16) {
+        if (tma_st) {
+          uint32_t w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if constexpr (OUT_DT == DT_BF16) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+              w[j] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              __half2 h = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+              w[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+          }
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<uint4*>(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tmC, stage, (int)(p.col_off + col0), row0 + quarter * 32);
+            bulk_commit_group();
+          }
+          continue;
+        }
+      }
       const int64_t off = (int64_t)row * p.ldo + p.col_off + col0;
       if (p.nout == 1) {
         store_out_chunk<OUT_DT>(reinterpret_cast<typename EO::T*>(p.out) + off, y, full_chunk, ncols);
@@ -300,7 +336,8 @@ template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR, int ISHIFT 
 __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* es, uint64_t* tfull, uint64_t* tempty,
                                               volatile int* abort_flag, uint32_t tmem_base, int first_tile,
                                               int tile_stride, int num_tiles, int num_m, int num_n, int row_off,
-                                              int warp, int lane) {
+                                              int warp, int lane, const CUtensorMap* tmC = nullptr,
+                                              uint8_t* stage = nullptr) {
   const int e = (warp - 2) * 32 + lane;  // 0..255
   const int quarter = warp & 3;
   const int half = (warp - 2) >> 2;
@@ -333,7 +370,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
     }
     epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter, half,
-                                   lane, es->ws[buf], es->bias[buf], xs);
+                                   lane, es->ws[buf], es->bias[buf], xs, tmC, stage);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
@@ -351,6 +388,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
   // peer stores are made visible system-wide before the kernel ends (the
   // caller's cross-GPU barrier orders them with the peers' reads)
   if (p.nout > 1) __threadfence_system();
+  if (tmC != nullptr && lane == 0) bulk_wait_all();  // TMA stores complete before exit
 }
 
 template <int BN, int EPI, int OUT_DT, bool B_INT4>
@@ -515,14 +553,21 @@ struct PairCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
   static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + 256 + 16 + sizeof(EpiSmem<BN>);
+  // 16-bit outputs leave through TMA stores staged per epilogue warp
+  static constexpr bool TMA_ST = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+  static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * EPI_STAGE_BYTES : 0;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 + 16 + sizeof(EpiSmem<BN>);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
+// tmC: the output as a 16-bit 2-D tensor map with 32 x 32 boxes and the
+// 64-byte swizzle; used when `use_tma_store` (one 16-byte-aligned
+// destination), else the epilogue stores directly.
 template <int EPI, int OUT_DT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>::NUM_THREADS, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmC, GemmParams p, int use_tma_store) {
   using Cfg = PairCfg<EPI, OUT_DT>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int BN = Cfg::BN;
@@ -530,7 +575,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* sC = sB + STAGES * Cfg::B_BYTES;  // [EPI_WARPS][EPI_STAGE_BYTES] (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;     // [2]
   uint64_t* tempty = tfull + 2;         // [2]
@@ -624,9 +670,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
   } else {
     // ---------------- epilogue (both CTAs) ----------------
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
+    const bool tma_st = Cfg::TMA_ST && use_tma_store;
+    if (tma_st && lane == 0) tma_prefetch_desc(&tmC);
     epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
                                                       num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
-                                                      lane);
+                                                      lane, tma_st ? &tmC : nullptr,
+                                                      sC + (warp - 2) * EPI_STAGE_BYTES);
   }
 
   tc_fence_before();
