@@ -231,7 +231,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
     tmem_ld_32x32b_x32(tmem_acc + c * 32 + ((uint32_t)(quarter * 32) << 16), r);
     tmem_ld_wait();
     const bool tma_st = tmC != nullptr;  // warp-uniform
-    if (tma_st ? (col0 >= p.N || row0 + quarter * 32 >= p.M) : (!row_ok || col0 >= p.N)) continue;
+    // gathered (peer) outputs also go through the staging buffer, then leave
+    // as row-contiguous stores
+    const bool peer_st = !tma_st && stage != nullptr && p.nout > 1;
+    const bool staged = tma_st || peer_st;
+    if (staged ? (col0 >= p.N || row0 + quarter * 32 >= p.M) : (!row_ok || col0 >= p.N)) continue;
     if constexpr (EPI == EPI_I32) {
       if constexpr (ISHIFT > 0) {
         // 16*q weights: the accumulator is 16x the product, exactly
@@ -288,7 +292,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
         for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
       }
       if constexpr (OUT_DT == DT_BF16 || OUT_DT == DT_F16) {
-        if (tma_st) {
+        if (staged) {
           uint32_t w[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -300,18 +304,43 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
               w[j] = *reinterpret_cast<uint32_t*>(&h);
             }
           }
-          if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
+          if (tma_st && lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
           __syncwarp();
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             *reinterpret_cast<uint4*>(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
                 make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-          fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(tmC, stage, (int)(p.col_off + col0), row0 + quarter * 32);
-            bulk_commit_group();
+          if (tma_st) {
+            fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(tmC, stage, (int)(p.col_off + col0), row0 + quarter * 32);
+              bulk_commit_group();
+            }
+            continue;
           }
+          __syncwarp();
+          // 128 16-byte granules (32 rows x 4): lane l takes granules l, l+32,
+          // l+64, l+96, so each store instruction covers 8 whole row segments
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int g = lane + 32 * it;
+            const int rr = g >> 2, k = g & 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
+            const int grow = row0 + quarter * 32 + rr;
+            const int gcol = col0 + 8 * k;
+            if (grow >= p.M || gcol >= p.N) continue;
+            const int64_t off = (int64_t)grow * p.ldo + p.col_off + gcol;
+            if (gcol + 8 <= p.N) {
+              for (int o = 0; o < p.nout; ++o)
+                *reinterpret_cast<uint4*>(reinterpret_cast<typename EO::T*>(p.outs[o]) + off) = v;
+            } else {
+              const typename EO::T* e = reinterpret_cast<const typename EO::T*>(&v);
+              for (int o = 0; o < p.nout; ++o)
+                for (int j = 0; j < p.N - gcol; ++j) reinterpret_cast<typename EO::T*>(p.outs[o])[off + j] = e[j];
+            }
+          }
+          __syncwarp();  // staging buffer reused by the next chunk
           continue;
         }
       }
