@@ -20,6 +20,7 @@ BF16, F16, F32, I8, I32 = range(5)
 ROT_NONE, ROT_REGULAR, ROT_SYLVESTER = range(3)
 WSCALE_TENSOR, WSCALE_ROW = 0, 1
 ROUND_NEAREST, ROUND_STOCHASTIC = 0, 1
+NORM_NONE, NORM_LAYER, NORM_RMS = range(3)
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -33,10 +34,12 @@ SIGNATURES = {
     "qlin_set_device": [_I],
     "qlin_device_error": [_P, _P],
     "qlin_quant_act_int8": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P, _P],
+    "qlin_quant_act_int8_norm": [_P, _I, _L, _L, _L, _I, _F, _P, _P, _L, _P, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_quant_act_int4": [_P, _I, _L, _L, _L, _I, _I, _F, _I, _F, _P, _P, _P],
     "qlin_rotate": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P],
     "qlin_situ": [_P, _I, _L, _L, _L, _P, _P],
     "qlin_gemm_w8a8": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _P],
+    "qlin_gemm_w8a8_fused": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _L, _P, _L, _P, _L, _L, _P],
     "qlin_gemm_w8a8_allgather": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _I, _L, _L, _L, _P],
     "qlin_int_mm": [_P, _P, _P, _L, _L, _L, _P],
     "qlin_int4_mm": [_P, _P, _P, _L, _L, _L, _P],

@@ -147,6 +147,33 @@ QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t 
   return launch_rowquant(L, x, ldx, M, K, rot_c, 0.0f, nullptr, 0, q, scale, nullptr, 0, s);
 }
 
+QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int norm_kind,
+                                      float eps, const void* norm_weight, const void* mod_mul, int64_t mul_ld,
+                                      const void* mod_add, int64_t add_ld, int64_t rows_per_sample, int rot_kind, int rot_group,
+                                      float rot_c, int8_t* q, float* scale, void* stream) {
+  if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (x_dtype != QLIN_BF16 && x_dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16 or F16");
+  if (norm_kind != QLIN_NORM_NONE && norm_kind != QLIN_NORM_LAYER && norm_kind != QLIN_NORM_RMS)
+    return fail(QLIN_ERR_INVALID_ARG, "bad norm_kind");
+  if (norm_weight != nullptr && norm_kind != QLIN_NORM_RMS)
+    return fail(QLIN_ERR_INVALID_ARG, "norm_weight is taken by QLIN_NORM_RMS only");
+  if (!(eps >= 0.0f)) return fail(QLIN_ERR_INVALID_ARG, "eps must be >= 0");
+  if ((mod_mul && mul_ld < K) || (mod_add && add_ld < K)) return fail(QLIN_ERR_INVALID_ARG, "modulation row stride < K");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (!rows_vec_ok(x, K, ldx, x_dtype) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "the fused prologue needs K % 16 == 0 and 16-byte aligned rows");
+  if ((norm_weight && !aligned16(norm_weight)) || (mod_mul && (!aligned16(mod_mul) || (mul_ld * 2) % 16)) ||
+      (mod_add && (!aligned16(mod_add) || (add_ld * 2) % 16)))
+    return fail(QLIN_ERR_ALIGNMENT, "norm weight and modulation rows must be 16-byte aligned");
+  FusedPrologue f{norm_kind, eps, norm_weight, mod_mul, mul_ld, mod_add, add_ld, rows_per_sample};
+  return launch_rowquant_fused(x_dtype, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, rot_c, x, ldx, M, K, f,
+                               q, scale, static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                  int rot_group, float rot_c, int group, float clamp_min, int8_t* q, float* scale,
                                  void* stream) {
@@ -199,6 +226,35 @@ QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t*
     return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
   return launch_gemm(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, false, a, w, a_scale,
                      w_scale, bias, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                  int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
+                                  int64_t K, int64_t gelu_col0, const void* residual, int64_t ld_res,
+                                  const void* gate, int64_t gate_ld, int64_t rows_per_gate, void* stream) {
+  int rc = gemm_common_checks(a, w, M, N, K, 16);
+  if (rc || M == 0 || N == 0) return rc;
+  if (out_dtype != QLIN_BF16 && out_dtype != QLIN_F16)
+    return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16 or F16 for the fused epilogue");
+  if (!a_scale || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (wscale_mode != QLIN_WSCALE_ROW && wscale_mode != QLIN_WSCALE_TENSOR)
+    return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
+  if (gelu_col0 < 0) return fail(QLIN_ERR_INVALID_ARG, "gelu_col0 < 0");
+  if (gate && !residual) return fail(QLIN_ERR_INVALID_ARG, "a gate needs a residual");
+  if (residual && ld_res < N) return fail(QLIN_ERR_INVALID_ARG, "ld_res < N");
+  if (gate && gate_ld < N) return fail(QLIN_ERR_INVALID_ARG, "gate_ld < N");
+  if ((residual && (!aligned16(residual) || (ld_res * 2) % 16)) || (gate && (!aligned16(gate) || (gate_ld * 2) % 16)))
+    return fail(QLIN_ERR_ALIGNMENT, "residual and gate rows must be 16-byte aligned");
+  if (N % 8) return fail(QLIN_ERR_ALIGNMENT, "the fused epilogue needs N % 8 == 0");
+  OutSpec o;
+  for (int i = 0; i < 8; ++i) o.outs[i] = nullptr;
+  o.outs[0] = out;
+  o.nout = 1;
+  o.col_off = 0;
+  o.ldo = N;
+  EpiPost e{gelu_col0 < N ? gelu_col0 : INT64_MAX, residual, ld_res, gate, gate_ld, rows_per_gate};
+  return launch_gemm_to(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, false, a, w, a_scale,
+                        w_scale, bias, o, out_dtype, M, N, K, static_cast<cudaStream_t>(stream), &e);
 }
 
 QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, const int8_t* w_shard,

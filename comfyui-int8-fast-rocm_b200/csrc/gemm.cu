@@ -1,5 +1,6 @@
 // Host side of the tcgen05 GEMMs: TMA descriptors, tile configuration, launch.
 #include <atomic>
+#include <cstdint>
 #include <cstdlib>
 #include <mutex>
 
@@ -103,7 +104,18 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
 }
 
 int dispatch_pair(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool post = false) {
+  if (post) {  // 16-bit outputs only (checked by the caller)
+    if (kind == GEMM_W8A8_ROW) {
+      if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_ROW | EPI_POST, DT_BF16>(ta, tb, p, s);
+      if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_ROW | EPI_POST, DT_F16>(ta, tb, p, s);
+    }
+    if (kind == GEMM_W8A8_TENSOR) {
+      if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_TENSOR | EPI_POST, DT_BF16>(ta, tb, p, s);
+      if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_TENSOR | EPI_POST, DT_F16>(ta, tb, p, s);
+    }
+    return fail(QLIN_ERR_UNSUPPORTED, "epilogue steps need a W8A8 GEMM with bf16 or f16 output");
+  }
   if (kind == GEMM_I32) return launch_pair_cfg<EPI_I32, DT_F32>(ta, tb, p, s);
   if (kind == GEMM_W8A8_ROW) {
     if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_ROW, DT_BF16>(ta, tb, p, s);
@@ -120,7 +132,22 @@ int dispatch_pair(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap
 
 template <int BN, bool B_INT4>
 int dispatch_epi(int kind, int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                 cudaStream_t s) {
+                 cudaStream_t s, bool post = false) {
+  if constexpr (!B_INT4) {
+    if (post) {
+      if (kind == GEMM_W8A8_ROW) {
+        if (out_dt == DT_BF16) return launch_cfg<BN, EPI_W8A8_ROW | EPI_POST, DT_BF16, false>(ta, tb, p, s);
+        if (out_dt == DT_F16) return launch_cfg<BN, EPI_W8A8_ROW | EPI_POST, DT_F16, false>(ta, tb, p, s);
+      }
+      if (kind == GEMM_W8A8_TENSOR) {
+        if (out_dt == DT_BF16) return launch_cfg<BN, EPI_W8A8_TENSOR | EPI_POST, DT_BF16, false>(ta, tb, p, s);
+        if (out_dt == DT_F16) return launch_cfg<BN, EPI_W8A8_TENSOR | EPI_POST, DT_F16, false>(ta, tb, p, s);
+      }
+      return fail(QLIN_ERR_UNSUPPORTED, "epilogue steps need a W8A8 GEMM with bf16 or f16 output");
+    }
+  } else {
+    if (post) return fail(QLIN_ERR_UNSUPPORTED, "epilogue steps need a W8A8 GEMM with bf16 or f16 output");
+  }
   if (kind == GEMM_I32) return launch_cfg<BN, EPI_I32, DT_F32, B_INT4>(ta, tb, p, s);
   if constexpr (!B_INT4) {
     if (kind == GEMM_W8A8_ROW) {
@@ -167,7 +194,18 @@ GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale, co
   p.nout = o.nout;
   p.col_off = o.col_off;
   for (int i = 0; i < kMaxOutputs; ++i) p.outs[i] = i < o.nout ? o.outs[i] : nullptr;
+  p.gelu_col0 = INT64_MAX;  // EPI_POST fields: no GELU, no residual
+  p.rows_per_gate = 1;
   return p;
+}
+
+void set_post(GemmParams& p, const EpiPost& e) {
+  p.gelu_col0 = e.gelu_col0;
+  p.residual = e.residual;
+  p.ld_res = e.ld_res;
+  p.gate = e.gate;
+  p.gate_ld = e.gate_ld;
+  p.rows_per_gate = e.rows_per_gate > 0 ? e.rows_per_gate : INT64_MAX;
 }
 
 }  // namespace
@@ -185,9 +223,10 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
 
 int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
                    const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
-                   int64_t K, cudaStream_t stream) {
+                   int64_t K, cudaStream_t stream, const EpiPost* post) {
   if (M == 0 || N == 0) return QLIN_OK;
   if (o.nout < 1 || o.nout > kMaxOutputs) return fail(QLIN_ERR_INVALID_ARG, "between 1 and 8 outputs");
+  if (post != nullptr && o.nout != 1) return fail(QLIN_ERR_UNSUPPORTED, "epilogue steps need one destination");
   const int sms = device_sm_count();
   if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
   CUtensorMap ta, tb;
@@ -198,7 +237,8 @@ int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, cons
     rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
-    return dispatch_pair(kind, out_dt, ta, tb, p, stream);
+    if (post != nullptr) set_post(p, *post);
+    return dispatch_pair(kind, out_dt, ta, tb, p, stream, post != nullptr);
   }
   // Narrow outputs waste half a 256-wide tile; use 128 columns there.
   const int BN = (N <= 128) ? 128 : 256;
@@ -212,12 +252,14 @@ int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, cons
   }
   if (rc) return rc;
   GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
+  if (post != nullptr) set_post(p, *post);
+  const bool ps = post != nullptr;
   if (b_int4) {
-    if (BN == 128) return dispatch_epi<128, true>(kind, out_dt, ta, tb, p, stream);
-    return dispatch_epi<256, true>(kind, out_dt, ta, tb, p, stream);
+    if (BN == 128) return dispatch_epi<128, true>(kind, out_dt, ta, tb, p, stream, ps);
+    return dispatch_epi<256, true>(kind, out_dt, ta, tb, p, stream, ps);
   }
-  if (BN == 128) return dispatch_epi<128, false>(kind, out_dt, ta, tb, p, stream);
-  return dispatch_epi<256, false>(kind, out_dt, ta, tb, p, stream);
+  if (BN == 128) return dispatch_epi<128, false>(kind, out_dt, ta, tb, p, stream, ps);
+  return dispatch_epi<256, false>(kind, out_dt, ta, tb, p, stream, ps);
 }
 
 namespace {

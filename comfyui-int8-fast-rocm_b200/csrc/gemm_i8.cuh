@@ -57,7 +57,9 @@ enum : int {
   EPI_W8A8_TENSOR = 1,  // dt(dt(float(acc)*(ws*xs[m])) + bias[n])
   EPI_W4A4_ROW = 2,     // dt(float(acc)*xs[m]*ws[n] + float(bias[n]))
   EPI_I32 = 3,          // raw int32
+  EPI_POST = 8,         // flag on the W8A8 epilogues: GELU / residual + gate after them
 };
+constexpr int epi_base(int epi) { return epi & 7; }
 
 constexpr int kMaxOutputs = 8;  // destinations of one GEMM (tensor-parallel gather)
 
@@ -72,6 +74,15 @@ struct GemmParams {
   int nout;              // number of destinations
   int64_t col_off;       // column of this GEMM's column 0 in every destination
   void* outs[kMaxOutputs];  // destinations when nout > 1 (peer buffers)
+  // EPI_POST steps (16-bit outputs): y = dt(gelu_tanh(y)) for columns >=
+  // gelu_col0, then y = dt(residual + dt(gate * y)) (dt(residual + y)
+  // without a gate); residual [M, ld_res], gate row = row / rows_per_gate
+  int64_t gelu_col0;
+  const void* residual;
+  int64_t ld_res;
+  const void* gate;
+  int64_t gate_ld;
+  int64_t rows_per_gate;
 };
 
 constexpr int GEMM_BM = 128;
@@ -186,11 +197,79 @@ __device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, 
   if (e >= BN) return;
   const int col = colt0 + e;
   if (col >= p.N) return;
-  if constexpr (EPI == EPI_W8A8_ROW) ws = __ldg(p.w_scale + col);
+  if constexpr (epi_base(EPI) == EPI_W8A8_ROW) ws = __ldg(p.w_scale + col);
   // packed-int4 B is unpacked as 16*q: ws/16 (exact) restores the products
-  if constexpr (EPI == EPI_W4A4_ROW) ws = __ldg(p.w_scale + col) * 0.0625f;
+  if constexpr (epi_base(EPI) == EPI_W4A4_ROW) ws = __ldg(p.w_scale + col) * 0.0625f;
   if constexpr (EPI != EPI_I32) {
     if (p.bias != nullptr) b = Elem<OUT_DT>::to_f(reinterpret_cast<const typename Elem<OUT_DT>::T*>(p.bias)[col]);
+  }
+}
+
+// tanh-form GELU in float32 as PyTorch's CUDA kernel evaluates
+// F.gelu(approximate="tanh"): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+// with the inner sum contracted to one FMA (nvcc's default contraction in
+// that build) and CUDA's tanhf.
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack8(uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (DT == DT_BF16) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+// EPI_POST steps on one thread's 32 output columns [col0, col0 + ncols) of
+// row `row` (values already rounded to the output dtype).  Residual and gate
+// rows are 16-byte aligned (checked on the host).
+template <int OUT_DT>
+__device__ __forceinline__ void epi_post(const GemmParams& p, float (&y)[32], int row, int col0, int ncols) {
+  using EO = Elem<OUT_DT>;
+  using T = typename EO::T;
+  if (p.gelu_col0 < (int64_t)col0 + 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j >= p.gelu_col0) y[j] = EO::round(gelu_tanh_f(y[j]));
+  }
+  if (p.residual == nullptr || row >= p.M) return;
+  const T* rs = reinterpret_cast<const T*>(p.residual) + (int64_t)row * p.ld_res + col0;
+  const T* gs = p.gate == nullptr ? nullptr
+                                  : reinterpret_cast<const T*>(p.gate) + (int64_t)(row / p.rows_per_gate) * p.gate_ld + col0;
+  if (ncols == 32) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float rv[8], gv[8];
+      unpack8<OUT_DT>(__ldg(reinterpret_cast<const uint4*>(rs) + q), rv);
+      if (gs != nullptr) {
+        unpack8<OUT_DT>(__ldg(reinterpret_cast<const uint4*>(gs) + q), gv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[8 * q + k] = EO::round(__fadd_rn(rv[k], EO::round(__fmul_rn(gv[k], y[8 * q + k]))));
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[8 * q + k] = EO::round(__fadd_rn(rv[k], y[8 * q + k]));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j >= ncols) continue;
+      const float t = gs != nullptr ? EO::round(__fmul_rn(EO::to_f(gs[j]), y[j])) : y[j];
+      y[j] = EO::round(__fadd_rn(EO::to_f(rs[j]), t));
+    }
   }
 }
 
@@ -209,9 +288,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
                                               int half, int lane, const float* s_ws, const float* s_b, float xs,
                                               const CUtensorMap* tmC = nullptr, uint8_t* stage = nullptr) {
   using EO = Elem<OUT_DT>;  // EPI_I32 ignores it (instantiated with DT_F32)
+  constexpr int EB = epi_base(EPI);
+  constexpr bool POST = (EPI & EPI_POST) != 0;
   constexpr int CHUNKS = BN / 32;
   constexpr int CPW = CHUNKS / 2;  // chunks per warp
-  const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+  const bool out16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EB != EPI_I32;
   const int vec_n = out16 ? 8 : 4;
   // (every destination base is 16-byte aligned when nout > 1: checked on the host)
   const bool vec_ok = (p.ldo % vec_n) == 0 && (p.col_off % vec_n) == 0 &&
@@ -220,7 +301,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
   const int row = row0 + quarter * 32 + lane;
   const bool row_ok = row < p.M;
   float s_tensor = 0.0f;
-  if constexpr (EPI == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
+  if constexpr (EB == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
 #pragma unroll 1
   for (int cc = 0; cc < CPW; ++cc) {
     const int c = half * CPW + cc;
@@ -236,7 +317,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
     const bool peer_st = !tma_st && stage != nullptr && p.nout > 1;
     const bool staged = tma_st || peer_st;
     if (staged ? (col0 >= p.N || row0 + quarter * 32 >= p.M) : (!row_ok || col0 >= p.N)) continue;
-    if constexpr (EPI == EPI_I32) {
+    if constexpr (EB == EPI_I32) {
       if constexpr (ISHIFT > 0) {
         // 16*q weights: the accumulator is 16x the product, exactly
 #pragma unroll
@@ -259,7 +340,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         float wv[4] = {0.f, 0.f, 0.f, 0.f};
-        if constexpr (EPI != EPI_W8A8_TENSOR) {
+        if constexpr (EB != EPI_W8A8_TENSOR) {
           const float4 t = w4[i];
           wv[0] = t.x; wv[1] = t.y; wv[2] = t.z; wv[3] = t.w;
         }
@@ -268,9 +349,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
           const int j = 4 * i + k;
           const float f = __int2float_rn((int32_t)r[j]);  // res.float()
           float v;
-          if constexpr (EPI == EPI_W8A8_TENSOR) {
+          if constexpr (EB == EPI_W8A8_TENSOR) {
             v = EO::round(__fmul_rn(f, s_tensor));             // .mul_(ws * xs).to(dt)
-          } else if constexpr (EPI == EPI_W8A8_ROW) {
+          } else if constexpr (EB == EPI_W8A8_ROW) {
             v = EO::round(__fmul_rn(__fmul_rn(f, xs), wv[k]));  // .mul_(xs).mul_(ws.T).to(dt)
           } else {
             v = __fmul_rn(__fmul_rn(f, xs), wv[k]);            // float32, rounded once below
@@ -287,10 +368,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
           y[4 * i + 2] = EO::round(__fadd_rn(y[4 * i + 2], t.z));
           y[4 * i + 3] = EO::round(__fadd_rn(y[4 * i + 3], t.w));
         }
-      } else if constexpr (EPI == EPI_W4A4_ROW) {
+      } else if constexpr (EB == EPI_W4A4_ROW) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) y[j] = EO::round(y[j]);
       }
+      if constexpr (POST) epi_post<OUT_DT>(p, y, row, col0, ncols);
       if constexpr (OUT_DT == DT_BF16 || OUT_DT == DT_F16) {
         if (staged) {
           uint32_t w[16];

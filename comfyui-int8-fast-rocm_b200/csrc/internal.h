@@ -31,6 +31,21 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
                     float clamp_min, const float* in_scale, int in_scale_per_row, int8_t* q, float* scale,
                     void* out, uint64_t seed, cudaStream_t stream);
 
+// Row norm + modulation prologue of the int8 activation quantiser (see
+// RowQuantParams): norm_kind NORM_*, vectors in the input dtype.
+struct FusedPrologue {
+  int norm_kind;
+  float eps;
+  const void* norm_w;
+  const void* mod_mul;
+  int64_t mul_ld;
+  const void* mod_add;
+  int64_t add_ld;
+  int64_t rows_per_sample;  // <= 0: one sample
+};
+int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
+                          int64_t K, const FusedPrologue& f, int8_t* q, float* scale, cudaStream_t stream);
+
 int launch_rowquant_generic(int dt, int mode, const void* x, int64_t ldx, int64_t M, int64_t K, float clamp_min,
                             int8_t* q, float* scale, cudaStream_t stream);
 
@@ -50,9 +65,21 @@ struct OutSpec {
   int64_t col_off;
   int64_t ldo;
 };
+// Element-wise steps after the W8A8 epilogue (16-bit outputs, one
+// destination): y = dt(gelu_tanh(y)) for columns >= gelu_col0, then
+// y = dt(residual + dt(gate * y)) (or dt(residual + y) without a gate), gate
+// row = output row / rows_per_gate.
+struct EpiPost {
+  int64_t gelu_col0;        // >= N: no GELU
+  const void* residual;     // [M, ld_res] or null
+  int64_t ld_res;
+  const void* gate;         // [M / rows_per_gate, gate_ld] or null
+  int64_t gate_ld;
+  int64_t rows_per_gate;
+};
 int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
                    const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
-                   int64_t K, cudaStream_t stream);
+                   int64_t K, cudaStream_t stream, const EpiPost* post = nullptr);
 
 int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,

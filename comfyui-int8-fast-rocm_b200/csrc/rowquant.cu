@@ -124,9 +124,9 @@ int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s,
 constexpr size_t kX2SmemBudget = 200 * 1024;  // hard limit (one CTA)
 constexpr size_t kX2SmemTarget = 72 * 1024;   // keeps three CTAs per SM
 
-template <int DT, int KIND, int R, int CHUNKS>
+template <int DT, int KIND, int R, int CHUNKS, bool FUSED>
 int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
-  auto kern = rowquant_x2_kernel<DT, KIND, R, CHUNKS>;
+  auto kern = rowquant_x2_kernel<DT, KIND, R, CHUNKS, FUSED>;
   constexpr int EB = DT == DT_F32 ? 4 : 2;
   const int per = (nchunks + CHUNKS - 1) / CHUNKS;
   const int tpr = ((per + 31) / 32) * 32;
@@ -169,28 +169,28 @@ int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
   return QLIN_OK;
 }
 
-template <int DT, int CHUNKS>
+template <int DT, int CHUNKS, bool FUSED>
 int x2_by_rot(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
   switch (rc) {
-    case RC_NONE: return launch_x2<DT, ROT_NONE, 1, CHUNKS>(p, nchunks, s);
-    case RC_REG16: return launch_x2<DT, ROT_REGULAR, 1, CHUNKS>(p, nchunks, s);
-    case RC_REG64: return launch_x2<DT, ROT_REGULAR, 4, CHUNKS>(p, nchunks, s);
-    case RC_REG256: return launch_x2<DT, ROT_REGULAR, 16, CHUNKS>(p, nchunks, s);
-    case RC_SYL32: return launch_x2<DT, ROT_SYLVESTER, 2, CHUNKS>(p, nchunks, s);
-    case RC_SYL128: return launch_x2<DT, ROT_SYLVESTER, 8, CHUNKS>(p, nchunks, s);
+    case RC_NONE: return launch_x2<DT, ROT_NONE, 1, CHUNKS, FUSED>(p, nchunks, s);
+    case RC_REG16: return launch_x2<DT, ROT_REGULAR, 1, CHUNKS, FUSED>(p, nchunks, s);
+    case RC_REG64: return launch_x2<DT, ROT_REGULAR, 4, CHUNKS, FUSED>(p, nchunks, s);
+    case RC_REG256: return launch_x2<DT, ROT_REGULAR, 16, CHUNKS, FUSED>(p, nchunks, s);
+    case RC_SYL32: return launch_x2<DT, ROT_SYLVESTER, 2, CHUNKS, FUSED>(p, nchunks, s);
+    case RC_SYL128: return launch_x2<DT, ROT_SYLVESTER, 8, CHUNKS, FUSED>(p, nchunks, s);
     default: return fail(QLIN_ERR_UNSUPPORTED, "unsupported rotation");
   }
 }
 
 // Chunks per thread: per-row work is amortised over more elements for long
 // rows, while short rows keep a full warp per row.
-template <int DT>
+template <int DT, bool FUSED = false>
 int x2_by_chunks(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t s) {
   if constexpr (DT != DT_F32) {  // float32 rows would need twice the prefetch registers
-    if (nchunks >= 512) return x2_by_rot<DT, 4>(rc, p, nchunks, s);
+    if (nchunks >= 512) return x2_by_rot<DT, 4, FUSED>(rc, p, nchunks, s);
   }
-  if (nchunks >= 64) return x2_by_rot<DT, 2>(rc, p, nchunks, s);
-  return x2_by_rot<DT, 1>(rc, p, nchunks, s);
+  if (nchunks >= 64) return x2_by_rot<DT, 2, FUSED>(rc, p, nchunks, s);
+  return x2_by_rot<DT, 1, FUSED>(rc, p, nchunks, s);
 }
 
 }  // namespace
@@ -199,7 +199,7 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
                     float clamp_min, const float* in_scale, int in_scale_per_row, int8_t* q, float* scale,
                     void* out, uint64_t seed, cudaStream_t stream) {
   if (M == 0 || K == 0) return QLIN_OK;
-  RowQuantParams p;
+  RowQuantParams p{};
   p.x = x;
   p.ldx = ldx;
   p.M = (int)M;
@@ -257,6 +257,41 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
     default: break;
   }
   return fail(QLIN_ERR_UNSUPPORTED, "unsupported input/compute dtype pair");
+}
+
+// Per-token int8 quantisation with the row norm / modulation prologue
+// (16-bit inputs, K % 16 == 0, 16-byte aligned rows and vectors: checked by
+// the caller).
+int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
+                          int64_t K, const FusedPrologue& f, int8_t* q, float* scale, cudaStream_t stream) {
+  if (M == 0 || K == 0) return QLIN_OK;
+  RowQuantParams p{};
+  p.x = x;
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.K = (int)K;
+  p.rot_c = rot_c;
+  p.q = q;
+  p.scale = scale;
+  p.one = 1.0f;
+  p.norm_kind = f.norm_kind;
+  p.eps = f.eps;
+  p.norm_w = f.norm_w;
+  p.mod_mul = f.mod_mul;
+  p.mul_ld = f.mul_ld;
+  p.mod_add = f.mod_add;
+  p.add_ld = f.add_ld;
+  p.rows_per_sample = f.rows_per_sample > 0 ? f.rows_per_sample : M;
+  const RotCode rc = rot_code(rot_kind, rot_kind == 0 ? 0 : rot_group);
+  if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
+  const int64_t nchunks = K / 16;
+  if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  int r = QLIN_ERR_UNSUPPORTED;
+  if (dt == DT_BF16) r = x2_by_chunks<DT_BF16, true>(rc, p, (int)nchunks, stream);
+  else if (dt == DT_F16) r = x2_by_chunks<DT_F16, true>(rc, p, (int)nchunks, stream);
+  else return fail(QLIN_ERR_UNSUPPORTED, "the fused norm prologue takes bf16 or f16 input");
+  if (r == QLIN_ERR_UNSUPPORTED) return fail(QLIN_ERR_UNSUPPORTED, "row too long for the fused norm prologue");
+  return r;
 }
 
 // Error word of the row kernels: read and clear (bit 1: a bulk-copy wait

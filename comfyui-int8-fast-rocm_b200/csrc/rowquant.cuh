@@ -43,6 +43,23 @@ struct RowQuantParams {
                          // or packed int4 codes [M, K/2] for the int4 modes
   uint64_t seed;         // MODE_REQUANT_SR
   float one;             // 1.0f, unknown to the compiler (see rowquant_pair_kernel)
+  // fused prologue of rowquant_x2_kernel<..., FUSED = true> (input dtype):
+  //   y = dt(norm(x)); y = dt(y * mod_mul[s, k]); y = dt(y + mod_add[s, k])
+  // with s = row / rows_per_sample; then rotation and quantisation of y
+  int norm_kind;         // NORM_NONE / NORM_LAYER / NORM_RMS
+  float eps;
+  const void* norm_w;    // NORM_RMS weight [K] or null
+  const void* mod_mul;   // [S, mul_ld] or null
+  int64_t mul_ld;
+  const void* mod_add;   // [S, add_ld] or null
+  int64_t add_ld;
+  int64_t rows_per_sample;
+};
+
+enum : int {
+  NORM_NONE = 0,
+  NORM_LAYER = 1,  // (x - mean) * rsqrt(var + eps), no affine (F.layer_norm without weight)
+  NORM_RMS = 2,    // (x * rsqrt(mean(x^2) + eps)) * weight, rounded once (F.rms_norm)
 };
 
 // Swizzled float index inside a warp's 512-float staging buffer.  XORs the
@@ -545,6 +562,42 @@ __device__ __forceinline__ bool rq_wait_bounded(uint64_t* bar, uint32_t parity) 
   }
 }
 
+// Round both halves to the dtype DT (RN-even) and widen back to float.
+template <int DT>
+__device__ __forceinline__ float2 round2(float2 v) {
+  if constexpr (DT == DT_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+  } else if constexpr (DT == DT_F16) {
+    return __half22float2(__floats2half2_rn(v.x, v.y));
+  } else {
+    return v;
+  }
+}
+
+// 16 elements [16*ci, 16*ci + 16) of a DT vector (16-byte aligned), as pairs.
+template <int DT>
+__device__ __forceinline__ void load_chunk2(const void* base, int ci, float2 (&v)[8]) {
+  RawChunk<DT> raw;
+  load_raw<DT>(base, (int64_t)ci * 16, raw);
+  unpack_raw2<DT>(raw, v);
+}
+
+// Sum of one value per thread over the tpr threads of a row, in a fixed
+// order (shuffle tree, then the row's warps in index order); one CTA
+// barrier.  buf: [32 rows][17] floats, not touched again before the next
+// barrier of the caller.
+__device__ __forceinline__ float row_sum(float x, float (*buf)[17], int lane, int warp_in_row, int nw) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, o));
+  if (lane == 0) buf[threadIdx.y][warp_in_row] = x;
+  __syncthreads();
+  float t = buf[threadIdx.y][0];
+  for (int w = 1; w < nw; ++w) t = __fadd_rn(t, buf[threadIdx.y][w]);
+  return t;
+}
+
 // Per-token int8 quantisation of activations (optionally ConvRot-rotated).
 // Rows stream through a ring of `stages` shared-memory slots filled by 1-D
 // bulk copies (one thread issues them, completion counted on an mbarrier per
@@ -558,7 +611,11 @@ __device__ __forceinline__ bool rq_wait_bounded(uint64_t* bar, uint32_t parity) 
 //
 // Dynamic shared memory: [stages x slot_bytes ring][warps x 512 floats
 // transpose buffers (rotations with R > 1)][stages mbarriers].
-template <int DT, int KIND, int R, int CHUNKS>
+//
+// FUSED: the row norm and the modulation of a DiT block run on the row in
+// registers before the rotation (two extra CTA barriers per row for the
+// layer norm's mean and variance, one for the RMS norm).
+template <int DT, int KIND, int R, int CHUNKS, bool FUSED = false>
 __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int stages, int slot_bytes) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float red[2][32][33];
@@ -648,6 +705,80 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = make_float2(0.0f, 0.0f);
+      }
+    }
+
+    if constexpr (FUSED) {
+      // ---- row norm + modulation, in the input dtype's rounding steps ----
+      __shared__ float nred[2][32][17];
+      const int nw = tpr >> 5;
+      if (p.norm_kind != NORM_NONE) {
+        const bool layer = p.norm_kind == NORM_LAYER;
+        float2 a2 = make_float2(0.0f, 0.0f);  // padding chunks hold zeros
+#pragma unroll
+        for (int i = 0; i < CHUNKS; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a2 = layer ? f2_add(a2, v[i][j]) : f2_fma(v[i][j], v[i][j], a2);
+        const float m1 = __fdiv_rn(row_sum(__fadd_rn(a2.x, a2.y), nred[0], lane, warp_in_row, nw), (float)p.K);
+        if (layer) {
+          const float2 mean2 = make_float2(m1, m1);
+          float2 b2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int i = 0; i < CHUNKS; ++i) {
+            if (t + i * tpr >= nchunks) continue;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float2 d = f2_sub(v[i][j], mean2);
+              b2 = f2_fma(d, d, b2);
+            }
+          }
+          const float var = __fdiv_rn(row_sum(__fadd_rn(b2.x, b2.y), nred[1], lane, warp_in_row, nw), (float)p.K);
+          const float rstd = __frsqrt_rn(__fadd_rn(var, p.eps));
+          const float2 r2 = make_float2(rstd, rstd);
+#pragma unroll
+          for (int i = 0; i < CHUNKS; ++i) {
+            const bool pad = t + i * tpr >= nchunks;  // padding chunks stay zero (absmax)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              v[i][j] = pad ? make_float2(0.0f, 0.0f) : round2<DT>(f2_mul(f2_sub(v[i][j], mean2), r2));
+          }
+        } else {
+          // dt((x * rstd) * w): one rounding, as torch's rms_norm
+          const float rstd = __frsqrt_rn(__fadd_rn(m1, p.eps));
+          const float2 r2 = make_float2(rstd, rstd);
+#pragma unroll
+          for (int i = 0; i < CHUNKS; ++i) {
+            const int ci = t + i * tpr;
+            if (p.norm_w != nullptr && ci < nchunks) {
+              float2 w[8];
+              load_chunk2<DT>(p.norm_w, ci, w);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i][j] = round2<DT>(f2_mul(f2_mul(v[i][j], r2), w[j]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i][j] = round2<DT>(f2_mul(v[i][j], r2));
+            }
+          }
+        }
+      }
+      if (row_ok && (p.mod_mul != nullptr || p.mod_add != nullptr)) {
+        const int64_t smp = row / p.rows_per_sample;
+#pragma unroll
+        for (int i = 0; i < CHUNKS; ++i) {
+          const int ci = t + i * tpr;
+          if (ci >= nchunks) continue;
+          float2 w[8];
+          if (p.mod_mul != nullptr) {
+            load_chunk2<DT>(reinterpret_cast<const uint8_t*>(p.mod_mul) + smp * p.mul_ld * EB, ci, w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = round2<DT>(f2_mul(v[i][j], w[j]));
+          }
+          if (p.mod_add != nullptr) {
+            load_chunk2<DT>(reinterpret_cast<const uint8_t*>(p.mod_add) + smp * p.add_ld * EB, ci, w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = round2<DT>(f2_add(v[i][j], w[j]));
+          }
+        }
       }
     }
 

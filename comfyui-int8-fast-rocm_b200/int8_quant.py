@@ -95,6 +95,37 @@ def int8_forward_dynamic_per_row(x: Tensor, weight: Tensor, weight_scale: Tensor
     return ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=True)
 
 
+@torch.no_grad()
+def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dtype, rot=None, per_row=True, *,
+                       norm=None, eps: float = 1e-6, norm_weight=None, mod_mul=None, mod_add=None,
+                       rows_per_sample=None, gelu_from=None, residual=None, gate=None,
+                       rows_per_gate=None) -> Tensor:
+    """:func:`int8_forward_dynamic_per_row` / :func:`int8_forward_dynamic`
+    with the element-wise neighbours of a DiT block's linear fused into its
+    two kernels (no counterpart in the reference, which runs them as eager
+    ops around ``Int8TensorwiseOps.Linear``):
+
+    * prologue (activation quantiser): ``dt(norm(x))`` (``norm`` "layer" or
+      "rms" with ``norm_weight``), ``dt(. * mod_mul[s])``, ``dt(. +
+      mod_add[s])`` with ``s = row // rows_per_sample`` -- a Flux block's
+      ``layer_norm(x) * (1 + scale) + shift`` is ``norm="layer",
+      mod_mul=1 + scale, mod_add=shift``;
+    * epilogue (GEMM): ``dt(gelu_tanh(y))`` on columns ``>= gelu_from``, then
+      ``dt(residual + dt(gate[g] * y))`` with ``g = row // rows_per_gate``.
+    """
+    prologue = norm is not None or mod_mul is not None or mod_add is not None
+    if prologue:
+        xq, xs = ops.quant_act_int8_norm(x, rot, norm, eps, norm_weight, mod_mul, mod_add, rows_per_sample)
+    else:
+        xq, xs = ops.quant_act_int8(x, rot)
+    if not per_row and not isinstance(weight_scale, torch.Tensor):
+        weight_scale = torch.tensor([float(weight_scale)], dtype=torch.float32, device=x.device)
+    if gelu_from is None and residual is None:
+        return ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row)
+    return ops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row,
+                               gelu_from=gelu_from, residual=residual, gate=gate, rows_per_gate=rows_per_gate)
+
+
 def lowvram_patch_int8(weight: Tensor, scale, convrot_groupsize, delta_fn, stochastic=False, seed=0) -> Tensor:
     """INT8LowVramPatch.__call__ / bake-in path (int8_quant.py:809-843,
     881-941) on the kernels: dequant (+ un-rotate) -> ``delta_fn`` (the

@@ -97,6 +97,70 @@ def quant_act_int8(x: torch.Tensor, rot=None):
     return q, s
 
 
+_NORM = {None: N.NORM_NONE, "none": N.NORM_NONE, "layer": N.NORM_LAYER, "layer_norm": N.NORM_LAYER,
+         "rms": N.NORM_RMS, "rms_norm": N.NORM_RMS}
+
+
+def _vec_rows(v: torch.Tensor, K: int, dtype: torch.dtype, device):
+    """A per-sample parameter ([K] or [S, K], unit inner stride) as
+    (tensor, row stride); copies only when the layout does not fit."""
+    if v.dim() == 1:
+        v = v.reshape(1, -1)
+    if v.dim() != 2 or v.shape[1] != K:
+        raise ValueError(f"expected a [K] or [S, K] tensor with K={K}, got shape {tuple(v.shape)}")
+    if v.dtype != dtype or v.device != device:
+        v = v.to(device=device, dtype=dtype)
+    fits = v.stride(1) == 1 and v.data_ptr() % 16 == 0 and (v.stride(0) * v.element_size()) % 16 == 0 and \
+        (v.shape[0] == 1 or v.stride(0) >= K)
+    if not fits:
+        v = _aligned(v)
+    return v, (v.stride(0) if v.shape[0] > 1 else K)
+
+
+def quant_act_int8_norm(x: torch.Tensor, rot=None, norm=None, eps: float = 1e-6, norm_weight=None, mod_mul=None,
+                        mod_add=None, rows_per_sample=None):
+    """Per-token int8 of a DiT block's normalised, modulated activation:
+    ``y = dt(norm(x))``, ``y = dt(y * mod_mul[s])``, ``y = dt(y + mod_add[s])``
+    (sample ``s = row // rows_per_sample``), then the rotation and the
+    quantisation of :func:`quant_act_int8`, in one pass over ``x``.
+
+    ``norm``: None, ``"layer"`` (F.layer_norm without affine) or ``"rms"``
+    (F.rms_norm with ``norm_weight``); ``mod_mul`` / ``mod_add``: ``[K]`` or
+    ``[S, K]`` in x.dtype (bf16 / f16).  Returns (q int8 [M,K], scale [M,1])."""
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"the fused norm prologue takes bfloat16 or float16 input, got {x.dtype}")
+    if norm not in _NORM:
+        raise ValueError(f"norm must be one of {sorted(k for k in _NORM if k)} or None, got {norm!r}")
+    x, ldx = _rows(x)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    if M == 0 or K == 0:
+        return q, s
+    st = _stream(x)
+    if x.data_ptr() % 16:
+        x, ldx = x.clone(), K
+    kind, g, c = _rot_args(rot, x.dtype)
+    w = None
+    if norm_weight is not None:
+        w, _ = _vec_rows(norm_weight.reshape(-1), K, x.dtype, x.device)
+    mm = ma = None
+    mul_ld = add_ld = K
+    if mod_mul is not None:
+        mm, mul_ld = _vec_rows(mod_mul, K, x.dtype, x.device)
+    if mod_add is not None:
+        ma, add_ld = _vec_rows(mod_add, K, x.dtype, x.device)
+    S = max([t.shape[0] for t in (mm, ma) if t is not None] or [1])
+    rps = int(rows_per_sample) if rows_per_sample is not None else (M // S if S > 1 else M)
+    if rows_per_sample is None and S > 1 and rps * S != M:
+        raise ValueError(f"{M} rows do not split into {S} samples")
+    if rps <= 0 or -(-M // rps) > S:  # every row's sample must have a modulation row
+        raise ValueError(f"rows_per_sample={rps} needs {-(-M // max(rps, 1))} modulation rows, got {S}")
+    N.call("qlin_quant_act_int8_norm", x.data_ptr(), dtype_code(x.dtype), M, K, ldx, _NORM[norm], float(eps),
+           _ptr(w), _ptr(mm), mul_ld, _ptr(ma), add_ld, rps, kind, g, c, q.data_ptr(), s.data_ptr(), st)
+    return q, s
+
+
 def quant_act_int4(x: torch.Tensor, rot=None, group: int = 0):
     """Signed int4-range codes in int8 storage: (q [M,K], scale float32
     [M] (group 0) or [M, K/128] (group 128))."""
@@ -193,6 +257,56 @@ def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, p
     N.call("qlin_gemm_w8a8", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
            N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
            M, Nn, K, st)
+    return out
+
+
+def gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, per_row=True, gelu_from=None,
+                    residual=None, gate=None, rows_per_gate=None):
+    """:func:`gemm_w8a8` with a DiT block's element-wise steps in the
+    epilogue: ``y = dt(gelu_tanh(y))`` for output columns ``>= gelu_from``,
+    then ``y = dt(residual + dt(gate[g] * y))`` (``dt(residual + y)`` without
+    ``gate``), gate row ``g = row // rows_per_gate``.  ``residual`` [M, N],
+    ``gate`` [N] or [G, N], both cast to ``out_dtype`` (bf16 / f16)."""
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"the fused epilogue writes bfloat16 or float16, got {out_dtype}")
+    _check_gemm(a_q, w_q)
+    a_q, w_q = _pad_k(_aligned(a_q), _aligned(w_q), 16)
+    M, K = a_q.shape
+    Nn = w_q.shape[0]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
+    if M == 0 or Nn == 0:
+        return out
+    a_scale = a_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    w_scale = w_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    if per_row and w_scale.numel() != Nn:
+        raise ValueError(f"per-row weight scale must have {Nn} entries, got {w_scale.numel()}")
+    if not per_row and w_scale.numel() != 1:
+        raise ValueError("tensorwise weight scale must be a scalar")
+    if bias is not None:
+        bias = bias.reshape(-1).to(device=a_q.device, dtype=out_dtype).contiguous()
+    gelu_col0 = Nn if gelu_from is None else max(0, int(gelu_from))
+    ld_res = gate_ld = Nn
+    rpg = M
+    if residual is not None:
+        if tuple(residual.shape) != (M, Nn):
+            raise ValueError(f"residual must be [{M}, {Nn}], got {tuple(residual.shape)}")
+        residual, ld_res = _vec_rows(residual, Nn, out_dtype, a_q.device)
+        if residual.shape[0] == 1:
+            ld_res = Nn
+    if gate is not None:
+        if residual is None:
+            raise ValueError("a gate needs a residual")
+        gate, gate_ld = _vec_rows(gate, Nn, out_dtype, a_q.device)
+        G = gate.shape[0]
+        rpg = int(rows_per_gate) if rows_per_gate is not None else M // G
+        if rows_per_gate is None and rpg * G != M:
+            raise ValueError(f"{M} rows do not split into {G} gate rows")
+        if rpg <= 0 or -(-M // rpg) > G:  # every row's gate row must exist
+            raise ValueError(f"rows_per_gate={rpg} needs {-(-M // max(rpg, 1))} gate rows, got {G}")
+    st = _stream(a_q)
+    N.call("qlin_gemm_w8a8_fused", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
+           N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
+           M, Nn, K, gelu_col0, _ptr(residual), ld_res, _ptr(gate), gate_ld, rpg, st)
     return out
 
 

@@ -58,6 +58,11 @@ extern "C" {
 #define QLIN_WSCALE_TENSOR 0 /* one float: int8_quant.py:113-133 order (ws*xs) */
 #define QLIN_WSCALE_ROW 1    /* float[N]:  int8_quant.py:137-164 order (xs then ws) */
 
+/* row norms of the fused activation prologue */
+#define QLIN_NORM_NONE 0
+#define QLIN_NORM_LAYER 1  /* (x - mean) * rsqrt(var + eps), no affine: F.layer_norm(x, (K,), eps=eps) */
+#define QLIN_NORM_RMS 2    /* dt((x * rsqrt(mean(x^2) + eps)) * weight): F.rms_norm(x, (K,), weight, eps) */
+
 /* rounding modes for weight requantisation */
 #define QLIN_ROUND_NEAREST 0    /* quantize_int8 (int8_quant.py:41-42)             */
 #define QLIN_ROUND_STOCHASTIC 1 /* stochastic_round_int8_delta (int8_quant.py:80-106) */
@@ -86,6 +91,29 @@ QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits);
 QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                                  int rot_kind, int rot_group, float rot_c,
                                  int8_t* q, float* scale, void* stream);
+
+/* qlin_quant_act_int8 preceded by a DiT block's row norm and modulation,
+ * each step rounded to x_dtype as the eager PyTorch sequence rounds it:
+ *   y = dt(norm(x))                          norm_kind QLIN_NORM_* (float32 row statistics,
+ *                                            rsqrt correctly rounded), norm_weight [K] or NULL
+ *   y = dt(y * mod_mul[s, :])                if mod_mul (e.g. 1 + scale of a Flux modulation)
+ *   y = dt(y + mod_add[s, :])                if mod_add (the shift)
+ * with s = row / rows_per_sample (rows_per_sample <= 0: one sample),
+ * mod_mul rows mul_ld and mod_add rows add_ld elements apart (rows
+ * 0 .. (M-1)/rows_per_sample must exist); then the optional rotation and the
+ * per-token int8 quantisation of qlin_quant_act_int8 on y.
+ * x_dtype BF16 or F16; K % 16 == 0 (K <= 32768); x rows, q, norm_weight and
+ * every mod_* row 16-byte aligned.
+ * Replaces the eager prologue of the quantised linear: the kitchen
+ * input_act RMS norm (rocm_int8_kitchen_patch.py:136) and a DiT block's
+ * LayerNorm + (1 + scale) * x + shift in front of Int8TensorwiseOps.Linear
+ * (int8_quant.py:633-716); the rows' statistics are summed in float32 in a
+ * fixed order, which the eager kernels do in their own order. */
+QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                                      int norm_kind, float eps, const void* norm_weight,
+                                      const void* mod_mul, int64_t mul_ld, const void* mod_add,
+                                      int64_t add_ld, int64_t rows_per_sample, int rot_kind, int rot_group, float rot_c,
+                                      int8_t* q, float* scale, void* stream);
 
 /* Signed int4-range quantisation (codes in [-7,7], one per int8 byte) with
  * the int4_quant.py conventions computed in x_dtype: absmax clamped at
@@ -123,6 +151,24 @@ QLIN_API int qlin_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t
 QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                             int wscale_mode, const void* bias, void* out, int out_dtype,
                             int64_t M, int64_t N, int64_t K, void* stream);
+
+/* qlin_gemm_w8a8 followed, inside the epilogue, by the element-wise steps
+ * that follow a DiT block's linears (out_dtype BF16 or F16; y = the
+ * qlin_gemm_w8a8 value, already rounded to out_dtype):
+ *   y = dt(gelu_tanh(y))                       columns >= gelu_col0 (gelu_col0 >= N: none)
+ *   y = dt(residual + dt(gate[g, n] * y))      if residual; without gate dt(residual + y)
+ * with g = row / rows_per_gate (<= 0: one gate row; gate rows
+ * 0 .. (M-1)/rows_per_gate must exist), residual [M, ld_res] and gate rows
+ * gate_ld elements apart, both in out_dtype, 16-byte aligned rows.  gelu_tanh is F.gelu(approximate="tanh") as PyTorch's CUDA kernel
+ * evaluates it in float32 (inner sum as one FMA, CUDA tanhf).
+ * Replaces: the kitchen residual form residual + residual_scale * linear(x)
+ * (rocm_int8_kitchen_patch.py:176) and a DiT block's gated residual
+ * x + gate * linear(h) / GELU after Int8TensorwiseOps.Linear. */
+QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                  int wscale_mode, const void* bias, void* out, int out_dtype,
+                                  int64_t M, int64_t N, int64_t K, int64_t gelu_col0,
+                                  const void* residual, int64_t ld_res, const void* gate, int64_t gate_ld,
+                                  int64_t rows_per_gate, void* stream);
 
 /* Tensor-parallel W8A8 linear fused with its all-gather: this rank's column
  * shard, out[:, col_off : col_off + N_shard] = the qlin_gemm_w8a8 result for

@@ -519,3 +519,108 @@ def rotate_requant_int8(w, scale, group=0, kind="regular"):
     s = np.asarray(scale, F32)
     s = s.reshape(-1, 1) if s.size > 1 else s.reshape(())
     return quantize_int8(w, s)
+
+
+# ---------------------------------------------------------------------------
+# Neighbours of the linear in a DiT block -- the eager PyTorch sequence that
+# the fused prologue / epilogue replace (kitchen input_act and residual form,
+# rocm_int8_kitchen_patch.py:136, 176; a Flux block's LayerNorm + modulation
+# in front of Int8TensorwiseOps.Linear, int8_quant.py:633-716, and its gated
+# residual / GELU behind it).  RESTATEMENT of torch's element-wise rounding:
+# every eager op rounds to the activation dtype.  Row statistics are summed in
+# float64 and rounded once, so they are exact whenever the float32 sums are
+# (the kernels sum in float32 in their own fixed order; eager torch in its
+# own) -- tests use exactly summable rows for bit parity and a tolerance
+# elsewhere.
+# ---------------------------------------------------------------------------
+
+GELU_BETA = F32(0.7978845608028654)  # sqrt(2 / pi)
+GELU_KAPPA = F32(0.044715)
+
+
+def rsqrt_rn(v: np.ndarray) -> np.ndarray:
+    """float32 1/sqrt(v) (float64 evaluation, one rounding to float32)."""
+    return (1.0 / np.sqrt(np.asarray(v, np.float64))).astype(F32)
+
+
+def row_norm(x: np.ndarray, kind: str, eps: float, dtype: str, weight=None) -> np.ndarray:
+    """``F.layer_norm(x, (K,), eps=eps)`` (no affine; kind "layer") or
+    ``F.rms_norm(x, (K,), weight, eps)`` (kind "rms": ``dt((x * rstd) *
+    weight)``, one rounding) on rows of ``dtype`` values."""
+    x = np.asarray(x, F32)
+    K = F32(x.shape[-1])
+    e = F32(eps)
+    if kind == "layer":
+        mean = (x.astype(np.float64).sum(-1, keepdims=True).astype(F32) / K).astype(F32)
+        d = (x - mean).astype(F32)
+        var = ((d.astype(np.float64) ** 2).sum(-1, keepdims=True).astype(F32) / K).astype(F32)
+        rstd = rsqrt_rn((var + e).astype(F32))
+        return rnd(dtype, d * rstd)
+    if kind == "rms":
+        ms = ((x.astype(np.float64) ** 2).sum(-1, keepdims=True).astype(F32) / K).astype(F32)
+        rstd = rsqrt_rn((ms + e).astype(F32))
+        y = (x * rstd).astype(F32)
+        if weight is not None:
+            y = (y * np.asarray(weight, F32)).astype(F32)
+        return rnd(dtype, y)
+    raise ValueError(kind)
+
+
+def _per_sample(v, M: int, rows_per: int) -> np.ndarray:
+    """[S, N] (or [N]) per-sample rows broadcast to the M rows of x."""
+    v = np.asarray(v, F32)
+    if v.ndim == 1:
+        v = v[None, :]
+    return v[np.arange(M) // rows_per]
+
+
+def norm_modulate(x, dtype: str, norm=None, eps: float = 1e-6, weight=None, mod_mul=None, mod_add=None,
+                  rows_per_sample=None) -> np.ndarray:
+    """``dt(norm(x))``, ``dt(. * mod_mul[s])``, ``dt(. + mod_add[s])`` (a Flux
+    block's ``layer_norm(x) * (1 + scale) + shift`` with ``mod_mul = dt(1 +
+    scale)``), sample ``s = row // rows_per_sample``."""
+    y = np.asarray(x, F32)
+    M = y.shape[0]
+    rps = rows_per_sample or M
+    if norm is not None:
+        y = row_norm(y, norm, eps, dtype, weight)
+    if mod_mul is not None:
+        y = rnd(dtype, y * _per_sample(mod_mul, M, rps))
+    if mod_add is not None:
+        y = rnd(dtype, y + _per_sample(mod_add, M, rps))
+    return y
+
+
+def norm_quant_int8(x, dtype: str, rot=None, **kw):
+    """Fused prologue + per-token int8: (q, scale[M, 1])."""
+    y = norm_modulate(x, dtype, **kw)
+    if rot is not None:
+        y = rotate(y, rot[1], rot[0], dtype)
+    return quantize_int8_axiswise(y, dim=-1)
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    """float32 ``0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))`` in the
+    expression order of ``F.gelu(approximate="tanh")`` on CUDA (inner sum as
+    one fused multiply-add).  numpy's tanh is not CUDA's: near ``1 + tanh ->
+    0`` a 1-ulp difference of tanh shows in the bf16 result (about 0.5% of
+    values differ by 1 ulp from either torch kernel)."""
+    x = np.asarray(x, F32)
+    x3 = ((x * x).astype(F32) * x).astype(F32)
+    fma = (GELU_KAPPA.astype(np.float64) * x3 + x).astype(F32)
+    inner = (GELU_BETA * fma).astype(F32)
+    return ((F32(0.5) * x).astype(F32) * (F32(1.0) + np.tanh(inner).astype(F32)).astype(F32)).astype(F32)
+
+
+def linear_post(y, dtype: str, gelu_from=None, residual=None, gate=None, rows_per_gate=None) -> np.ndarray:
+    """The element-wise steps after a quantised linear's output ``y`` (dtype
+    values): ``dt(gelu_tanh(y))`` on columns ``>= gelu_from``, then
+    ``dt(residual + dt(gate[g] * y))`` (or ``dt(residual + y)``)."""
+    y = np.array(y, F32)
+    M = y.shape[0]
+    if gelu_from is not None:
+        y[:, gelu_from:] = rnd(dtype, gelu_tanh(y[:, gelu_from:]))
+    if residual is not None:
+        t = y if gate is None else rnd(dtype, _per_sample(gate, M, rows_per_gate or M) * y)
+        y = rnd(dtype, np.asarray(residual, F32) + t)
+    return y

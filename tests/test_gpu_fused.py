@@ -1,0 +1,315 @@
+"""Parity of the fused DiT-step neighbours of the quantised linear (through
+the C-ABI): the row norm + modulation prologue of the int8 activation
+quantiser and the GELU / gated-residual epilogue of the W8A8 GEMM.
+
+Bit parity with the oracle wherever the float32 arithmetic is fully
+determined: rows whose statistics sum exactly in float32 (then the kernel's
+summation order cannot matter) and the residual / gate steps.  Elsewhere the
+tolerance is stated per test: the row statistics are summed in a different
+(fixed) order than the oracle's float64 sums, and the oracle's numpy tanh is
+not CUDA's tanhf, so a dtype rounding can flip by one unit.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import cuda_ok
+from oracle import qlinear_oracle as O
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+TDT = {"bf16": torch.bfloat16, "f16": torch.float16}
+
+
+@pytest.fixture(scope="module")
+def P(pkg):
+    return pkg
+
+
+def dev(a, dt=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dt is not None:
+        t = t.to(TDT[dt])
+    return t.cuda()
+
+
+def exact_rows(rng, M, K, dt, with_mean):
+    """Rows of multiples of 1/8 in [-4, 4] whose sum is K*c exactly (c a
+    multiple of 1/8, or 0): every float32 partial sum of the row, of
+    (x - mean)^2 and of x^2 is exact, so the statistics do not depend on the
+    summation order."""
+    half = rng.integers(-24, 25, size=(M, K // 2)).astype(np.float32) / 8
+    v = np.concatenate([half, -half], axis=1)
+    v = np.take_along_axis(v, rng.permuted(np.tile(np.arange(K), (M, 1)), axis=1), axis=1)
+    if with_mean:
+        v = v + (rng.integers(-4, 5, size=(M, 1)).astype(np.float32) / 8)
+    return O.rnd(dt, v)
+
+
+def rnd_vec(rng, shape, dt, scale=1.0, offset=0.0):
+    return O.rnd(dt, rng.standard_normal(shape).astype(np.float32) * scale + offset)
+
+
+ROTS = [None, ("regular", 256), ("sylvester", 128)]
+
+
+# ---------------------------------------------------------------------------
+# prologue: norm + modulation + (rotation) + per-token int8
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("norm", ["layer", "rms"])
+@pytest.mark.parametrize("rot", ROTS)
+@pytest.mark.parametrize("M,K,S", [(37, 256, 1), (96, 3072, 3), (8, 4096, 2), (5, 1024, 5)])
+def test_norm_quant_exact_rows(P, dt, norm, rot, M, K, S):
+    rng = np.random.default_rng(M * 7 + K + S)
+    x = exact_rows(rng, M, K, dt, with_mean=norm == "layer")
+    w = rnd_vec(rng, K, dt, 0.5, 1.0) if norm == "rms" else None
+    mul = O.rnd(dt, 1.0 + rnd_vec(rng, (S, K), dt, 0.3))
+    add = rnd_vec(rng, (S, K), dt, 0.2)
+    kw = dict(norm=norm, eps=1e-6, weight=w, mod_mul=mul, mod_add=add, rows_per_sample=M // S)
+    q_ref, s_ref = O.norm_quant_int8(x, dt, rot, **kw)
+    q, s = P.ops.quant_act_int8_norm(dev(x, dt), rot, norm=norm, eps=1e-6,
+                                     norm_weight=None if w is None else dev(w, dt),
+                                     mod_mul=dev(mul, dt), mod_add=dev(add, dt), rows_per_sample=M // S)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), s_ref.astype(np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("rot", [None, ("sylvester", 128)])
+def test_norm_only_and_mod_only(P, dt, rot):
+    """Each step on its own: norm without modulation, modulation without
+    norm (multiply only, add only), single sample."""
+    rng = np.random.default_rng(3)
+    M, K = 64, 1024
+    x = exact_rows(rng, M, K, dt, with_mean=True)
+    mul = O.rnd(dt, 1.0 + rnd_vec(rng, K, dt, 0.3))
+    add = rnd_vec(rng, K, dt, 0.2)
+    cases = [dict(norm="layer"), dict(norm="rms"), dict(mod_mul=mul), dict(mod_add=add),
+             dict(mod_mul=mul, mod_add=add)]
+    for kw in cases:
+        q_ref, s_ref = O.norm_quant_int8(x, dt, rot, **kw)
+        args = {k: (dev(v, dt) if isinstance(v, np.ndarray) else v) for k, v in kw.items()}
+        q, s = P.ops.quant_act_int8_norm(dev(x, dt), rot, **args)
+        np.testing.assert_array_equal(q.cpu().numpy(), q_ref, err_msg=str(list(kw)))
+        np.testing.assert_array_equal(s.cpu().numpy(), s_ref, err_msg=str(list(kw)))
+
+
+def _code_tolerance(q, q_ref, s, s_ref, max_frac):
+    """Scales within one bf16 unit (the row absmax can move by one dtype
+    unit); codes within one unit in rows with equal scales and within two
+    where the scale moved (the code of an element that itself moved by one
+    dtype unit is then also rescaled); at most ``max_frac`` codes differ."""
+    np.testing.assert_allclose(s, s_ref, rtol=2.0 ** -7, atol=0)
+    d = np.abs(q.astype(np.int32) - q_ref.astype(np.int32))
+    same = (s.reshape(-1) == s_ref.reshape(-1))
+    assert d[same].max(initial=0) <= 1
+    assert d[~same].max(initial=0) <= 2
+    assert d.astype(bool).mean() <= max_frac, d.astype(bool).mean()
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("norm", ["layer", "rms"])
+def test_norm_quant_dit_rows(P, dt, norm):
+    """DiT-like activations (hidden 3072, two samples of 4608 tokens, Flux
+    modulation) against the oracle and against the eager CUDA sequence the
+    fused kernel replaces.  Tolerance: codes within 1 unit on <= 0.2% of
+    elements against the oracle (a one-unit flip of a normalised value from
+    the row statistics' summation order moves several rotated codes)."""
+    rng = np.random.default_rng(11)
+    S, L, K = 2, 4608, 3072
+    M = S * L
+    x = rnd_vec(rng, (M, K), dt, 1.5, 0.1)
+    scale = rnd_vec(rng, (S, K), dt, 0.3)
+    shift = rnd_vec(rng, (S, K), dt, 0.2)
+    w = rnd_vec(rng, K, dt, 0.5, 1.0) if norm == "rms" else None
+    rot = ("regular", 256)
+    xt, sc, sh = dev(x, dt), dev(scale, dt), dev(shift, dt)
+    mul_t = 1 + sc  # eager: (1 + scale) in the activation dtype
+    q, s = P.ops.quant_act_int8_norm(xt, rot, norm=norm, eps=1e-6, norm_weight=None if w is None else dev(w, dt),
+                                     mod_mul=mul_t, mod_add=sh, rows_per_sample=L)
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    q_ref, s_ref = O.norm_quant_int8(x, dt, rot, norm=norm, eps=1e-6, weight=w, mod_mul=mul_t.float().cpu().numpy(),
+                                     mod_add=shift, rows_per_sample=L)
+    _code_tolerance(q, q_ref, s, s_ref, 2e-3)
+    # the eager CUDA sequence: torch norm, broadcast modulation, then the
+    # product quantiser
+    x3 = xt.view(S, L, K)
+    if norm == "layer":
+        n = F.layer_norm(x3, (K,), eps=1e-6)
+    else:
+        n = F.rms_norm(x3, (K,), dev(w, dt), 1e-6)
+    y = (n * mul_t[:, None] + sh[:, None]).reshape(M, K)
+    qe, se = P.ops.quant_act_int8(y, rot)
+    # torch's CUDA norms use their own statistics (Welford, rsqrtf): 0.5%
+    _code_tolerance(q, qe.cpu().numpy(), s, se.cpu().numpy(), 5e-3)
+
+
+def test_norm_quant_nonfinite_and_constant_rows(P):
+    """A row holding Inf gives the quantiser's Inf/NaN row result (scale
+    non-finite, codes 0); a constant row under layer norm is all zeros
+    (scale clamps at 1e-30, codes 0), as in eager torch."""
+    rng = np.random.default_rng(5)
+    M, K = 8, 512
+    x = rnd_vec(rng, (M, K), "bf16")
+    x[2, 17] = np.inf
+    x[5, :] = 0.75
+    q, s = P.ops.quant_act_int8_norm(dev(x, "bf16"), None, norm="layer", eps=1e-6)
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    assert not np.isfinite(s[2, 0]) and (q[2] == 0).all()
+    assert s[5, 0] == np.float32(1e-30) and (q[5] == 0).all()
+    keep = [r for r in range(M) if r not in (2, 5)]
+    q_ref, s_ref = O.norm_quant_int8(x[keep], "bf16", None, norm="layer", eps=1e-6)
+    _code_tolerance(q[keep], q_ref, s[keep], s_ref, 2e-3)
+
+
+def test_norm_quant_empty_and_errors(P):
+    x = torch.zeros((0, 256), dtype=torch.bfloat16, device="cuda")
+    q, s = P.ops.quant_act_int8_norm(x, None, norm="layer")
+    assert q.shape == (0, 256) and s.shape == (0, 1)
+    x = torch.zeros((4, 256), dtype=torch.float32, device="cuda")
+    with pytest.raises(TypeError):
+        P.ops.quant_act_int8_norm(x, None, norm="layer")
+    xb = x.to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        P.ops.quant_act_int8_norm(xb, None, norm="group")
+    with pytest.raises(ValueError):
+        P.ops.quant_act_int8_norm(xb, None, mod_mul=torch.ones((3, 256), dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(P._native.NativeError):  # K % 16 != 0
+        P.ops.quant_act_int8_norm(torch.zeros((4, 200), dtype=torch.bfloat16, device="cuda"), None, norm="rms")
+
+
+# ---------------------------------------------------------------------------
+# epilogue: GELU / residual + gate after the W8A8 epilogue
+# ---------------------------------------------------------------------------
+
+
+def _gemm_case(rng, M, N, K, dt):
+    a = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    xs = (rng.random((M, 1), dtype=np.float32) * 0.02 + 1e-3).astype(np.float32)
+    ws = (rng.random(N, dtype=np.float32) * 0.002 + 1e-4).astype(np.float32)
+    b = rnd_vec(rng, N, dt, 0.5)
+    return a, w, xs, ws, b
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K,G", [(512, 768, 256, 2), (300, 200, 512, 3), (100, 256, 128, 1), (4096, 3072, 3072, 2)])
+@pytest.mark.parametrize("per_row", [True, False])
+def test_gemm_residual_gate_exact(P, dt, M, N, K, G, per_row):
+    rng = np.random.default_rng(M + N + K)
+    a, w, xs, ws, b = _gemm_case(rng, M, N, K, dt)
+    if not per_row:
+        ws = ws[:1]
+    res = rnd_vec(rng, (M, N), dt, 2.0)
+    gate = rnd_vec(rng, (G, N), dt, 0.5)
+    rpg = M // G
+    Mg = rpg * G  # rows covered by whole gate groups
+    acc = O.int_mm(a[:Mg], w)
+    ep = O.w8a8_epilogue_per_row if per_row else O.w8a8_epilogue_tensorwise
+    y_ref = ep(acc, xs[:Mg], ws if per_row else ws[0], b, dt)
+    for g in (gate, None):
+        ref = O.linear_post(y_ref, dt, residual=res[:Mg], gate=g, rows_per_gate=rpg)
+        y = P.ops.gemm_w8a8_fused(dev(a[:Mg]), dev(xs[:Mg]), dev(w), dev(ws), dev(b, dt), TDT[dt], per_row=per_row,
+                                  residual=dev(res[:Mg], dt), gate=None if g is None else dev(g, dt),
+                                  rows_per_gate=rpg)
+        np.testing.assert_array_equal(y.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K,gelu_from", [(512, 1024, 256, 0), (384, 1280, 512, 768), (64, 512, 256, 0),
+                                             (4096, 12288, 3072, 0)])
+def test_gemm_gelu(P, dt, M, N, K, gelu_from):
+    """GELU in the epilogue equals eager ``F.gelu(y, approximate="tanh")`` on
+    the GPU bit for bit (same float32 expression, CUDA tanhf); against the
+    numpy oracle one unit of the dtype (or 2^-20 absolute where tanh
+    saturates) on <= 5% of the GELU'd outputs (numpy's tanh)."""
+    rng = np.random.default_rng(N + gelu_from)
+    a, w, xs, ws, b = _gemm_case(rng, M, N, K, dt)
+    y = P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), dev(b, dt), TDT[dt], gelu_from=gelu_from)
+    plain = P.ops.gemm_w8a8(dev(a), dev(xs), dev(w), dev(ws), dev(b, dt), TDT[dt])
+    eager = plain.clone()
+    eager[:, gelu_from:] = F.gelu(plain[:, gelu_from:], approximate="tanh")
+    assert torch.equal(y, eager)
+    ref = O.linear_post(plain.float().cpu().numpy(), dt, gelu_from=gelu_from)
+    yo = y.float().cpu().numpy()
+    np.testing.assert_array_equal(yo[:, :gelu_from], ref[:, :gelu_from])
+    g, r = yo[:, gelu_from:], ref[:, gelu_from:]
+    unit = 2.0 ** -7 if dt == "bf16" else 2.0 ** -10
+    assert (np.abs(g - r) <= np.maximum(np.abs(r) * unit, 2.0 ** -20)).all()
+    assert (g != r).mean() <= 0.05
+
+
+def test_gemm_gelu_then_residual(P):
+    """Both steps: residual + gate * gelu(y) (order of the epilogue)."""
+    rng = np.random.default_rng(9)
+    M, N, K = 512, 512, 256
+    a, w, xs, ws, b = _gemm_case(rng, M, N, K, "bf16")
+    res = rnd_vec(rng, (M, N), "bf16")
+    gate = rnd_vec(rng, (2, N), "bf16", 0.5)
+    y = P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16, gelu_from=0,
+                              residual=dev(res, "bf16"), gate=dev(gate, "bf16"))
+    plain = P.ops.gemm_w8a8(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16)
+    g = dev(gate, "bf16")
+    eager = dev(res, "bf16") + torch.repeat_interleave(g, M // 2, 0) * F.gelu(plain, approximate="tanh")
+    assert torch.equal(y, eager)
+
+
+def test_gemm_fused_strided_gate_and_errors(P):
+    """A gate that is a column slice of a wider modulation output (row stride
+    6N, as a Flux block's chunk(6) views) needs no copy; bad requests raise."""
+    rng = np.random.default_rng(4)
+    M, N, K = 256, 256, 128
+    a, w, xs, ws, b = _gemm_case(rng, M, N, K, "bf16")
+    mod = dev(rnd_vec(rng, (2, 6 * N), "bf16", 0.5), "bf16")
+    gate = mod[:, 2 * N:3 * N]
+    res = dev(rnd_vec(rng, (M, N), "bf16"), "bf16")
+    y = P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16, residual=res,
+                              gate=gate)
+    plain = P.ops.gemm_w8a8(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16)
+    assert torch.equal(y, res + torch.repeat_interleave(gate, M // 2, 0) * plain)
+    with pytest.raises(ValueError):
+        P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), None, torch.bfloat16, gate=gate)
+    with pytest.raises(TypeError):
+        P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), None, torch.float32, gelu_from=0)
+    with pytest.raises(ValueError):
+        P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), None, torch.bfloat16, residual=res[:100])
+
+
+def test_dit_blocks_fused_match_unfused(P, monkeypatch):
+    """The measured DiT step with its neighbours fused (bench.py's
+    dit_forward_fused) against the same blocks with eager norm / modulation /
+    GELU / residual around the plain quantised linear, on a small config:
+    equal up to the LayerNorm statistics' order (relative L2 <= 1e-2 after
+    two double and two single blocks)."""
+    import bench
+    monkeypatch.setitem(bench.DIT, "hidden", 256)
+    monkeypatch.setitem(bench.DIT, "heads", 2)
+    monkeypatch.setitem(bench.DIT, "img", 96)
+    monkeypatch.setitem(bench.DIT, "txt", 32)
+    dev_ = torch.device("cuda", 0)
+    rot = (bench.DIT["kind"], bench.DIT["group"])
+    params = bench._dit_params(dev_, lambda w: P.ops.quant_weight_int8(w, rot), 2, 2)
+    pub = P.int8_quant
+
+    def lin(x, layer):
+        y = pub.int8_forward_dynamic_per_row(x.reshape(-1, x.shape[-1]), layer.wq, layer.ws, layer.b,
+                                             torch.bfloat16, rot)
+        return y.reshape(*x.shape[:-1], layer.n)
+
+    def fl(x, layer, residual=None, gate=None, **kw):
+        rows = x.numel() // x.shape[-1] // x.shape[0]
+        y = pub.int8_forward_fused(x.reshape(-1, x.shape[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16, rot,
+                                   rows_per_sample=rows, rows_per_gate=rows, gate=gate,
+                                   residual=None if residual is None else residual.reshape(-1, layer.n), **kw)
+        return y.reshape(*x.shape[:-1], layer.n)
+
+    img, txt, vec = bench.dit_inputs(2, dev_, 7)
+    with torch.no_grad():
+        a = bench.dit_forward_fused(params, img, txt, vec, fl).float()
+        b = bench.dit_forward(params, img, txt, vec, lin).float()
+    assert torch.isfinite(a).all()
+    assert ((a - b).norm() / b.norm()).item() <= 1e-2
