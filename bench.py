@@ -210,15 +210,19 @@ def _dit_params(dev, quant, n_double, n_single):
 
 
 def _rope_tables(L, dev):
+    """float32 cos / sin [L, head_dim / 2] of the token positions (Flux keeps
+    its rotary tables in float32)."""
     hd = DIT["head_dim"]
-    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
-    ang = torch.arange(L, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
-    return torch.cos(ang).to(torch.bfloat16), torch.sin(ang).to(torch.bfloat16)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float64) / hd))
+    ang = torch.arange(L, device=dev, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous()
 
 
 def _rope(x, cos, sin):
-    x1, x2 = x[..., 0::2], x[..., 1::2]
-    return torch.stack((x1 * cos - x2 * sin, x1 * sin + x2 * cos), dim=-1).flatten(-2)
+    """Rotary embedding of adjacent pairs in float32, rounded once to x's
+    dtype (Flux's apply_rope)."""
+    a, b = x[..., 0::2].float(), x[..., 1::2].float()
+    return torch.stack((a * cos - b * sin, a * sin + b * cos), dim=-1).flatten(-2).to(x.dtype)
 
 
 def _attention(qkv, blk, cos, sin):
@@ -227,6 +231,18 @@ def _attention(qkv, blk, cos, sin):
     q, k, v = qkv.view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
     q = _rope(torch.nn.functional.rms_norm(q, (hd,), blk["qn"], 1e-6), cos, sin)
     k = _rope(torch.nn.functional.rms_norm(k, (hd,), blk["kn"], 1e-6), cos, sin)
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    return o.transpose(1, 2).reshape(B, L, H * hd)
+
+
+def _attention_fused(qkv, blk, cos, sin, qk):
+    """_attention with the q/k RMSNorm and the rotary embedding done in place
+    on the qkv projection by one kernel (``qk``); q, k, v reach the attention
+    as strided views of it."""
+    B, L, _ = qkv.shape
+    H, hd = DIT["heads"], DIT["head_dim"]
+    qk(qkv, H, hd, blk["qn"], blk["kn"], 1e-6, cos, sin)
+    q, k, v = qkv[..., :3 * H * hd].view(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
     o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
     return o.transpose(1, 2).reshape(B, L, H * hd)
 
@@ -266,12 +282,13 @@ def dit_forward(params, img, txt, vec, lin):
     return x[:, Lt:]
 
 
-def dit_forward_fused(params, img, txt, vec, fl):
+def dit_forward_fused(params, img, txt, vec, fl, qk):
     """``dit_forward`` with the element-wise neighbours of every linear fused
     into its kernels: ``fl(x, layer, **fusion)`` runs LayerNorm + modulation
-    in the activation quantiser and GELU / gated residual in the GEMM
-    epilogue.  Same arithmetic as ``dit_forward`` up to the float32 order of
-    the LayerNorm statistics."""
+    in the activation quantiser (and reads a concatenated input from its two
+    parts) and GELU / gated residual in the GEMM epilogue; ``qk`` is the
+    in-place q/k RMSNorm + rotary kernel.  Same arithmetic as ``dit_forward``
+    up to the float32 order of the norm statistics."""
     D = DIT["hidden"]
     dbl, sgl = params
     Lt = txt.shape[1]
@@ -285,7 +302,7 @@ def dit_forward_fused(params, img, txt, vec, fl):
         mi = fl(svec, blk["img_mod"]).chunk(6, dim=-1)
         mt = fl(svec, blk["txt_mod"]).chunk(6, dim=-1)
         qkv = torch.cat((fl(txt, blk["txt_qkv"], **pre(mt[0], mt[1])), fl(img, blk["img_qkv"], **pre(mi[0], mi[1]))), 1)
-        o = _attention(qkv, blk, cos, sin)
+        o = _attention_fused(qkv, blk, cos, sin, qk)
         txt = fl(o[:, :Lt], blk["txt_proj"], residual=txt, gate=mt[2])
         img = fl(o[:, Lt:], blk["img_proj"], residual=img, gate=mi[2])
         img = fl(fl(img, blk["img_mlp0"], gelu_from=0, **pre(mi[3], mi[4])), blk["img_mlp1"], residual=img, gate=mi[5])
@@ -294,9 +311,8 @@ def dit_forward_fused(params, img, txt, vec, fl):
     for blk in sgl:
         m = fl(svec, blk["mod"]).chunk(3, dim=-1)
         h = fl(x, blk["linear1"], gelu_from=3 * D, **pre(m[0], m[1]))
-        qkv, mlp = h.split((3 * D, DIT["mlp"] * D), dim=-1)
-        o = _attention(qkv.contiguous(), blk, cos, sin)
-        x = fl(torch.cat((o, mlp), -1), blk["linear2"], residual=x, gate=m[2])
+        o = _attention_fused(h, blk, cos, sin, qk)
+        x = fl(o, blk["linear2"], residual=x, gate=m[2], x2=h[..., 3 * D:])
     return x[:, Lt:]
 
 
@@ -319,6 +335,31 @@ def dit_inputs(samples, dev, seed):
     return mk(samples, DIT["img"], D), mk(samples, DIT["txt"], D), mk(samples, D)
 
 
+def dit_linears(pkg, rot):
+    """The two forms of a quantised DiT linear on [batch, tokens, K] inputs:
+    ``lin(x, layer)`` (the public W8A8 + ConvRot op) and ``fl(x, layer,
+    **fusion)`` (its fused-neighbour form; ``x2`` = second part of a
+    concatenated input)."""
+    pub = pkg.int8_quant
+
+    def lin(x, layer):
+        shp = x.shape
+        y = pub.int8_forward_dynamic_per_row(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16,
+                                             rot)
+        return y.reshape(*shp[:-1], layer.n)
+
+    def fl(x, layer, residual=None, gate=None, x2=None, **kw):
+        shp = x.shape
+        rows = x.numel() // shp[-1] // shp[0]  # tokens per sample
+        y = pub.int8_forward_fused(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16, rot,
+                                   rows_per_sample=rows, rows_per_gate=rows, gate=gate,
+                                   residual=None if residual is None else residual.reshape(-1, layer.n),
+                                   x2=None if x2 is None else x2.reshape(-1, x2.shape[-1]), **kw)
+        return y.reshape(*shp[:-1], layer.n)
+
+    return lin, fl
+
+
 def run_dit(pkg, dev, world, rank):
     """DiT steps/s with the 16 samples split across ranks (strong scaling, no
     collective), max step time over ranks; plus the CPU extrapolation."""
@@ -329,23 +370,9 @@ def run_dit(pkg, dev, world, rank):
     if per_rank * world != DIT["samples"]:
         return {"skipped": f"{DIT['samples']} samples do not split over {world} ranks"}
     params = _dit_params(dev, lambda w: ops.quant_weight_int8(w, rot), DIT["double"], DIT["single"])
-
-    def lin(x, layer):
-        shp = x.shape
-        y = pub.int8_forward_dynamic_per_row(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16,
-                                             rot)
-        return y.reshape(*shp[:-1], layer.n)
-
-    def fl(x, layer, residual=None, gate=None, **kw):
-        shp = x.shape
-        rows = x.numel() // shp[-1] // shp[0]  # tokens per sample
-        y = pub.int8_forward_fused(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16, rot,
-                                   rows_per_sample=rows, rows_per_gate=rows, gate=gate,
-                                   residual=None if residual is None else residual.reshape(-1, layer.n), **kw)
-        return y.reshape(*shp[:-1], layer.n)
-
+    lin, fl = dit_linears(pkg, rot)
     img, txt, vec = dit_inputs(per_rank, dev, DIT["seed"] + 100 * rank)
-    variants = {"fused": lambda: dit_forward_fused(params, img, txt, vec, fl),
+    variants = {"fused": lambda: dit_forward_fused(params, img, txt, vec, fl, ops.qk_norm_rope_),
                 "unfused": lambda: dit_forward(params, img, txt, vec, lin)}
     times, outs = {}, {}
     with torch.no_grad():

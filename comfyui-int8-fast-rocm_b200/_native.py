@@ -35,6 +35,8 @@ SIGNATURES = {
     "qlin_device_error": [_P, _P],
     "qlin_quant_act_int8": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_quant_act_int8_norm": [_P, _I, _L, _L, _L, _I, _F, _P, _P, _L, _P, _L, _L, _I, _I, _F, _P, _P, _P],
+    "qlin_quant_act_int8_cat": [_P, _L, _L, _P, _L, _L, _I, _L, _I, _I, _F, _P, _P, _P],
+    "qlin_qk_norm_rope": [_P, _I, _L, _L, _I, _I, _P, _P, _F, _P, _P, _L, _P],
     "qlin_quant_act_int4": [_P, _I, _L, _L, _L, _I, _I, _F, _I, _F, _P, _P, _P],
     "qlin_rotate": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P],
     "qlin_situ": [_P, _I, _L, _L, _L, _P, _P],

@@ -174,6 +174,43 @@ QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int
                                q, scale, static_cast<cudaStream_t>(stream));
 }
 
+QLIN_API int qlin_quant_act_int8_cat(const void* x1, int64_t ld1, int64_t K1, const void* x2, int64_t ld2,
+                                     int64_t K2, int x_dtype, int64_t M, int rot_kind, int rot_group, float rot_c,
+                                     int8_t* q, float* scale, void* stream) {
+  if (M < 0 || K1 <= 0 || K2 <= 0 || ld1 < K1 || ld2 < K2) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
+  if (M == 0) return QLIN_OK;
+  if (!x1 || !x2 || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K1 + K2))) return rc;
+  if (!rows_vec_ok(x1, K1, ld1, x_dtype) || !rows_vec_ok(x2, K2, ld2, x_dtype) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "concatenated rows need K1, K2 % 16 == 0 and 16-byte aligned rows");
+  return launch_rowquant_cat(x_dtype, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, rot_c, x1, ld1, K1, x2,
+                             ld2, K2, M, q, scale, static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_qk_norm_rope(void* qkv, int dtype, int64_t rows, int64_t ld, int heads, int head_dim,
+                               const void* q_weight, const void* k_weight, float eps, const float* cos_tab,
+                               const float* sin_tab, int64_t positions, void* stream) {
+  if (rows < 0 || heads < 0 || positions < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (dtype != QLIN_BF16 && dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "dtype must be BF16 or F16");
+  if (head_dim != 64 && head_dim != 128) return fail(QLIN_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (ld < 2 * (int64_t)heads * head_dim) return fail(QLIN_ERR_INVALID_ARG, "row stride shorter than the q and k heads");
+  if (!(eps >= 0.0f)) return fail(QLIN_ERR_INVALID_ARG, "eps must be >= 0");
+  if ((cos_tab == nullptr) != (sin_tab == nullptr)) return fail(QLIN_ERR_INVALID_ARG, "give both cos and sin tables");
+  if (cos_tab && positions == 0) return fail(QLIN_ERR_INVALID_ARG, "the rotary tables need positions > 0");
+  if (rows == 0 || heads == 0) return QLIN_OK;
+  if (!qkv) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if (!aligned16(qkv) || (ld * 2) % 16 || (q_weight && !aligned16(q_weight)) || (k_weight && !aligned16(k_weight)) ||
+      (cos_tab && (!aligned16(cos_tab) || !aligned16(sin_tab))))
+    return fail(QLIN_ERR_ALIGNMENT, "qkv rows, norm weights and rotary tables must be 16-byte aligned");
+  return launch_qk_norm_rope(dtype, qkv, rows, ld, heads, head_dim, q_weight, k_weight, eps, cos_tab, sin_tab,
+                             positions, static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                  int rot_group, float rot_c, int group, float clamp_min, int8_t* q, float* scale,
                                  void* stream) {

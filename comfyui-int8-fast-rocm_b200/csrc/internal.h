@@ -46,6 +46,15 @@ struct FusedPrologue {
 int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
                           int64_t K, const FusedPrologue& f, int8_t* q, float* scale, cudaStream_t stream);
 
+int launch_rowquant_cat(int dt, int rot_kind, int rot_group, float rot_c, const void* x1, int64_t ld1, int64_t K1,
+                        const void* x2, int64_t ld2, int64_t K2, int64_t M, int8_t* q, float* scale,
+                        cudaStream_t stream);
+
+// In-place q/k RMSNorm + rotary embedding of fused qkv rows (dit.cu).
+int launch_qk_norm_rope(int dt, void* qkv, int64_t rows, int64_t ld, int heads, int head_dim, const void* q_w,
+                        const void* k_w, float eps, const float* cos_t, const float* sin_t, int64_t positions,
+                        cudaStream_t stream);
+
 int launch_rowquant_generic(int dt, int mode, const void* x, int64_t ldx, int64_t M, int64_t K, float clamp_min,
                             int8_t* q, float* scale, cudaStream_t stream);
 

@@ -294,6 +294,38 @@ int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, cons
   return r;
 }
 
+// Per-token int8 quantisation of concatenated rows [x1[r, 0:K1] | x2[r, 0:K2]]
+// (16-bit or float32 inputs, K1 and K2 multiples of 16, 16-byte aligned
+// sources and row strides: checked by the caller).  The two parts land next
+// to each other in the ring slot, so the rotation groups may straddle them.
+int launch_rowquant_cat(int dt, int rot_kind, int rot_group, float rot_c, const void* x1, int64_t ld1, int64_t K1,
+                        const void* x2, int64_t ld2, int64_t K2, int64_t M, int8_t* q, float* scale,
+                        cudaStream_t stream) {
+  if (M == 0) return QLIN_OK;
+  RowQuantParams p{};
+  p.x = x1;
+  p.ldx = ld1;
+  p.x2 = x2;
+  p.ldx2 = ld2;
+  p.k1 = (int)K1;
+  p.M = (int)M;
+  p.K = (int)(K1 + K2);
+  p.rot_c = rot_c;
+  p.q = q;
+  p.scale = scale;
+  p.one = 1.0f;
+  const RotCode rc = rot_code(rot_kind, rot_kind == 0 ? 0 : rot_group);
+  if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
+  const int64_t nchunks = p.K / 16;
+  if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  int r = QLIN_ERR_UNSUPPORTED;
+  if (dt == DT_BF16) r = x2_by_chunks<DT_BF16>(rc, p, (int)nchunks, stream);
+  else if (dt == DT_F16) r = x2_by_chunks<DT_F16>(rc, p, (int)nchunks, stream);
+  else if (dt == DT_F32) r = x2_by_chunks<DT_F32>(rc, p, (int)nchunks, stream);
+  if (r == QLIN_ERR_UNSUPPORTED) return fail(QLIN_ERR_UNSUPPORTED, "row too long for the concatenating quantiser");
+  return r;
+}
+
 // Error word of the row kernels: read and clear (bit 1: a bulk-copy wait
 // timed out).
 int read_rowquant_error(cudaStream_t stream, uint32_t* bits) {

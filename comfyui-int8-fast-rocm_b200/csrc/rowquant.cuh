@@ -54,6 +54,11 @@ struct RowQuantParams {
   const void* mod_add;   // [S, add_ld] or null
   int64_t add_ld;
   int64_t rows_per_sample;
+  // second source of rowquant_x2_kernel (x2 != null): row r is the
+  // concatenation [x[r, 0:k1] | x2[r, 0:K-k1]], x2 rows ldx2 elements apart
+  const void* x2;
+  int64_t ldx2;
+  int k1;
 };
 
 enum : int {
@@ -662,7 +667,9 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
   __syncthreads();
 
   // fill slot s with the rows of iteration `it` (thread 0 only)
-  const bool dense = (int64_t)p.ldx * EB == row_bytes;
+  const bool two_src = p.x2 != nullptr;
+  const bool dense = !two_src && (int64_t)p.ldx * EB == row_bytes;
+  const int bytes1 = two_src ? p.k1 * EB : row_bytes;  // 16-byte multiple (checked by the host)
   auto issue = [&](int it, int s) {
     const int64_t f = ((int64_t)blockIdx.x + (int64_t)it * gridDim.x) * rpc;
     if (f >= p.M) return;
@@ -673,8 +680,13 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
     if (dense) {
       bulk_load(dst, src + f * row_bytes, (uint32_t)(nrows * row_bytes), &full[s]);
     } else {
-      for (int r = 0; r < nrows; ++r)
-        bulk_load(dst + (size_t)r * row_bytes, src + (f + r) * (int64_t)p.ldx * EB, (uint32_t)row_bytes, &full[s]);
+      for (int r = 0; r < nrows; ++r) {
+        bulk_load(dst + (size_t)r * row_bytes, src + (f + r) * (int64_t)p.ldx * EB, (uint32_t)bytes1, &full[s]);
+        if (two_src)
+          bulk_load(dst + (size_t)r * row_bytes + bytes1,
+                    reinterpret_cast<const uint8_t*>(p.x2) + (f + r) * (int64_t)p.ldx2 * EB,
+                    (uint32_t)(row_bytes - bytes1), &full[s]);
+      }
     }
   };
   if (tid == 0)

@@ -99,7 +99,7 @@ def int8_forward_dynamic_per_row(x: Tensor, weight: Tensor, weight_scale: Tensor
 def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dtype, rot=None, per_row=True, *,
                        norm=None, eps: float = 1e-6, norm_weight=None, mod_mul=None, mod_add=None,
                        rows_per_sample=None, gelu_from=None, residual=None, gate=None,
-                       rows_per_gate=None) -> Tensor:
+                       rows_per_gate=None, x2=None) -> Tensor:
     """:func:`int8_forward_dynamic_per_row` / :func:`int8_forward_dynamic`
     with the element-wise neighbours of a DiT block's linear fused into its
     two kernels (no counterpart in the reference, which runs them as eager
@@ -111,10 +111,16 @@ def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dt
       ``layer_norm(x) * (1 + scale) + shift`` is ``norm="layer",
       mod_mul=1 + scale, mod_add=shift``;
     * epilogue (GEMM): ``dt(gelu_tanh(y))`` on columns ``>= gelu_from``, then
-      ``dt(residual + dt(gate[g] * y))`` with ``g = row // rows_per_gate``.
+      ``dt(residual + dt(gate[g] * y))`` with ``g = row // rows_per_gate``;
+    * ``x2``: the linear's input is ``torch.cat((x, x2), -1)``, read from the
+      two tensors by the quantiser (no prologue steps then).
     """
     prologue = norm is not None or mod_mul is not None or mod_add is not None
-    if prologue:
+    if x2 is not None:
+        if prologue:
+            raise ValueError("a concatenated input takes no norm / modulation prologue")
+        xq, xs = ops.quant_act_int8_cat(x, x2, rot)
+    elif prologue:
         xq, xs = ops.quant_act_int8_norm(x, rot, norm, eps, norm_weight, mod_mul, mod_add, rows_per_sample)
     else:
         xq, xs = ops.quant_act_int8(x, rot)

@@ -161,6 +161,75 @@ def quant_act_int8_norm(x: torch.Tensor, rot=None, norm=None, eps: float = 1e-6,
     return q, s
 
 
+def quant_act_int8_cat(x1: torch.Tensor, x2: torch.Tensor, rot=None):
+    """Per-token int8 of the row concatenation ``torch.cat((x1, x2), -1)``
+    without materialising it: ``x1`` [M, K1] and ``x2`` [M, K2] (row-strided
+    views are read in place, e.g. column slices of a wider output).  Returns
+    (q int8 [M, K1 + K2], scale float32 [M, 1])."""
+    if x1.dim() != 2 or x2.dim() != 2 or x1.shape[0] != x2.shape[0]:
+        raise ValueError(f"expected [M, K1] and [M, K2] tensors, got {tuple(x1.shape)} and {tuple(x2.shape)}")
+    if x1.dtype != x2.dtype or x1.device != x2.device:
+        raise ValueError("the two parts must share dtype and device")
+    x1, ld1 = _rows(x1)
+    x2, ld2 = _rows(x2)
+    M, K1 = x1.shape
+    K2 = x2.shape[1]
+    q = torch.empty((M, K1 + K2), dtype=torch.int8, device=x1.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x1.device)
+    if M == 0:
+        return q, s
+    st = _stream(x1)
+    es = x1.element_size()
+    if x1.data_ptr() % 16 or (ld1 * es) % 16:
+        x1, ld1 = x1.contiguous().clone(), K1
+    if x2.data_ptr() % 16 or (ld2 * es) % 16:
+        x2, ld2 = x2.contiguous().clone(), K2
+    kind, g, c = _rot_args(rot, x1.dtype)
+    N.call("qlin_quant_act_int8_cat", x1.data_ptr(), ld1, K1, x2.data_ptr(), ld2, K2, dtype_code(x1.dtype), M,
+           kind, g, c, q.data_ptr(), s.data_ptr(), st)
+    return q, s
+
+
+def qk_norm_rope_(qkv: torch.Tensor, heads: int, head_dim: int, q_weight=None, k_weight=None, eps: float = 1e-6,
+                  cos=None, sin=None) -> torch.Tensor:
+    """In place on the fused qkv projection ``qkv`` [..., L, >= 3*heads*head_dim]
+    (bf16/f16, unit inner stride, rows may be strided): every q and k head
+    vector becomes ``rope(dt(F.rms_norm(x, (head_dim,), weight, eps)))``;
+    ``cos`` / ``sin`` are float32 [L, head_dim // 2] tables indexed by the
+    token position within its sample (None: no rotation); the rotation of
+    the pair (a, b) = (n[2i], n[2i+1]) is (c*a - s*b, s*a + c*b), each float32
+    product and sum rounded, then rounded to the dtype.  Returns ``qkv``."""
+    if qkv.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"qk_norm_rope_ takes bfloat16 or float16, got {qkv.dtype}")
+    if qkv.stride(-1) != 1:
+        raise ValueError("qkv needs a unit inner stride")
+    ld = qkv.stride(-2) if qkv.dim() >= 2 else qkv.shape[-1]
+    rows = qkv.numel() // qkv.shape[-1]
+    if qkv.dim() >= 3:  # rows must be evenly strided across the leading dims
+        for d in range(qkv.dim() - 2):
+            if qkv.stride(d) != qkv.stride(d + 1) * qkv.shape[d + 1]:
+                raise ValueError("qkv rows must be evenly strided")
+    positions = qkv.shape[-2] if qkv.dim() >= 2 else 1
+    st = _stream(qkv)
+
+    def vec(w):
+        if w is None:
+            return None
+        w = w.reshape(-1).to(device=qkv.device, dtype=qkv.dtype)
+        if w.numel() != head_dim:
+            raise ValueError(f"norm weight must have {head_dim} elements")
+        return _aligned(w)
+
+    qw, kw = vec(q_weight), vec(k_weight)
+    ct = stb = None
+    if cos is not None:
+        ct = _aligned(cos.to(device=qkv.device, dtype=torch.float32).reshape(positions, head_dim // 2))
+        stb = _aligned(sin.to(device=qkv.device, dtype=torch.float32).reshape(positions, head_dim // 2))
+    N.call("qlin_qk_norm_rope", qkv.data_ptr(), dtype_code(qkv.dtype), rows, ld, int(heads), int(head_dim),
+           _ptr(qw), _ptr(kw), float(eps), _ptr(ct), _ptr(stb), positions, st)
+    return qkv
+
+
 def quant_act_int4(x: torch.Tensor, rot=None, group: int = 0):
     """Signed int4-range codes in int8 storage: (q [M,K], scale float32
     [M] (group 0) or [M, K/128] (group 128))."""

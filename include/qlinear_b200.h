@@ -115,6 +115,38 @@ QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int
                                       int64_t add_ld, int64_t rows_per_sample, int rot_kind, int rot_group, float rot_c,
                                       int8_t* q, float* scale, void* stream);
 
+/* qlin_quant_act_int8 of concatenated rows: row r of the quantised input is
+ * [x1[r, 0:K1] | x2[r, 0:K2]] (K = K1 + K2), x1 rows ld1 and x2 rows ld2
+ * elements apart, so the concatenation is never written to memory.
+ * x_dtype BF16, F16 or F32; K1 and K2 multiples of 16 (K <= 32768); both
+ * sources and both row strides 16-byte aligned; q [M, K], scale [M].
+ * Replaces the torch.cat that feeds a quantised linear, e.g. a Flux single
+ * block's linear2(cat(attention, mlp_act(mlp))) in front of
+ * Int8TensorwiseOps.Linear (int8_quant.py:633-716); no counterpart in the
+ * reference's own files, which leave the model code to ComfyUI. */
+QLIN_API int qlin_quant_act_int8_cat(const void* x1, int64_t ld1, int64_t K1, const void* x2, int64_t ld2,
+                                     int64_t K2, int x_dtype, int64_t M, int rot_kind, int rot_group, float rot_c,
+                                     int8_t* q, float* scale, void* stream);
+
+/* Attention prologue of a Flux-style DiT block, in place on the fused qkv
+ * projection: rows [rows, ld] in dtype (BF16 or F16), each row holding
+ * `heads` q vectors, then `heads` k vectors, then the v vectors, head_dim
+ * (64 or 128) elements each.  For every q and k vector x:
+ *   n = dt((x * rsqrt(mean(x^2) + eps)) * w)     (F.rms_norm; w = q_weight or
+ *                                                 k_weight [head_dim], NULL = none)
+ * then, when cos_tab / sin_tab are given (float32 [positions, head_dim/2],
+ * table row = row % positions), each pair (a, b) = (n[2i], n[2i+1]) becomes
+ *   (dt(c*a - s*b), dt(s*a + c*b))               (each float32 product and sum rounded)
+ * with c = cos_tab[pos, i], s = sin_tab[pos, i].  v is not touched.
+ * qkv, ld * element size, the weights and the tables 16-byte aligned;
+ * ld >= 2 * heads * head_dim.  No counterpart in the reference (the model
+ * code around its quantised linears lives in ComfyUI); replaces the eager
+ * q/k RMSNorm and rotary embedding between a DiT block's quantised qkv
+ * linear and its attention. */
+QLIN_API int qlin_qk_norm_rope(void* qkv, int dtype, int64_t rows, int64_t ld, int heads, int head_dim,
+                               const void* q_weight, const void* k_weight, float eps, const float* cos_tab,
+                               const float* sin_tab, int64_t positions, void* stream);
+
 /* Signed int4-range quantisation (codes in [-7,7], one per int8 byte) with
  * the int4_quant.py conventions computed in x_dtype: absmax clamped at
  * clamp_min (1e-10 in x_dtype), scale = absmax/7, round(x/scale).

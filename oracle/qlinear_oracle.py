@@ -624,3 +624,32 @@ def linear_post(y, dtype: str, gelu_from=None, residual=None, gate=None, rows_pe
         t = y if gate is None else rnd(dtype, _per_sample(gate, M, rows_per_gate or M) * y)
         y = rnd(dtype, np.asarray(residual, F32) + t)
     return y
+
+
+def qk_norm_rope(qkv, heads: int, head_dim: int, dtype: str, q_weight=None, k_weight=None, eps: float = 1e-6,
+                 cos=None, sin=None, positions=None) -> np.ndarray:
+    """The attention prologue of a Flux-style DiT block on rows ``qkv`` [R, C]
+    (C >= 3*heads*head_dim; q heads, k heads, v heads): every q and k head
+    vector gets ``F.rms_norm(x, (head_dim,), weight, eps)`` (``row_norm``
+    "rms") and then the rotary embedding of adjacent pairs in float32,
+    ``(c*a - s*b, s*a + c*b)`` with every product and sum rounded to float32
+    and the result rounded once to ``dtype`` (Flux's apply_rope on float32
+    tables ``cos`` / ``sin`` [positions, head_dim/2], table row = row %
+    positions).  Returns a new array; v and the columns after it are kept.
+    No counterpart in the reference (ComfyUI's model code)."""
+    x = np.array(qkv, F32, copy=True)
+    R = x.shape[0]
+    D = heads * head_dim
+    for part, w in ((0, q_weight), (1, k_weight)):
+        v = x[:, part * D:(part + 1) * D].reshape(R * heads, head_dim)
+        n = row_norm(v, "rms", eps, dtype, w).reshape(R, heads, head_dim)
+        if cos is not None:
+            pos = np.arange(R) % (positions or R)
+            c = np.asarray(cos, F32)[pos][:, None, :]
+            s = np.asarray(sin, F32)[pos][:, None, :]
+            a, b = n[..., 0::2], n[..., 1::2]
+            o0 = ((c * a).astype(F32) - (s * b).astype(F32)).astype(F32)
+            o1 = ((s * a).astype(F32) + (c * b).astype(F32)).astype(F32)
+            n = rnd(dtype, np.stack((o0, o1), axis=-1).reshape(R, heads, head_dim))
+        x[:, part * D:(part + 1) * D] = n.reshape(R, D)
+    return x

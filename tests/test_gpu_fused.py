@@ -281,10 +281,11 @@ def test_gemm_fused_strided_gate_and_errors(P):
 
 def test_dit_blocks_fused_match_unfused(P, monkeypatch):
     """The measured DiT step with its neighbours fused (bench.py's
-    dit_forward_fused) against the same blocks with eager norm / modulation /
-    GELU / residual around the plain quantised linear, on a small config:
-    equal up to the LayerNorm statistics' order (relative L2 <= 1e-2 after
-    two double and two single blocks)."""
+    dit_forward_fused: norm / modulation in the quantiser, GELU / residual in
+    the GEMM epilogue, q/k norm + rotary kernel, concatenated linear2 input)
+    against the same blocks with those steps eager around the plain
+    quantised linear, on a small config: equal up to the norm statistics'
+    order (relative L2 <= 1e-2 after two double and two single blocks)."""
     import bench
     monkeypatch.setitem(bench.DIT, "hidden", 256)
     monkeypatch.setitem(bench.DIT, "heads", 2)
@@ -293,23 +294,11 @@ def test_dit_blocks_fused_match_unfused(P, monkeypatch):
     dev_ = torch.device("cuda", 0)
     rot = (bench.DIT["kind"], bench.DIT["group"])
     params = bench._dit_params(dev_, lambda w: P.ops.quant_weight_int8(w, rot), 2, 2)
-    pub = P.int8_quant
-
-    def lin(x, layer):
-        y = pub.int8_forward_dynamic_per_row(x.reshape(-1, x.shape[-1]), layer.wq, layer.ws, layer.b,
-                                             torch.bfloat16, rot)
-        return y.reshape(*x.shape[:-1], layer.n)
-
-    def fl(x, layer, residual=None, gate=None, **kw):
-        rows = x.numel() // x.shape[-1] // x.shape[0]
-        y = pub.int8_forward_fused(x.reshape(-1, x.shape[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16, rot,
-                                   rows_per_sample=rows, rows_per_gate=rows, gate=gate,
-                                   residual=None if residual is None else residual.reshape(-1, layer.n), **kw)
-        return y.reshape(*x.shape[:-1], layer.n)
+    lin, fl = bench.dit_linears(P, rot)
 
     img, txt, vec = bench.dit_inputs(2, dev_, 7)
     with torch.no_grad():
-        a = bench.dit_forward_fused(params, img, txt, vec, fl).float()
+        a = bench.dit_forward_fused(params, img, txt, vec, fl, P.ops.qk_norm_rope_).float()
         b = bench.dit_forward(params, img, txt, vec, lin).float()
     assert torch.isfinite(a).all()
     assert ((a - b).norm() / b.norm()).item() <= 1e-2

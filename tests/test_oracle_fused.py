@@ -77,3 +77,35 @@ def test_gated_residual_matches_torch(dt):
     got = O.linear_post(y, dt, residual=res, gate=gate, rows_per_gate=L)
     np.testing.assert_array_equal(ref.float().numpy(), got)
     np.testing.assert_array_equal((_t(res, dt) + _t(y, dt)).float().numpy(), O.linear_post(y, dt, residual=res))
+
+
+def _rope_tables(L, hd):
+    inv = 1.0 / (10000.0 ** (np.arange(0, hd, 2, dtype=np.float64) / hd))
+    ang = np.arange(L, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_qk_norm_rope_matches_torch(dt):
+    """q/k RMSNorm + float32 rotary embedding (Flux's apply_rope) in torch's
+    CPU kernels vs the oracle: rare last-unit differences from the norm's
+    float32 statistics only."""
+    rng = np.random.default_rng(4)
+    B, L, H, hd = 2, 48, 3, 128
+    qkv = _x(rng, (B * L, 3 * H * hd + 32), dt, 1.5)
+    qw, kw = _x(rng, hd, dt, 0.3, 1.0), _x(rng, hd, dt, 0.3, 1.0)
+    cos, sin = _rope_tables(L, hd)
+    t = _t(qkv, dt).view(B, L, -1)
+    q, k, v = t[..., :3 * H * hd].reshape(B, L, 3, H, hd).permute(2, 0, 3, 1, 4)
+
+    def rope(x):
+        a, b = x[..., 0::2].float(), x[..., 1::2].float()
+        c, s = torch.from_numpy(cos), torch.from_numpy(sin)
+        return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2).to(x.dtype)
+
+    rq = rope(F.rms_norm(q, (hd,), _t(qw, dt), 1e-6)).transpose(1, 2).reshape(B * L, H * hd)
+    rk = rope(F.rms_norm(k, (hd,), _t(kw, dt), 1e-6)).transpose(1, 2).reshape(B * L, H * hd)
+    got = O.qk_norm_rope(qkv, H, hd, dt, qw, kw, 1e-6, cos, sin, positions=L)
+    assert (rq.float().numpy() != got[:, :H * hd]).mean() <= 1e-3
+    assert (rk.float().numpy() != got[:, H * hd:2 * H * hd]).mean() <= 1e-3
+    np.testing.assert_array_equal(got[:, 2 * H * hd:], qkv[:, 2 * H * hd:])
