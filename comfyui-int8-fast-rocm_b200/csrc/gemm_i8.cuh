@@ -96,6 +96,8 @@ template <int BN>
 struct EpiSmem {
   float ws[2][BN];
   float bias[2][BN];
+  float gate[2][BN];  // EPI_POST gate row of the tile (when its rows share one)
+  int gate_ok[2];
 };
 
 template <int BN, bool B_INT4>
@@ -205,16 +207,22 @@ __device__ __forceinline__ void epi_load_params(const GemmParams& p, int colt0, 
   }
 }
 
-// tanh-form GELU in float32 as PyTorch's CUDA kernel evaluates
-// F.gelu(approximate="tanh"): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-// with the inner sum contracted to one FMA (nvcc's default contraction in
-// that build) and CUDA's tanhf.
+// tanh-form GELU, 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3),
+// evaluated as the equal x * sigmoid(2u) = x / (1 + 2^(-2u log2(e))): the
+// exponential and the reciprocal on the special-function unit (ex2.approx,
+// rcp.approx; a few float32 units of error), so a 16-bit result is within
+// one unit of the exact function's -- including where 1 + tanh(u) cancels
+// in float32 (x < -3), which the tanh form evaluates with large relative
+// error.  Infinities and NaN behave as in the tanh form (+inf -> +inf,
+// -inf -> NaN, NaN -> NaN); large negative x gives -0.
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float kKappa = 0.044715f;
+  const float kNeg2BetaLog2e = -2.302208198144325f;  // -2 sqrt(2/pi) / ln(2)
   const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-  const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+  const float t = __fmul_rn(kNeg2BetaLog2e, __fmaf_rn(0.044715f, x3, x));
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
+  return __fmul_rn(x, r);
 }
 
 template <int DT>
@@ -438,6 +446,253 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
   }
 }
 
+// Residual values of row `row`, columns [col0, col0 + 32) of an EPI_POST
+// residual, as 16 packed pairs (zeros outside the tensor).  Rows are 16-byte
+// aligned (checked on the host).
+template <int OUT_DT>
+__device__ __forceinline__ void load_res32(const GemmParams& p, int row, int col0, uint4 (&rv)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) rv[q] = make_uint4(0u, 0u, 0u, 0u);
+  if (p.residual == nullptr || row < 0 || row >= p.M || col0 >= p.N) return;
+  const uint16_t* rs = reinterpret_cast<const uint16_t*>(p.residual) + (int64_t)row * p.ld_res + col0;
+  if (col0 + 32 <= p.N) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) rv[q] = __ldg(reinterpret_cast<const uint4*>(rs) + q);
+  } else {
+    const int n = p.N - col0;
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = 2 * j < n ? (uint32_t)rs[2 * j] : 0u;
+      const uint32_t hi = 2 * j + 1 < n ? (uint32_t)rs[2 * j + 1] : 0u;
+      w[j] = lo | (hi << 16);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) rv[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
+}
+
+// Round 32 float values to the 16-bit dtype and back, two per conversion
+// instruction (cvt.rn.{bf16x2,f16x2}.f32): the conversion unit, which
+// handles 16 operations per clock per SM, bounds this epilogue, so every
+// rounding step goes through it in pairs.
+template <int OUT_DT>
+__device__ __forceinline__ void rnd_pairs(float (&y)[32]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (OUT_DT == DT_BF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+      const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+      y[2 * j] = __uint_as_float(u << 16);
+      y[2 * j + 1] = __uint_as_float(u & 0xFFFF0000u);
+    } else {
+      const float2 f = __half22float2(__floats2half2_rn(y[2 * j], y[2 * j + 1]));
+      y[2 * j] = f.x;
+      y[2 * j + 1] = f.y;
+    }
+  }
+}
+
+// One 32-column chunk of the TMA-store epilogue: accumulator registers `r`
+// (already waited for) -> the reference's epilogue -> EPI_POST steps ->
+// 16-bit values staged in `sb` (64-byte TMA swizzle) -> one TMA store.
+// `g32`: the tile's gate row staged in shared memory, or null (per-row gate
+// loads).  Bulk stores are double-buffered per warp: before `sb` is written,
+// every store but the most recent one (which used the other buffer) has
+// read its source.
+template <int EPI, int OUT_DT>
+__device__ __forceinline__ void epi_chunk_tma(const GemmParams& p, const uint32_t (&r)[32], const uint4 (&rv)[4],
+                                              const float* ws32, const float* b32, const float* g32, float xs,
+                                              float s_tensor, bool has_bias, int row, int row_base, int col0, int lane,
+                                              const CUtensorMap* tmC, uint8_t* sb) {
+  constexpr int EB = epi_base(EPI);
+  constexpr bool POST = (EPI & EPI_POST) != 0;
+  // The reference's rounding sequence with each dt() applied in pairs; the
+  // last dt() of the chain is the packing conversion of the store, so a
+  // value is never converted twice:
+  //   W8A8: dt(dt(float(acc) * xs * ws) + bias)   W4A4: dt(float(acc) * xs * ws + bias)
+  float y[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float wv[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (EB != EPI_W8A8_TENSOR) {
+      const float4 t = reinterpret_cast<const float4*>(ws32)[i];
+      wv[0] = t.x; wv[1] = t.y; wv[2] = t.z; wv[3] = t.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * i + k;
+      const float f = __int2float_rn((int32_t)r[j]);  // res.float()
+      if constexpr (EB == EPI_W8A8_TENSOR) {
+        y[j] = __fmul_rn(f, s_tensor);              // .mul_(ws * xs)
+      } else {
+        y[j] = __fmul_rn(__fmul_rn(f, xs), wv[k]);  // .mul_(xs).mul_(ws.T)
+      }
+    }
+  }
+  if constexpr (EB != EPI_W4A4_ROW) rnd_pairs<OUT_DT>(y);  // .to(dt)
+  if (has_bias) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = reinterpret_cast<const float4*>(b32)[i];
+      y[4 * i] = __fadd_rn(y[4 * i], t.x);
+      y[4 * i + 1] = __fadd_rn(y[4 * i + 1], t.y);
+      y[4 * i + 2] = __fadd_rn(y[4 * i + 2], t.z);
+      y[4 * i + 3] = __fadd_rn(y[4 * i + 3], t.w);
+    }
+  }
+  if constexpr (POST) {
+    // the steps below take the dtype value of the linear's output
+    if (has_bias || EB == EPI_W4A4_ROW) rnd_pairs<OUT_DT>(y);
+    if (p.gelu_col0 <= (int64_t)col0) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[j] = gelu_tanh_f(y[j]);
+      if (p.residual != nullptr) rnd_pairs<OUT_DT>(y);
+    } else if (p.gelu_col0 < (int64_t)col0 + 32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j >= p.gelu_col0) y[j] = gelu_tanh_f(y[j]);
+      rnd_pairs<OUT_DT>(y);  // exact on the columns that were already rounded
+    }
+    if (p.residual != nullptr) {
+      float rres[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float t8[8];
+        unpack8<OUT_DT>(rv[q], t8);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) rres[8 * q + k] = t8[k];
+      }
+      if (p.gate != nullptr) {
+        float gv[32];
+        if (g32 != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 t = reinterpret_cast<const float4*>(g32)[i];
+            gv[4 * i] = t.x; gv[4 * i + 1] = t.y; gv[4 * i + 2] = t.z; gv[4 * i + 3] = t.w;
+          }
+        } else {
+          // the CTA's rows span two gate rows: this row's own gate values
+          const uint16_t* gs = reinterpret_cast<const uint16_t*>(p.gate) +
+                               (int64_t)(min(row, p.M - 1) / p.rows_per_gate) * p.gate_ld + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const uint16_t h = col0 + j < p.N ? gs[j] : (uint16_t)0;
+            if constexpr (OUT_DT == DT_BF16) gv[j] = __uint_as_float((uint32_t)h << 16);
+            else gv[j] = __half2float(__ushort_as_half(h));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = __fmul_rn(gv[j], y[j]);
+        rnd_pairs<OUT_DT>(y);  // dt(gate * y)
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(rres[j], y[j]);  // rounded by the store's packing
+    }
+  }
+  uint32_t w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (OUT_DT == DT_BF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  if (lane == 0) bulk_wait_read_1();  // the store two chunks back (same buffer) has read it
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<uint4*>(sb + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmC, sb, (int)(p.col_off + col0), row_base);
+    bulk_commit_group();
+  }
+}
+
+// Epilogue of one 128-row accumulator tile for 16-bit outputs leaving
+// through TMA stores (one destination).  Stores alternate between the
+// warp's two staging buffers (`stc` counts this warp's stores across tiles
+// and picks the buffer).  Without EPI_POST the warp's CPW chunks are
+// software pipelined: the TMEM load of chunk c+1 is in flight while chunk c
+// is converted and stored.  With EPI_POST (register budget: one accumulator
+// chunk at a time) the residual loads of chunk c+1 are in flight instead;
+// `res` holds the residual of the warp's first chunk on entry (loaded
+// during the previous tile) and of the next tile's first chunk (row `nrow`,
+// column `ncol0`; nrow < 0: none) on return.
+template <int BN, int EPI, int OUT_DT>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, uint32_t tmem_acc, int row0, int colt0,
+                                                  int quarter, int half, int lane, const float* s_ws,
+                                                  const float* s_b, const float* s_gate, float xs,
+                                                  const CUtensorMap* tmC, uint8_t* stage, uint32_t& stc,
+                                                  uint4 (&res)[4], int nrow, int ncol0) {
+  constexpr int EB = epi_base(EPI);
+  constexpr bool POST = (EPI & EPI_POST) != 0;
+  constexpr int CPW = BN / 64;  // chunks per warp (two warps per lane quarter)
+  static_assert(CPW % 2 == 0, "chunks are processed in pairs");
+  const bool has_bias = p.bias != nullptr;
+  const int row = row0 + quarter * 32 + lane;
+  const int row_base = row0 + quarter * 32;
+  float s_tensor = 0.0f;
+  if constexpr (EB == EPI_W8A8_TENSOR) s_tensor = __fmul_rn(__ldg(p.w_scale), xs);
+  const int c0 = half * CPW;
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const bool quarter_live = row_base < p.M;  // warp-uniform
+  if constexpr (POST) {
+    const bool has_res = p.residual != nullptr;
+#pragma unroll 1
+    for (int cc = 0; cc < CPW; ++cc) {
+      const int col = colt0 + (c0 + cc) * 32;
+      uint32_t ra[32];
+      tmem_ld_32x32b_x32(tmem_acc + (c0 + cc) * 32 + lane_off, ra);
+      uint4 rn[4];
+      if (has_res) {
+        if (cc + 1 < CPW) load_res32<OUT_DT>(p, row, col + 32, rn);
+        else load_res32<OUT_DT>(p, nrow < 0 ? -1 : nrow, ncol0, rn);  // the next tile's first chunk
+      }
+      tmem_ld_wait_regs(ra);
+      if (quarter_live && col < p.N) {
+        epi_chunk_tma<EPI, OUT_DT>(p, ra, res, s_ws + (c0 + cc) * 32, s_b + (c0 + cc) * 32,
+                                   s_gate ? s_gate + (c0 + cc) * 32 : nullptr, xs, s_tensor, has_bias, row, row_base,
+                                   col, lane, tmC, stage + (stc & 1) * EPI_STAGE_BYTES);
+        ++stc;
+      }
+      if (has_res) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) res[q] = rn[q];
+      }
+    }
+    return;
+  }
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(tmem_acc + c0 * 32 + lane_off, ra);
+#pragma unroll 1
+  for (int cc = 0; cc < CPW; cc += 2) {
+    const int colA = colt0 + (c0 + cc) * 32;
+    const int colB = colA + 32;
+    tmem_ld_wait_regs(ra);
+    tmem_ld_32x32b_x32(tmem_acc + (c0 + cc + 1) * 32 + lane_off, rb);
+    if (quarter_live && colA < p.N) {
+      epi_chunk_tma<EPI, OUT_DT>(p, ra, res, s_ws + (c0 + cc) * 32, s_b + (c0 + cc) * 32, nullptr, xs, s_tensor,
+                                 has_bias, row, row_base, colA, lane, tmC, stage + (stc & 1) * EPI_STAGE_BYTES);
+      ++stc;
+    }
+    tmem_ld_wait_regs(rb);
+    if (cc + 2 < CPW) tmem_ld_32x32b_x32(tmem_acc + (c0 + cc + 2) * 32 + lane_off, ra);
+    if (quarter_live && colB < p.N) {
+      epi_chunk_tma<EPI, OUT_DT>(p, rb, res, s_ws + (c0 + cc + 1) * 32, s_b + (c0 + cc + 1) * 32, nullptr, xs,
+                                 s_tensor, has_bias, row, row_base, colB, lane, tmC,
+                                 stage + (stc & 1) * EPI_STAGE_BYTES);
+      ++stc;
+    }
+  }
+}
+
 // The epilogue role of a GEMM kernel: for each tile of this CTA, wait for the
 // accumulator, convert it, release it.  Parameters of tile i+1 are loaded into
 // registers while tile i is converted and staged into shared memory after it.
@@ -452,17 +707,61 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
   const int e = (warp - 2) * 32 + lane;  // 0..255
   const int quarter = warp & 3;
   const int half = (warp - 2) >> 2;
+  constexpr bool TMA16 = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+  constexpr bool POST = (EPI & EPI_POST) != 0;
+  constexpr int CPW = BN / 64;
   int acc = 0;
   uint32_t acc_phase = 0;
-  float nws, nb, nxs = 0.0f;
+  float nws, nb, nxs = 0.0f, ngate = 0.0f;
+  int ngok = 0;
   int buf = 0;
+  uint32_t stc = 0;  // TMA stores issued by this warp (staging buffer parity)
+  uint4 res[4] = {};
+  // EPI_POST gate of a tile: staged when the CTA's rows of the tile share one
+  // gate row (warp-uniform), else read per row in the epilogue
+  auto load_gate = [&](int mb, int nbk, float& g, int& ok) {
+    g = 0.0f;
+    ok = 0;
+    if constexpr (POST) {
+      if (p.gate == nullptr || p.residual == nullptr) return;
+      const int r_first = mb * ROWS_PER_TILE + row_off;
+      if (r_first >= p.M) return;
+      const int r_last = min(r_first + GEMM_BM - 1, p.M - 1);
+      if ((int64_t)r_first / p.rows_per_gate != (int64_t)r_last / p.rows_per_gate) return;
+      ok = 1;
+      const int col = nbk * BN + e;
+      if (e < BN && col < p.N) {
+        const uint16_t h =
+            reinterpret_cast<const uint16_t*>(p.gate)[((int64_t)r_first / p.rows_per_gate) * p.gate_ld + col];
+        g = OUT_DT == DT_BF16 ? __uint_as_float((uint32_t)h << 16) : __half2float(__ushort_as_half(h));
+      }
+    }
+  };
+  // EPI_POST residual rows of a tile (this lane's row, the warp's columns)
+  // into L2 a tile ahead of their use
+  auto prefetch_res = [&](int mb, int nbk) {
+    if constexpr (TMA16 && POST) {
+      if (tmC == nullptr || p.residual == nullptr) return;
+      const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
+      const int col0 = nbk * BN + half * CPW * 32;
+      if (row >= p.M || col0 >= p.N) return;
+      const uint32_t bytes = (uint32_t)(min(CPW * 32, p.N - col0) * 2) & ~15u;
+      if (bytes) bulk_prefetch_l2(reinterpret_cast<const uint16_t*>(p.residual) + (int64_t)row * p.ld_res + col0, bytes);
+    }
+  };
   if (first_tile < num_tiles) {
     int mb, nb_;
     tile_coords(first_tile, num_m, num_n, mb, nb_);
+    prefetch_res(mb, nb_);
     epi_load_params<BN, EPI, OUT_DT>(p, nb_ * BN, e, nws, nb);
     const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
     if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
-    if (e < BN) { es->ws[0][e] = nws; es->bias[0][e] = nb; }
+    load_gate(mb, nb_, ngate, ngok);
+    if (e < BN) { es->ws[0][e] = nws; es->bias[0][e] = nb; es->gate[0][e] = ngate; }
+    if (e == 0) es->gate_ok[0] = ngok;
+    if constexpr (TMA16 && POST) {
+      if (tmC != nullptr && p.residual != nullptr) load_res32<OUT_DT>(p, row, nb_ * BN + half * CPW * 32, res);
+    }
   }
   for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
     int mb, nbk;
@@ -473,15 +772,31 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
     if (*abort_flag) break;
     tc_fence_after();
     const int next = tile + tile_stride;
+    int nrow = -1, ncol0 = 0;
     if (next < num_tiles) {
       int mb2, nb2;
       tile_coords(next, num_m, num_n, mb2, nb2);
       epi_load_params<BN, EPI, OUT_DT>(p, nb2 * BN, e, nws, nb);
       const int row = mb2 * ROWS_PER_TILE + row_off + quarter * 32 + lane;
       if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+      load_gate(mb2, nb2, ngate, ngok);
+      prefetch_res(mb2, nb2);
+      nrow = row;
+      ncol0 = nb2 * BN + half * CPW * 32;
     }
-    epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter, half,
-                                   lane, es->ws[buf], es->bias[buf], xs, tmC, stage);
+    bool done = false;
+    if constexpr (TMA16) {
+      if (tmC != nullptr) {
+        epilogue_tile_tma<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter,
+                                           half, lane, es->ws[buf], es->bias[buf],
+                                           es->gate_ok[buf] ? es->gate[buf] : nullptr, xs, tmC, stage, stc, res,
+                                           nrow, ncol0);
+        done = true;
+      }
+    }
+    if (!done)
+      epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter,
+                                             half, lane, es->ws[buf], es->bias[buf], xs, tmC, stage);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
@@ -492,7 +807,8 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       }
     }
     buf ^= 1;
-    if (next < num_tiles && e < BN) { es->ws[buf][e] = nws; es->bias[buf][e] = nb; }
+    if (next < num_tiles && e < BN) { es->ws[buf][e] = nws; es->bias[buf][e] = nb; es->gate[buf][e] = ngate; }
+    if (next < num_tiles && e == 0) es->gate_ok[buf] = ngok;
     acc ^= 1;
     if (acc == 0) acc_phase ^= 1;
   }
@@ -660,13 +976,14 @@ template <int EPI, int OUT_DT>
 struct PairCfg {
   static constexpr int BN = 256;           // tile columns (both CTAs)
   static constexpr int BNH = 128;          // B rows loaded per CTA
-  static constexpr int STAGES = 6;
+  // 16-bit outputs leave through TMA stores staged per epilogue warp (two
+  // 2 KB buffers each); the operand ring gives up a stage for them
+  static constexpr bool TMA_ST = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
+  static constexpr int STAGES = TMA_ST ? 5 : 6;
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
   static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
-  // 16-bit outputs leave through TMA stores staged per epilogue warp
-  static constexpr bool TMA_ST = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
-  static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * EPI_STAGE_BYTES : 0;
+  static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * 2 * EPI_STAGE_BYTES : 0;
   static constexpr int SMEM_BYTES =
       1024 + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 + 16 + sizeof(EpiSmem<BN>);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -786,7 +1103,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
     epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
                                                       num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
                                                       lane, tma_st ? &tmC : nullptr,
-                                                      sC + (warp - 2) * EPI_STAGE_BYTES);
+                                                      sC + (warp - 2) * 2 * EPI_STAGE_BYTES);
   }
 
   tc_fence_before();

@@ -191,8 +191,11 @@ QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t*
  *   y = dt(residual + dt(gate[g, n] * y))      if residual; without gate dt(residual + y)
  * with g = row / rows_per_gate (<= 0: one gate row; gate rows
  * 0 .. (M-1)/rows_per_gate must exist), residual [M, ld_res] and gate rows
- * gate_ld elements apart, both in out_dtype, 16-byte aligned rows.  gelu_tanh is F.gelu(approximate="tanh") as PyTorch's CUDA kernel
- * evaluates it in float32 (inner sum as one FMA, CUDA tanhf).
+ * gate_ld elements apart, both in out_dtype, 16-byte aligned rows.
+ * gelu_tanh is F.gelu(approximate="tanh"), 0.5 y (1 + tanh(u)), evaluated
+ * as the equal y * sigmoid(2u) in float32 with the special-function unit's
+ * exp2 and reciprocal: within one unit of out_dtype of the exact function
+ * (eager PyTorch's tanh form loses accuracy where 1 + tanh(u) cancels).
  * Replaces: the kitchen residual form residual + residual_scale * linear(x)
  * (rocm_int8_kitchen_patch.py:176) and a DiT block's gated residual
  * x + gate * linear(h) / GELU after Int8TensorwiseOps.Linear. */

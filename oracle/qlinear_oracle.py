@@ -600,16 +600,17 @@ def norm_quant_int8(x, dtype: str, rot=None, **kw):
 
 
 def gelu_tanh(x: np.ndarray) -> np.ndarray:
-    """float32 ``0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))`` in the
-    expression order of ``F.gelu(approximate="tanh")`` on CUDA (inner sum as
-    one fused multiply-add).  numpy's tanh is not CUDA's: near ``1 + tanh ->
-    0`` a 1-ulp difference of tanh shows in the bf16 result (about 0.5% of
-    values differ by 1 ulp from either torch kernel)."""
-    x = np.asarray(x, F32)
-    x3 = ((x * x).astype(F32) * x).astype(F32)
-    fma = (GELU_KAPPA.astype(np.float64) * x3 + x).astype(F32)
-    inner = (GELU_BETA * fma).astype(F32)
-    return ((F32(0.5) * x).astype(F32) * (F32(1.0) + np.tanh(inner).astype(F32)).astype(F32)).astype(F32)
+    """The tanh-form GELU ``0.5 x (1 + tanh(u))``, ``u = sqrt(2/pi) (x +
+    0.044715 x^3)`` (``F.gelu(approximate="tanh")``), evaluated exactly in
+    float64 as the equal ``x / (1 + exp(-2u))`` and rounded once to float32.
+    Kernels are held within one unit of the 16-bit dtype of this value;
+    eager PyTorch's float32 tanh form differs from it by more where
+    ``1 + tanh(u)`` cancels (x < -3, values below 2^-20 there)."""
+    x64 = np.asarray(x, F32).astype(np.float64)
+    u = np.sqrt(2.0 / np.pi) * (x64 + 0.044715 * x64 ** 3)
+    with np.errstate(over="ignore", invalid="ignore"):
+        y = x64 / (1.0 + np.exp(-2.0 * u))
+    return y.astype(F32)
 
 
 def linear_post(y, dtype: str, gelu_from=None, residual=None, gate=None, rows_per_gate=None) -> np.ndarray:

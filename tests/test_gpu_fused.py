@@ -223,28 +223,31 @@ def test_gemm_residual_gate_exact(P, dt, M, N, K, G, per_row):
 @pytest.mark.parametrize("M,N,K,gelu_from", [(512, 1024, 256, 0), (384, 1280, 512, 768), (64, 512, 256, 0),
                                              (4096, 12288, 3072, 0)])
 def test_gemm_gelu(P, dt, M, N, K, gelu_from):
-    """GELU in the epilogue equals eager ``F.gelu(y, approximate="tanh")`` on
-    the GPU bit for bit (same float32 expression, CUDA tanhf); against the
-    numpy oracle one unit of the dtype (or 2^-20 absolute where tanh
-    saturates) on <= 5% of the GELU'd outputs (numpy's tanh)."""
+    """GELU in the epilogue against the exact function (the oracle, float64):
+    one unit of the dtype relative, or 2^-20 absolute, on every output and
+    a different value on <= 1% of them; against eager ``F.gelu(y,
+    approximate="tanh")`` on the GPU within the same bound (its float32
+    tanh form cancels below x = -3, where all values are under 2^-20)."""
     rng = np.random.default_rng(N + gelu_from)
     a, w, xs, ws, b = _gemm_case(rng, M, N, K, dt)
     y = P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), dev(b, dt), TDT[dt], gelu_from=gelu_from)
     plain = P.ops.gemm_w8a8(dev(a), dev(xs), dev(w), dev(ws), dev(b, dt), TDT[dt])
-    eager = plain.clone()
-    eager[:, gelu_from:] = F.gelu(plain[:, gelu_from:], approximate="tanh")
-    assert torch.equal(y, eager)
+    unit = 2.0 ** -7 if dt == "bf16" else 2.0 ** -10
+    eager = F.gelu(plain[:, gelu_from:], approximate="tanh").float()
+    ge = y[:, gelu_from:].float()
+    assert torch.all((ge - eager).abs() <= torch.clamp(eager.abs() * unit, min=2.0 ** -20))
+    assert torch.equal(y[:, :gelu_from], plain[:, :gelu_from])
     ref = O.linear_post(plain.float().cpu().numpy(), dt, gelu_from=gelu_from)
     yo = y.float().cpu().numpy()
     np.testing.assert_array_equal(yo[:, :gelu_from], ref[:, :gelu_from])
     g, r = yo[:, gelu_from:], ref[:, gelu_from:]
-    unit = 2.0 ** -7 if dt == "bf16" else 2.0 ** -10
     assert (np.abs(g - r) <= np.maximum(np.abs(r) * unit, 2.0 ** -20)).all()
-    assert (g != r).mean() <= 0.05
+    assert (g != r).mean() <= 0.01
 
 
 def test_gemm_gelu_then_residual(P):
-    """Both steps: residual + gate * gelu(y) (order of the epilogue)."""
+    """Both steps: residual + gate * gelu(y) (order of the epilogue), against
+    the oracle with the exact GELU."""
     rng = np.random.default_rng(9)
     M, N, K = 512, 512, 256
     a, w, xs, ws, b = _gemm_case(rng, M, N, K, "bf16")
@@ -253,9 +256,12 @@ def test_gemm_gelu_then_residual(P):
     y = P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16, gelu_from=0,
                               residual=dev(res, "bf16"), gate=dev(gate, "bf16"))
     plain = P.ops.gemm_w8a8(dev(a), dev(xs), dev(w), dev(ws), dev(b, "bf16"), torch.bfloat16)
-    g = dev(gate, "bf16")
-    eager = dev(res, "bf16") + torch.repeat_interleave(g, M // 2, 0) * F.gelu(plain, approximate="tanh")
-    assert torch.equal(y, eager)
+    ref = O.linear_post(plain.float().cpu().numpy(), "bf16", gelu_from=0, residual=res, gate=gate, rows_per_gate=M // 2)
+    yo = y.float().cpu().numpy()
+    # a GELU value one unit off moves gate * gelu by one unit of it, which
+    # the residual add may round to one unit of the sum
+    assert (np.abs(yo - ref) <= np.maximum(np.abs(ref), np.abs(res)) * 2.0 ** -7 + 2.0 ** -20).all()
+    assert (yo != ref).mean() <= 0.01
 
 
 def test_gemm_fused_strided_gate_and_errors(P):
