@@ -497,9 +497,10 @@ __device__ __forceinline__ void rnd_pairs(float (&y)[32]) {
 // (already waited for) -> the reference's epilogue -> EPI_POST steps ->
 // 16-bit values staged in `sb` (64-byte TMA swizzle) -> one TMA store.
 // `g32`: the tile's gate row staged in shared memory, or null (per-row gate
-// loads).  Bulk stores are double-buffered per warp: before `sb` is written,
-// every store but the most recent one (which used the other buffer) has
-// read its source.
+// loads).  With EPI_POST the bulk stores are double-buffered per warp:
+// before `sb` is written, every store but the most recent one (which used
+// the other buffer) has read its source; otherwise one buffer, free once the
+// previous store has read it.
 template <int EPI, int OUT_DT>
 __device__ __forceinline__ void epi_chunk_tma(const GemmParams& p, const uint32_t (&r)[32], const uint4 (&rv)[4],
                                               const float* ws32, const float* b32, const float* g32, float xs,
@@ -601,7 +602,10 @@ __device__ __forceinline__ void epi_chunk_tma(const GemmParams& p, const uint32_
       w[j] = *reinterpret_cast<uint32_t*>(&h);
     }
   }
-  if (lane == 0) bulk_wait_read_1();  // the store two chunks back (same buffer) has read it
+  if (lane == 0) {
+    if constexpr (POST) bulk_wait_read_1();  // the store two chunks back (same buffer) has read it
+    else bulk_wait_read_all();               // one buffer: the previous store has read it
+  }
   __syncwarp();
 #pragma unroll
   for (int k = 0; k < 4; ++k)
@@ -616,9 +620,9 @@ __device__ __forceinline__ void epi_chunk_tma(const GemmParams& p, const uint32_
 }
 
 // Epilogue of one 128-row accumulator tile for 16-bit outputs leaving
-// through TMA stores (one destination).  Stores alternate between the
-// warp's two staging buffers (`stc` counts this warp's stores across tiles
-// and picks the buffer).  Without EPI_POST the warp's CPW chunks are
+// through TMA stores (one destination).  With EPI_POST, stores alternate
+// between the warp's two staging buffers (`stc` counts this warp's stores
+// across tiles and picks the buffer).  Without EPI_POST the warp's CPW chunks are
 // software pipelined: the TMEM load of chunk c+1 is in flight while chunk c
 // is converted and stored.  With EPI_POST (register budget: one accumulator
 // chunk at a time) the residual loads of chunk c+1 are in flight instead;
@@ -679,7 +683,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, uint32_t 
     tmem_ld_32x32b_x32(tmem_acc + (c0 + cc + 1) * 32 + lane_off, rb);
     if (quarter_live && colA < p.N) {
       epi_chunk_tma<EPI, OUT_DT>(p, ra, res, s_ws + (c0 + cc) * 32, s_b + (c0 + cc) * 32, nullptr, xs, s_tensor,
-                                 has_bias, row, row_base, colA, lane, tmC, stage + (stc & 1) * EPI_STAGE_BYTES);
+                                 has_bias, row, row_base, colA, lane, tmC, stage);
       ++stc;
     }
     tmem_ld_wait_regs(rb);
@@ -687,7 +691,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, uint32_t 
     if (quarter_live && colB < p.N) {
       epi_chunk_tma<EPI, OUT_DT>(p, rb, res, s_ws + (c0 + cc + 1) * 32, s_b + (c0 + cc + 1) * 32, nullptr, xs,
                                  s_tensor, has_bias, row, row_base, colB, lane, tmC,
-                                 stage + (stc & 1) * EPI_STAGE_BYTES);
+                                 stage);
       ++stc;
     }
   }
@@ -976,14 +980,16 @@ template <int EPI, int OUT_DT>
 struct PairCfg {
   static constexpr int BN = 256;           // tile columns (both CTAs)
   static constexpr int BNH = 128;          // B rows loaded per CTA
-  // 16-bit outputs leave through TMA stores staged per epilogue warp (two
-  // 2 KB buffers each); the operand ring gives up a stage for them
+  // 16-bit outputs leave through TMA stores staged per epilogue warp in 2 KB
+  // buffers: one, or two with the EPI_POST steps (whose longer epilogue
+  // overlaps a store with the next chunk; the operand ring gives up a stage)
   static constexpr bool TMA_ST = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
-  static constexpr int STAGES = TMA_ST ? 5 : 6;
+  static constexpr int EPI_BUFS = (EPI & EPI_POST) ? 2 : 1;
+  static constexpr int STAGES = (TMA_ST && EPI_BUFS == 2) ? 5 : 6;
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
   static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * 2 * EPI_STAGE_BYTES : 0;
+  static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * EPI_BUFS * EPI_STAGE_BYTES : 0;
   static constexpr int SMEM_BYTES =
       1024 + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 + 16 + sizeof(EpiSmem<BN>);
   static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -1103,7 +1109,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
     epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
                                                       num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
                                                       lane, tma_st ? &tmC : nullptr,
-                                                      sC + (warp - 2) * 2 * EPI_STAGE_BYTES);
+                                                      sC + (warp - 2) * Cfg::EPI_BUFS * EPI_STAGE_BYTES);
   }
 
   tc_fence_before();
