@@ -455,6 +455,98 @@ def dit_cpu_baseline():
 
 
 # ---------------------------------------------------------------------------
+# The other linear configurations, timed kernel by kernel (L2 flushed before
+# every launch, median of CFG_ITERS): the ConvRot W8A8 linear over its whole
+# shape grid, the group-128 W4A8 and W4A4 linears, and the reference's own
+# row-wise W4A4 ConvRot linear.
+# ---------------------------------------------------------------------------
+CFG_ITERS, CFG_WARM = 9, 2
+
+
+def _cfg_time(fn, flush):
+    ts = []
+    for i in range(CFG_WARM + CFG_ITERS):
+        flush.zero_()
+        torch.cuda._sleep(200_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= CFG_WARM:
+            ts.append(e0.elapsed_time(e1) * 1e3)
+    return statistics.median(ts)
+
+
+def run_configs(pkg, dev, int8_peak):
+    ops = pkg.ops
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    gen = torch.Generator(device=dev)
+
+    def rnd(shape, scale=1.0, seed=0):
+        gen.manual_seed(seed)
+        return torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * scale
+
+    def entry(Mv, Nv, Kv, us_gemm, us_quant):
+        tops = 2.0 * Mv * Nv * Kv / (us_gemm * 1e-6) / 1e12
+        return {"M": Mv, "N": Nv, "K": Kv, "gemm_us": round(us_gemm, 1), "gemm_tops": round(tops, 1),
+                "frac": round(tops / int8_peak, 3), "quant_us": round(us_quant, 1)}
+
+    out = {"timing": f"CUDA events per kernel, L2 flushed before each launch, median of {CFG_ITERS}",
+           "peak_tops": round(int8_peak, 1)}
+    rot = ("sylvester", 128)
+    sweep = []
+    for Mv in (1024, 4096, 8192):
+        x = (rnd((Mv, 12288), seed=Mv)).to(torch.bfloat16)
+        for Kv in (3072, 12288):
+            xk = x[:, :Kv].contiguous()
+            for Nv in (3072, 9216, 12288):
+                wq, ws = ops.quant_weight_int8(rnd((Nv, Kv), 0.02, seed=Nv + Kv), rot)
+                b = rnd((Nv,), 0.01, seed=3).to(torch.bfloat16)
+                xq, xs = ops.quant_act_int8(xk, rot)
+                tq = _cfg_time(lambda: ops.quant_act_int8(xk, rot), flush)
+                tg = _cfg_time(lambda: ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16), flush)
+                sweep.append(entry(Mv, Nv, Kv, tg, tq))
+                del wq, ws, b, xq, xs
+            del xk
+        del x
+    out["convrot_w8a8_sylvester128"] = sweep
+    out["convrot_w8a8_min_frac"] = min(e["frac"] for e in sweep)
+    # group-128 W4A8: per-token int8 activations, sym int4 weights (bf16 group scales)
+    Mv, Nv, Kv = 4096, 12288, 3072
+    x = rnd((Mv, Kv), seed=2).to(torch.bfloat16)
+    pw, psc = ops.quant_weight_int4(rnd((Nv, Kv), 0.02, seed=21).to(torch.bfloat16), None, 128)
+    b = rnd((Nv,), 0.01, seed=22).to(torch.bfloat16)
+    xq, xs = ops.quant_act_int8(x, None)
+    tq = _cfg_time(lambda: ops.quant_act_int8(x, None), flush)
+    tg = _cfg_time(lambda: ops.gemm_w4_g128(xq, xs, pw, psc, b, torch.bfloat16), flush)
+    out["w4a8_g128"] = entry(Mv, Nv, Kv, tg, tq)
+    # group-128 W4A4 with ConvRot (Sylvester 128) on both operands
+    w4a4 = []
+    xr = rnd((Mv, Kv), seed=3).to(torch.bfloat16)
+    for Nv in (3072, 12288):
+        pw, psc = ops.quant_weight_int4(rnd((Nv, Kv), 0.02, seed=31 + Nv).to(torch.bfloat16), rot, 128)
+        b = rnd((Nv,), 0.01, seed=32).to(torch.bfloat16)
+        aq, asc = ops.quant_act_int4(xr, rot, 128)
+        tq = _cfg_time(lambda: ops.quant_act_int4(xr, rot, 128), flush)
+        tg = _cfg_time(lambda: ops.gemm_w4_g128(aq, asc, pw, psc, b, torch.bfloat16, a_int4_groups=True), flush)
+        w4a4.append(entry(Mv, Nv, Kv, tg, tq))
+    out["w4a4_g128_sylvester128"] = w4a4
+    # the reference's own row-wise W4A4 ConvRot format (regular Hadamard 256)
+    Nv = 12288
+    rrot = ("regular", 256)
+    pw, psc = ops.quant_weight_int4(rnd((Nv, Kv), 0.02, seed=41), rrot, 0)
+    b = rnd((Nv,), 0.01, seed=42).to(torch.bfloat16)
+    aq, asc = ops.quant_act_int4(xr, rrot, 0)
+    tq = _cfg_time(lambda: ops.quant_act_int4(xr, rrot, 0), flush)
+    tg = _cfg_time(lambda: ops.gemm_w4a4(aq, asc, pw, psc, b, torch.bfloat16), flush)
+    out["w4a4_row_regular256"] = entry(Mv, Nv, Kv, tg, tq)
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Tensor-parallel latency mode (N > 1): one column-parallel ConvRot W8A8
 # linear over a single sample's tokens, fused GEMM + all-gather vs the GEMM
 # followed by an NCCL all-gather.
@@ -623,6 +715,7 @@ def run_ours(args):
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
     del x, b, wq, ws, xq, xs, y, flush, x_host, y_host, xd
     torch.cuda.empty_cache()
+    cfgs = run_configs(pkg, dev, int8_peak) if (rank == 0 and not args.no_configs) else None
     dit = run_dit(pkg, dev, world, rank) if not args.no_dit else {"skipped": "--no-dit"}
     tpres = run_tp(pkg, dev, world, rank) if world > 1 else None
     if rank == 0 and world == 1 and not args.no_dit:
@@ -651,6 +744,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
             "dit": dit,
+            "configs": cfgs,
             "tensor_parallel": tpres,
             "clocks": clk.summary(),
         }
@@ -666,6 +760,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-dit", action="store_true", help="skip the MMDiT step measurement")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration kernel timings")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
