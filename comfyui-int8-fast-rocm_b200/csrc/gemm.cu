@@ -264,6 +264,15 @@ int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, cons
 
 namespace {
 
+// QLIN_G128_NO_PAIR=1 forces the single-CTA group-128 kernel (comparison runs).
+bool g128_pair_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_G128_NO_PAIR");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
 template <int MODE, int OUT_DT>
 int launch_g128_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const G128Params& p, int sms, cudaStream_t stream) {
   auto kern = gemm_g128_kernel<MODE, OUT_DT>;
@@ -285,9 +294,45 @@ int launch_g128_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const G128Para
   return QLIN_OK;
 }
 
+template <int MODE, int OUT_DT>
+int launch_g128_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const G128Params& p,
+                         int sms, cudaStream_t stream) {
+  auto kern = gemm_g128_pair_kernel<MODE, OUT_DT>;
+  static std::atomic<uint64_t> attr_devices{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  cudaError_t e;
+  if (!(attr_devices.load() & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G128PairCfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm g128 pair)");
+    attr_devices.fetch_or(bit);
+  }
+  const int num_tiles = ((p.M + 2 * G128PairCfg::BM - 1) / (2 * G128PairCfg::BM)) *
+                        ((p.N + G128PairCfg::BN - 1) / G128PairCfg::BN);
+  const int clusters = num_tiles < sms / 2 ? num_tiles : sms / 2;
+  kern<<<2 * clusters, G128PairCfg::NUM_THREADS, G128PairCfg::SMEM_BYTES, stream>>>(ta, tb, tc, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm g128 pair launch");
+  return QLIN_OK;
+}
+
 template <int MODE>
-int dispatch_g128(int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const G128Params& p, int sms,
-                  cudaStream_t s) {
+int dispatch_g128(int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* w_packed,
+                  const G128Params& p, int sms, cudaStream_t s) {
+  // 16-bit outputs with 16-byte aligned rows: the CTA-pair kernel (TMA-store epilogue)
+  if ((out_dt == DT_BF16 || out_dt == DT_F16) && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+      (p.ldo * 2) % 16 == 0 && !g128_pair_disabled()) {
+    CUtensorMap tc, tb2;  // the pair loads 64 packed weight rows per CTA
+    int rc = make_tmap(&tc, p.out, (uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.ldo * 2, 32, 32,
+                       CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    if (rc) return rc;
+    rc = make_tmap(&tb2, w_packed, (uint64_t)(p.K / 2), (uint64_t)p.N, (uint64_t)(p.K / 2), G128PairCfg::BK / 2,
+                   G128PairCfg::BNH, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    if (out_dt == DT_BF16) return launch_g128_pair_cfg<MODE, DT_BF16>(ta, tb2, tc, p, sms, s);
+    return launch_g128_pair_cfg<MODE, DT_F16>(ta, tb2, tc, p, sms, s);
+  }
   if (out_dt == DT_BF16) return launch_g128_cfg<MODE, DT_BF16>(ta, tb, p, sms, s);
   if (out_dt == DT_F16) return launch_g128_cfg<MODE, DT_F16>(ta, tb, p, sms, s);
   if (out_dt == DT_F32) return launch_g128_cfg<MODE, DT_F32>(ta, tb, p, sms, s);
@@ -319,8 +364,8 @@ int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, 
   p.bias = bias;
   p.out = out;
   p.ldo = N;
-  if (a_int4_groups) return dispatch_g128<G128_W4A4>(out_dt, ta, tb, p, sms, stream);
-  return dispatch_g128<G128_W4A8>(out_dt, ta, tb, p, sms, stream);
+  if (a_int4_groups) return dispatch_g128<G128_W4A4>(out_dt, ta, tb, w_packed, p, sms, stream);
+  return dispatch_g128<G128_W4A8>(out_dt, ta, tb, w_packed, p, sms, stream);
 }
 
 int read_device_error(cudaStream_t stream, uint32_t* bits) {
