@@ -394,6 +394,52 @@ def run_dit(pkg, dev, world, rank):
                 torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             times[name] = float(t.item())
             outs[name] = out
+    # The fused step captured once in a CUDA graph and replayed (the same
+    # kernels without host launch gaps; reported beside the eager step,
+    # which is the headline).  Every rank takes
+    # the same collective steps (a failed capture on any rank skips the
+    # graph timing on all of them).
+    graph_ms, graph_equal, graph_note = None, None, None
+    with torch.no_grad():
+        graph, out_g, ok = None, None, 1.0
+        try:
+            step = variants["fused"]
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                step()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out_g = step()
+            graph.replay()
+            torch.cuda.synchronize()
+        except Exception as exc:  # reported in the line, eager numbers stand
+            graph_note = f"capture failed: {type(exc).__name__}: {exc}"[:200]
+            ok = 0.0
+            torch.cuda.synchronize()
+        flag = torch.tensor([ok], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+        if flag.item() > 0:
+            if world > 1:
+                torch.distributed.barrier()
+            s = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(DIT_STEPS):
+                graph.replay()
+            e1.record(s)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / DIT_STEPS], device=dev, dtype=torch.float64)
+            if world > 1:
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            graph_ms = float(t.item())
+            graph_equal = bool(torch.equal(out_g, outs["fused"]))
+        elif graph_note is None:
+            graph_note = "capture failed on another rank"
+        del graph, out_g
     ms = times["fused"]
     out = outs["fused"]
     ref = outs["unfused"].float()
@@ -411,7 +457,10 @@ def run_dit(pkg, dev, world, rank):
            "samples_per_rank": per_rank, "scaling": "strong", "steps": DIT_STEPS, "warmup": DIT_WARMUP,
            "int8_tops_in_step": round(ops_step / (ms * 1e-3) / 1e12, 1), "finite_output": finite,
            "fusions": "LayerNorm + modulation in the activation quantiser, GELU and gated residual in the GEMM "
-                      "epilogue (int8_quant.int8_forward_fused)",
+                      "epilogue, q/k RMSNorm + rotary in place on the qkv output, linear2 input read from its two "
+                      "parts (int8_quant.int8_forward_fused, ops.qk_norm_rope_)",
+           "graph_ms_per_step": None if graph_ms is None else round(graph_ms, 2), "graph_note": graph_note,
+           "graph_output_equals_eager": graph_equal,
            "unfused_ms_per_step": round(times["unfused"], 2),
            "unfused_steps_per_s": round(1000.0 / times["unfused"], 4),
            "rel_l2_diff_vs_unfused": round(rel_diff, 6)}
