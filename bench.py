@@ -467,6 +467,46 @@ def run_dit(pkg, dev, world, rank):
     return res
 
 
+def dit_breakdown(n_double=2, n_single=4):
+    """Kernel-time breakdown of the fused DiT forward on a reduced block
+    count (torch profiler, CUDA activity), printed as a table."""
+    from torch.profiler import ProfilerActivity, profile
+    pkg = load_pkg()
+    ops = pkg.ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rot = (DIT["kind"], DIT["group"])
+    params = _dit_params(dev, lambda w: ops.quant_weight_int8(w, rot), n_double, n_single)
+    _, fl = dit_linears(pkg, rot)
+    img, txt, vec = dit_inputs(DIT["samples"], dev, DIT["seed"])
+    step = lambda: dit_forward_fused(params, img, txt, vec, fl, ops.qk_norm_rope_)
+    with torch.no_grad():
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 3
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+    rows = []
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", 0) or getattr(e, "cuda_time_total", 0)
+        if t > 0:
+            rows.append((t, e.count, e.key))
+    rows.sort(reverse=True)
+    tot = sum(r[0] for r in rows)
+    print(f"fused forward: {ms:.2f} ms ({n_double} double + {n_single} single blocks, {DIT['samples']} samples); "
+          f"profiled kernel time {tot / 1e3:.2f} ms")
+    for t, c, k in rows[:14]:
+        print(f"{100 * t / tot:5.1f}%  {t / 1e3:8.2f} ms  x{c:4d}  {k[:100]}")
+
+
 def dit_cpu_baseline():
     """One double and one single block for one sample through the
     reference's PyTorch CPU linear, extrapolated to the full model and the
@@ -527,7 +567,7 @@ def _cfg_time(fn, flush):
     return statistics.median(ts)
 
 
-def run_configs(pkg, dev, int8_peak):
+def run_configs(pkg, dev, int8_peak, which="all"):
     ops = pkg.ops
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     gen = torch.Generator(device=dev)
@@ -545,7 +585,7 @@ def run_configs(pkg, dev, int8_peak):
            "peak_tops": round(int8_peak, 1)}
     rot = ("sylvester", 128)
     sweep = []
-    for Mv in (1024, 4096, 8192):
+    for Mv in ((1024, 4096, 8192) if which == "all" else ()):
         x = (rnd((Mv, 12288), seed=Mv)).to(torch.bfloat16)
         for Kv in (3072, 12288):
             xk = x[:, :Kv].contiguous()
@@ -559,8 +599,9 @@ def run_configs(pkg, dev, int8_peak):
                 del wq, ws, b, xq, xs
             del xk
         del x
-    out["convrot_w8a8_sylvester128"] = sweep
-    out["convrot_w8a8_min_frac"] = min(e["frac"] for e in sweep)
+    if sweep:
+        out["convrot_w8a8_sylvester128"] = sweep
+        out["convrot_w8a8_min_frac"] = min(e["frac"] for e in sweep)
     # group-128 W4A8: per-token int8 activations, sym int4 weights (bf16 group scales)
     Mv, Nv, Kv = 4096, 12288, 3072
     x = rnd((Mv, Kv), seed=2).to(torch.bfloat16)
@@ -581,6 +622,8 @@ def run_configs(pkg, dev, int8_peak):
         tg = _cfg_time(lambda: ops.gemm_w4_g128(aq, asc, pw, psc, b, torch.bfloat16, a_int4_groups=True), flush)
         w4a4.append(entry(Mv, Nv, Kv, tg, tq))
     out["w4a4_g128_sylvester128"] = w4a4
+    if which != "all":
+        return out
     # the reference's own row-wise W4A4 ConvRot format (regular Hadamard 256)
     Nv = 12288
     rrot = ("regular", 256)
@@ -764,7 +807,8 @@ def run_ours(args):
     cpu = cpu_baseline() if (rank == 0 and world == 1) else None
     del x, b, wq, ws, xq, xs, y, flush, x_host, y_host, xd
     torch.cuda.empty_cache()
-    cfgs = run_configs(pkg, dev, int8_peak) if (rank == 0 and not args.no_configs) else None
+    cfgs = run_configs(pkg, dev, int8_peak, args.kernel_configs) \
+        if (rank == 0 and args.kernel_configs != "none") else None
     dit = run_dit(pkg, dev, world, rank) if not args.no_dit else {"skipped": "--no-dit"}
     tpres = run_tp(pkg, dev, world, rank) if world > 1 else None
     if rank == 0 and world == 1 and not args.no_dit:
@@ -809,9 +853,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-dit", action="store_true", help="skip the MMDiT step measurement")
-    ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration kernel timings")
+    ap.add_argument("--kernel-configs", choices=["all", "group128", "none"], default="all",
+                    help="per-configuration kernel timings: all, only the group-128 GEMMs, or none")
+    ap.add_argument("--dit-breakdown", action="store_true",
+                    help="print a kernel-time breakdown of the fused DiT forward (2 double + 4 single blocks, "
+                         "16 samples, torch profiler) and exit")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.dit_breakdown:
+        dit_breakdown()
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
