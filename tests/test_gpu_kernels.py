@@ -344,6 +344,46 @@ def test_w4a4_vs_oracle(P, dt):
     np.testing.assert_array_equal(tbits(y), bits(dt, yo))
 
 
+def _w4a4_case(seed, M, N, K, with_bias, dt):
+    rng = np.random.default_rng(seed)
+    qa = rng.integers(-8, 8, (M, K), dtype=np.int8)
+    wn = rng.integers(-8, 8, (N, K), dtype=np.int8)
+    sa = (rng.random(M) * 0.02 + 1e-3).astype(np.float32)
+    ws = (rng.random(N) * 0.02 + 1e-3).astype(np.float32)
+    b = O.rnd(dt, rng.standard_normal(N).astype(np.float32)) if with_bias else None
+    return qa, wn, sa, ws, b
+
+
+# Row-wise W4A4 GEMM on ragged M, N and K tails (partial tiles in every
+# dimension, a K tail inside one 128-deep step), every output dtype, rows
+# that are not 16-byte aligned (N = 1028 in bf16), with and without bias
+@pytest.mark.parametrize("M,N,K,with_bias,dt", [(513, 264, 160, True, "bf16"), (256, 256, 128, False, "f16"),
+                                                 (600, 1000, 1024, True, "f32"), (1024, 3072, 3072, True, "bf16"),
+                                                 (300, 1028, 384, True, "bf16"), (255, 640, 512, True, "bf16"),
+                                                 (700, 200, 256, False, "f16")])
+def test_w4a4_rowwise_shapes(P, M, N, K, with_bias, dt):
+    qa, wn, sa, ws, b = _w4a4_case(M + N + K, M, N, K, with_bias, dt)
+    pw = O.pack_int4_row_major(wn)
+    y = P.ops.gemm_w4a4(dev(qa), torch.from_numpy(sa).cuda(), dev(pw), torch.from_numpy(ws).cuda(),
+                        None if b is None else dev(b, dt), TDT[dt])
+    yo = O.w4a4_rowwise_epilogue(O.int_mm(qa, wn), sa, ws, b, dt)
+    np.testing.assert_array_equal(tbits(y), bits(dt, yo))
+    assert P.ops.device_error() == 0
+
+
+def test_w4a4_rowwise_full_size_rows(P):
+    # Packed-INT4 W4A4 linear, M=4096 N=12288 K=3072, seed 5: whole GEMM on
+    # the GPU, oracle on a sample of rows (rows are independent)
+    M, N, K = 4096, 12288, 3072
+    qa, wn, sa, ws, b = _w4a4_case(5, M, N, K, True, "bf16")
+    pw = O.pack_int4_row_major(wn)
+    y = P.ops.gemm_w4a4(dev(qa), torch.from_numpy(sa).cuda(), dev(pw), torch.from_numpy(ws).cuda(), dev(b, "bf16"),
+                        torch.bfloat16)
+    rows = _rows_sample(M, seed=2)
+    yo = O.w4a4_rowwise_epilogue(O.int_mm(qa[rows], wn), sa[rows], ws, b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
 # ---------------------------------------------------------------------------
 # (c) group-128 int4-weight GEMMs (W4A8, W4A4)
 # ---------------------------------------------------------------------------
