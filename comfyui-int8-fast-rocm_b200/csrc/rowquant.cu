@@ -122,7 +122,12 @@ int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s,
 // (without launching) when two ring slots do not fit in shared memory; the
 // caller then uses the register-prefetch kernel.
 constexpr size_t kX2SmemBudget = 200 * 1024;  // hard limit (one CTA)
-constexpr size_t kX2SmemTarget = 72 * 1024;   // keeps three CTAs per SM
+// Ring target: four or five CTAs per SM for 3072-element bf16 rows.  The
+// ring gives up depth for CTAs, so the bytes in flight per SM stay about
+// the same.  Measured against a
+// 72 KB target (three CTAs per SM): 16384 x 3072 Sylvester-128 in 52 vs
+// 56 us; 4096 x 3072 and 8192 x 12288 unchanged.
+constexpr size_t kX2SmemTarget = 48 * 1024;
 
 template <int DT, int KIND, int R, int CHUNKS, bool FUSED>
 int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {

@@ -623,7 +623,7 @@ __device__ __forceinline__ float row_sum(float x, float (*buf)[17], int lane, in
 template <int DT, int KIND, int R, int CHUNKS, bool FUSED = false>
 __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int stages, int slot_bytes) {
   extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ float red[2][32][33];
+  __shared__ float red[2][32][17];  // [iteration parity][row][warp]: <= 512 threads, so <= 16 warps per row
   constexpr int EB = DT == DT_F32 ? 4 : 2;  // element bytes
   constexpr bool STAGED = KIND != ROT_NONE && R > 1;
 
@@ -875,7 +875,7 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const int nw = tpr >> 5;
-    float (*rb)[33] = red[it & 1];
+    float (*rb)[17] = red[it & 1];
     if (lane == 0) rb[threadIdx.y][warp_in_row] = amax;
     if (__syncthreads_or(!ok)) break;  // a bulk copy never arrived: leave together
     if (tid == 0) {
