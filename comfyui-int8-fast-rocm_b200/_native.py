@@ -40,6 +40,7 @@ SIGNATURES = {
     "qlin_quant_act_int4": [_P, _I, _L, _L, _L, _I, _I, _F, _I, _F, _P, _P, _P],
     "qlin_rotate": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P],
     "qlin_situ": [_P, _I, _L, _L, _L, _P, _P],
+    "qlin_quant_act_int8_situ": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_gemm_w8a8": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _P],
     "qlin_gemm_w8a8_fused": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _L, _P, _L, _P, _L, _L, _P],
     "qlin_gemm_w8a8_allgather": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _I, _L, _L, _L, _P],

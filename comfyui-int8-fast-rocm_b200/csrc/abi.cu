@@ -174,6 +174,21 @@ QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int
                                q, scale, static_cast<cudaStream_t>(stream));
 }
 
+QLIN_API int qlin_quant_act_int8_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
+                                      int rot_group, float rot_c, int8_t* q, float* scale, void* stream) {
+  if (M < 0 || K < 0 || ldx < 2 * K) return fail(QLIN_ERR_INVALID_ARG, "bad shape (rows are [hidden | gate], ldx >= 2K)");
+  if (x_dtype != QLIN_BF16 && x_dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16 or F16");
+  if (M == 0 || K == 0) return QLIN_OK;
+  if (!x || !q || !scale) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if ((rc = check_rot(rot_kind, rot_group, K))) return rc;
+  if (K % 16 != 0 || !rows_vec_ok(x, 2 * K, ldx, x_dtype) || !aligned16(q))
+    return fail(QLIN_ERR_ALIGNMENT, "the SiTU prologue needs K % 16 == 0 and 16-byte aligned rows");
+  return launch_rowquant_situ(x_dtype, rot_kind, rot_kind == QLIN_ROT_NONE ? 0 : rot_group, rot_c, x, ldx, M, K, q,
+                              scale, static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_quant_act_int8_cat(const void* x1, int64_t ld1, int64_t K1, const void* x2, int64_t ld2,
                                      int64_t K2, int x_dtype, int64_t M, int rot_kind, int rot_group, float rot_c,
                                      int8_t* q, float* scale, void* stream) {

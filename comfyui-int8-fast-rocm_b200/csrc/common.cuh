@@ -390,4 +390,27 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// SiTU gated activation (int8_fused_kernel.py:389-421), float32 math with
+// every step an explicit round-to-nearest operation, so the standalone
+// kernel and the quantiser prologue that share it produce identical values.
+// tanh without overflow: (1 - e^-2|x|) / (1 + e^-2|x|) with the sign
+// restored, and the odd Taylor polynomial x(1 - x^2(1/3 - 2x^2/15)) below
+// |x| = 0.02 where the quotient cancels (int8_fused_kernel.py:390-399).
+__device__ __forceinline__ float situ_tanh(float x) {
+  const float ax = fabsf(x);
+  const float t = expf(__fmul_rn(-2.0f, ax));
+  float big = __fdiv_rn(__fsub_rn(1.0f, t), __fadd_rn(1.0f, t));
+  big = x < 0.0f ? -big : big;
+  const float x2 = __fmul_rn(x, x);
+  const float inner = __fsub_rn(1.0f / 3.0f, __fmul_rn(x2, 2.0f / 15.0f));
+  const float small = __fmul_rn(x, __fsub_rn(1.0f, __fmul_rn(x2, inner)));
+  return ax < 0.02f ? small : big;
+}
+// out = 4 tanh(g/4) * sigmoid(g) * 25 tanh(h/25)  (int8_fused_kernel.py:403-421)
+__device__ __forceinline__ float situ_f(float h, float g) {
+  const float gate_cap = __fmul_rn(4.0f, situ_tanh(__fmul_rn(g, 0.25f)));
+  const float hidden_cap = __fmul_rn(25.0f, situ_tanh(__fdiv_rn(h, 25.0f)));
+  return __fmul_rn(__fdiv_rn(gate_cap, __fadd_rn(1.0f, expf(-g))), hidden_cap);
+}
+
 }  // namespace qlin

@@ -46,6 +46,9 @@ struct FusedPrologue {
 int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
                           int64_t K, const FusedPrologue& f, int8_t* q, float* scale, cudaStream_t stream);
 
+int launch_rowquant_situ(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
+                         int64_t K, int8_t* q, float* scale, cudaStream_t stream);
+
 int launch_rowquant_cat(int dt, int rot_kind, int rot_group, float rot_c, const void* x1, int64_t ld1, int64_t K1,
                         const void* x2, int64_t ld2, int64_t K2, int64_t M, int8_t* q, float* scale,
                         cudaStream_t stream);

@@ -124,9 +124,8 @@ int by_mode(int mode, RotCode rc, const RowQuantParams& p, const LaunchShape& s,
 constexpr size_t kX2SmemBudget = 200 * 1024;  // hard limit (one CTA)
 // Ring target: four or five CTAs per SM for 3072-element bf16 rows.  The
 // ring gives up depth for CTAs, so the bytes in flight per SM stay about
-// the same.  Measured against a
-// 72 KB target (three CTAs per SM): 16384 x 3072 Sylvester-128 in 52 vs
-// 56 us; 4096 x 3072 and 8192 x 12288 unchanged.
+// the same.  Measured against a 72 KB target (three CTAs per SM): 16384 x
+// 3072 Sylvester-128 in 52 vs 56 us; 4096 x 3072 and 8192 x 12288 unchanged.
 constexpr size_t kX2SmemTarget = 48 * 1024;
 
 template <int DT, int KIND, int R, int CHUNKS, bool FUSED>
@@ -138,7 +137,7 @@ int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
   int rpc = 256 / tpr;
   if (rpc < 1) rpc = 1;
   if (rpc > 32) rpc = 32;
-  const size_t row_bytes = (size_t)p.K * EB;
+  const size_t row_bytes = (size_t)p.K * EB * (FUSED && p.situ ? 2 : 1);  // source bytes per ring row
   const int slot_bytes = (int)(((size_t)rpc * row_bytes + 127) / 128 * 128);
   const size_t tbuf = (KIND != ROT_NONE && R > 1) ? (size_t)(rpc * tpr / 32) * 512 * sizeof(float) : 0;
   int stages = 4;
@@ -296,6 +295,36 @@ int launch_rowquant_fused(int dt, int rot_kind, int rot_group, float rot_c, cons
   else if (dt == DT_F16) r = x2_by_chunks<DT_F16, true>(rc, p, (int)nchunks, stream);
   else return fail(QLIN_ERR_UNSUPPORTED, "the fused norm prologue takes bf16 or f16 input");
   if (r == QLIN_ERR_UNSUPPORTED) return fail(QLIN_ERR_UNSUPPORTED, "row too long for the fused norm prologue");
+  return r;
+}
+
+// Per-token int8 quantisation of the SiTU activation of [hidden | gate] rows
+// (16-bit inputs, K % 16 == 0, ldx >= 2K, 16-byte aligned rows: checked by
+// the caller): the fused kernel with the SiTU prologue and no norm.
+int launch_rowquant_situ(int dt, int rot_kind, int rot_group, float rot_c, const void* x, int64_t ldx, int64_t M,
+                         int64_t K, int8_t* q, float* scale, cudaStream_t stream) {
+  if (M == 0 || K == 0) return QLIN_OK;
+  RowQuantParams p{};
+  p.x = x;
+  p.ldx = ldx;
+  p.M = (int)M;
+  p.K = (int)K;
+  p.rot_c = rot_c;
+  p.q = q;
+  p.scale = scale;
+  p.one = 1.0f;
+  p.norm_kind = NORM_NONE;
+  p.rows_per_sample = M;
+  p.situ = 1;
+  const RotCode rc = rot_code(rot_kind, rot_kind == 0 ? 0 : rot_group);
+  if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
+  const int64_t nchunks = K / 16;
+  if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  int r = QLIN_ERR_UNSUPPORTED;
+  if (dt == DT_BF16) r = x2_by_chunks<DT_BF16, true>(rc, p, (int)nchunks, stream);
+  else if (dt == DT_F16) r = x2_by_chunks<DT_F16, true>(rc, p, (int)nchunks, stream);
+  else return fail(QLIN_ERR_UNSUPPORTED, "the SiTU prologue takes bf16 or f16 input");
+  if (r == QLIN_ERR_UNSUPPORTED) return fail(QLIN_ERR_UNSUPPORTED, "row too long for the SiTU prologue");
   return r;
 }
 

@@ -59,6 +59,10 @@ struct RowQuantParams {
   const void* x2;
   int64_t ldx2;
   int k1;
+  // SiTU prologue of rowquant_x2_kernel<..., FUSED = true>: source row r is
+  // [hidden[r, 0:K] | gate[r, 0:K]] (x, ldx >= 2K elements); the row
+  // quantised is dt(situ_f(hidden, gate))
+  int situ;
 };
 
 enum : int {
@@ -619,7 +623,9 @@ __device__ __forceinline__ float row_sum(float x, float (*buf)[17], int lane, in
 //
 // FUSED: the row norm and the modulation of a DiT block run on the row in
 // registers before the rotation (two extra CTA barriers per row for the
-// layer norm's mean and variance, one for the RMS norm).
+// layer norm's mean and variance, one for the RMS norm); or (p.situ) the
+// SiTU activation of a [hidden | gate] source row, whose ring slot holds
+// both halves.
 template <int DT, int KIND, int R, int CHUNKS, bool FUSED = false>
 __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int stages, int slot_bytes) {
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -637,6 +643,7 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
   const int nwarps = (tpr >> 5) * rpc;
   const int warp_lin = threadIdx.y * (tpr >> 5) + warp_in_row;
   const int row_bytes = p.K * EB;
+  const int src_bytes = (FUSED && p.situ) ? 2 * row_bytes : row_bytes;  // per ring row
   uint8_t* ring = dsm;
   float* wbuf = reinterpret_cast<float*>(dsm + (size_t)stages * slot_bytes) + warp_lin * 512;
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + (size_t)stages * slot_bytes +
@@ -668,24 +675,24 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
 
   // fill slot s with the rows of iteration `it` (thread 0 only)
   const bool two_src = p.x2 != nullptr;
-  const bool dense = !two_src && (int64_t)p.ldx * EB == row_bytes;
-  const int bytes1 = two_src ? p.k1 * EB : row_bytes;  // 16-byte multiple (checked by the host)
+  const bool dense = !two_src && (int64_t)p.ldx * EB == src_bytes;
+  const int bytes1 = two_src ? p.k1 * EB : src_bytes;  // 16-byte multiple (checked by the host)
   auto issue = [&](int it, int s) {
     const int64_t f = ((int64_t)blockIdx.x + (int64_t)it * gridDim.x) * rpc;
     if (f >= p.M) return;
     const int nrows = (int)min((int64_t)rpc, (int64_t)p.M - f);
-    mbar_arrive_expect_tx(&full[s], (uint32_t)(nrows * row_bytes));
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(nrows * src_bytes));
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x);
     uint8_t* dst = ring + (size_t)s * slot_bytes;
     if (dense) {
-      bulk_load(dst, src + f * row_bytes, (uint32_t)(nrows * row_bytes), &full[s]);
+      bulk_load(dst, src + f * src_bytes, (uint32_t)(nrows * src_bytes), &full[s]);
     } else {
       for (int r = 0; r < nrows; ++r) {
-        bulk_load(dst + (size_t)r * row_bytes, src + (f + r) * (int64_t)p.ldx * EB, (uint32_t)bytes1, &full[s]);
+        bulk_load(dst + (size_t)r * src_bytes, src + (f + r) * (int64_t)p.ldx * EB, (uint32_t)bytes1, &full[s]);
         if (two_src)
-          bulk_load(dst + (size_t)r * row_bytes + bytes1,
+          bulk_load(dst + (size_t)r * src_bytes + bytes1,
                     reinterpret_cast<const uint8_t*>(p.x2) + (f + r) * (int64_t)p.ldx2 * EB,
-                    (uint32_t)(row_bytes - bytes1), &full[s]);
+                    (uint32_t)(src_bytes - bytes1), &full[s]);
       }
     }
   };
@@ -700,7 +707,7 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
     const bool ok = rq_wait_bounded(&full[s], parity);
     const int64_t row = first + threadIdx.y;
     const bool row_ok = row < p.M && ok;
-    const uint8_t* rsrc = ring + (size_t)s * slot_bytes + (size_t)threadIdx.y * row_bytes;
+    const uint8_t* rsrc = ring + (size_t)s * slot_bytes + (size_t)threadIdx.y * src_bytes;
     float2 v[CHUNKS][8];
 #pragma unroll
     for (int i = 0; i < CHUNKS; ++i) {
@@ -714,6 +721,21 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
           raw.w[4 * k] = w.x; raw.w[4 * k + 1] = w.y; raw.w[4 * k + 2] = w.z; raw.w[4 * k + 3] = w.w;
         }
         unpack_raw2<DT>(raw, v[i]);
+        if constexpr (FUSED) {
+          if (p.situ) {  // v holds the hidden chunk; its gate chunk sits K elements on
+            const uint4* qg = reinterpret_cast<const uint4*>(rsrc + row_bytes + (size_t)ci * 16 * EB);
+#pragma unroll
+            for (int k = 0; k < RawChunk<DT>::WORDS / 4; ++k) {
+              const uint4 w = qg[k];
+              raw.w[4 * k] = w.x; raw.w[4 * k + 1] = w.y; raw.w[4 * k + 2] = w.z; raw.w[4 * k + 3] = w.w;
+            }
+            float2 g[8];
+            unpack_raw2<DT>(raw, g);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              v[i][j] = round2<DT>(make_float2(situ_f(v[i][j].x, g[j].x), situ_f(v[i][j].y, g[j].y)));
+          }
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = make_float2(0.0f, 0.0f);

@@ -72,22 +72,8 @@ __global__ void __launch_bounds__(1024) requant_asym_w4a8_kernel(const uint8_t* 
   *reinterpret_cast<uint4*>(q + (int64_t)n * K + t * 16) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// tanh without overflow: (1 - e^-2|x|) / (1 + e^-2|x|) with the sign
-// restored, and the odd Taylor polynomial x(1 - x^2(1/3 - 2x^2/15)) below
-// |x| = 0.02 where the quotient cancels (int8_fused_kernel.py:390-399).
-__device__ __forceinline__ float situ_tanh(float x) {
-  const float ax = fabsf(x);
-  const float t = expf(-2.0f * ax);
-  float big = (1.0f - t) / (1.0f + t);
-  big = x < 0.0f ? -big : big;
-  const float x2 = x * x;
-  const float small = x * (1.0f - x2 * (1.0f / 3.0f - x2 * (2.0f / 15.0f)));
-  return ax < 0.02f ? small : big;
-}
-
 // SiTU gated activation on [hidden | gate] rows (int8_fused_kernel.py:403-421):
-// out = 4 tanh(g/4) * sigmoid(g) * 25 tanh(h/25), float32 math, one element
-// per thread.
+// out = situ_f(h, g), one element per thread.
 template <int DT>
 __global__ void __launch_bounds__(256) situ_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
                                                    void* __restrict__ y) {
@@ -100,10 +86,7 @@ __global__ void __launch_bounds__(256) situ_kernel(const void* __restrict__ x, i
   const T* xr = reinterpret_cast<const T*>(x) + row * ldx;
   const float h = E::to_f(xr[col]);
   const float g = E::to_f(xr[K + col]);
-  const float gate_cap = 4.0f * situ_tanh(g / 4.0f);
-  const float hidden_cap = 25.0f * situ_tanh(h / 25.0f);
-  const float out = gate_cap / (1.0f + expf(-g)) * hidden_cap;
-  reinterpret_cast<T*>(y)[row * K + col] = E::from_f(out);
+  reinterpret_cast<T*>(y)[row * K + col] = E::from_f(situ_f(h, g));
 }
 
 }  // namespace

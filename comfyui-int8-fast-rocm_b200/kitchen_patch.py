@@ -68,18 +68,24 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
                 out_dtype: torch.dtype = torch.bfloat16, convrot: bool = False, convrot_groupsize: int = 256,
                 input_act=None, input_act_weight=None, input_act_eps: float = 0.0, residual=None,
                 residual_scale=None) -> torch.Tensor:
-    if input_act == "situ":
+    # SiTU of 16-bit rows of 16-element multiples runs inside the activation
+    # quantiser (bit-equal to ops.situ followed by ops.quant_act_int8)
+    fuse_situ = (input_act == "situ" and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
+                 and x.shape[-1] % 32 == 0)
+    if input_act == "situ" and not fuse_situ:
         x = ops.situ(x)
+    if input_act == "situ":
         input_act = None
+    k_in = x.shape[-1] // 2 if fuse_situ else x.shape[-1]
     fuse_rms = _fusable_rms(x, input_act, input_act_weight)
-    if fuse_rms:
+    if fuse_rms or fuse_situ:
         pass  # applied inside the activation quantiser below
     elif ck_quant is not None:
         x = ck_quant._apply_input_act(x, input_act, input_act_weight, input_act_eps)
     elif input_act is not None:
         raise ValueError(f"input_act={input_act!r} needs comfy_kitchen")
-    if x.shape[-1] != weight.shape[-1]:
-        raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {weight.shape[-1]}")
+    if k_in != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {k_in} and {weight.shape[-1]}")
     weight = weight.to(device=x.device).contiguous()
     weight_scale = weight_scale.to(device=x.device, dtype=torch.float32).reshape(-1)
     if weight_scale.numel() not in (1, weight.shape[0]):
@@ -87,12 +93,14 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
                          f"for weight shape {tuple(weight.shape)}")
     rot = None
     if convrot:
-        if x.shape[-1] % convrot_groupsize != 0:
-            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide input features {x.shape[-1]}")
+        if k_in % convrot_groupsize != 0:
+            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide input features {k_in}")
         rot = rot_for_group(convrot_groupsize)
-    shape = x.shape
-    x2 = x.reshape(-1, shape[-1])
-    if fuse_rms:
+    shape = (*x.shape[:-1], k_in)
+    x2 = x.reshape(-1, x.shape[-1])
+    if fuse_situ:
+        xq, xs = ops.quant_act_int8_situ(x2, rot)
+    elif fuse_rms:
         xq, xs = ops.quant_act_int8_norm(x2, rot, "rms", float(input_act_eps), input_act_weight)
     else:
         xq, xs = ops.quant_act_int8(x2, rot)

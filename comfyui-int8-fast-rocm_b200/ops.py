@@ -190,6 +190,30 @@ def quant_act_int8_cat(x1: torch.Tensor, x2: torch.Tensor, rot=None):
     return q, s
 
 
+def quant_act_int8_situ(x: torch.Tensor, rot=None):
+    """Per-token int8 of ``situ(x)`` for ``x`` [M, 2K] = [hidden | gate]
+    (bf16/f16, K % 16 == 0; row-strided views are read in place) without
+    writing the [M, K] activation: bit-equal to
+    ``quant_act_int8(situ(x), rot)``.  Returns (q int8 [M, K], scale
+    float32 [M, 1])."""
+    if x.dim() != 2 or x.shape[1] % 2:
+        raise ValueError(f"expected [M, 2K] rows ([hidden | gate]), got {tuple(x.shape)}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"the SiTU prologue takes bf16 or f16 input, got {x.dtype}")
+    x2, ldx = _rows(x)
+    M, K = x2.shape[0], x2.shape[1] // 2
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    if M == 0 or K == 0:
+        return q, s
+    if x2.data_ptr() % 16 or (ldx * x2.element_size()) % 16:
+        x2, ldx = x2.contiguous().clone(), 2 * K
+    kind, g, c = _rot_args(rot, x.dtype)
+    N.call("qlin_quant_act_int8_situ", x2.data_ptr(), dtype_code(x.dtype), M, K, ldx, kind, g, c, q.data_ptr(),
+           s.data_ptr(), _stream(x2))
+    return q, s
+
+
 def qk_norm_rope_(qkv: torch.Tensor, heads: int, head_dim: int, q_weight=None, k_weight=None, eps: float = 1e-6,
                   cos=None, sin=None) -> torch.Tensor:
     """In place on the fused qkv projection ``qkv`` [..., L, >= 3*heads*head_dim]

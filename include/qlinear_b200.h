@@ -169,6 +169,18 @@ QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64
  * rocm_int8_linear (rocm_int8_kitchen_patch.py:131-133). */
 QLIN_API int qlin_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, void* out, void* stream);
 
+/* qlin_situ followed by qlin_quant_act_int8 in one kernel: row r of the
+ * quantised input is dt(situ(hidden[r], gate[r])) for x[M, 2K] =
+ * [hidden | gate] (row stride ldx >= 2K), optionally rotated; the [M, K]
+ * activation is never written to memory.  Codes and scales are bit-equal
+ * to the two-call sequence.  x_dtype BF16 or F16; K a multiple of 16
+ * (K <= 32768); x and the row stride 16-byte aligned; q [M, K], scale [M].
+ * Replaces the input_act="situ" prologue plus the activation quantisation
+ * of rocm_int8_linear (rocm_int8_kitchen_patch.py:131-171;
+ * int8_fused_kernel.py:389-440 then :23-85). */
+QLIN_API int qlin_quant_act_int8_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
+                                      int rot_group, float rot_c, int8_t* q, float* scale, void* stream);
+
 /* ---- (b) W8A8 GEMM on tcgen05 kind::i8 ------------------------------------ */
 
 /* out[M,N] = epilogue( a[M,K] int8 . w[N,K]^T int8 ) with int32 accumulation.

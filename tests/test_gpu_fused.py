@@ -308,3 +308,93 @@ def test_dit_blocks_fused_match_unfused(P, monkeypatch):
         b = bench.dit_forward(params, img, txt, vec, lin).float()
     assert torch.isfinite(a).all()
     assert ((a - b).norm() / b.norm()).item() <= 1e-2
+
+
+# ---------------------------------------------------------------------------
+# SiTU prologue of the activation quantiser (qlin_quant_act_int8_situ)
+# ---------------------------------------------------------------------------
+
+SITU_ROTS = [None, ("regular", 256), ("sylvester", 128), ("regular", 16)]
+
+
+def situ_rows(rng, M, K, pad, dt):
+    x = rng.standard_normal((M, 2 * K + pad)).astype(np.float32) * 3
+    x[0, :8] = 1e-3              # the small-|x| tanh branch
+    x[-1, K:K + 8] = -40.0        # sigmoid(gate) underflows towards 0
+    return x
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("rot", SITU_ROTS)
+@pytest.mark.parametrize("M,K,pad", [(37, 3072, 0), (5, 256, 64), (130, 1024, 16), (3, 12288, 0), (64, 512, 0)])
+def test_situ_quant_matches_two_calls(P, dt, rot, M, K, pad):
+    """Bit-equal to ops.situ followed by ops.quant_act_int8 (the same
+    device SiTU function, then the same rotation and quantisation); rows
+    read in place from a wider buffer when pad > 0."""
+    if rot is not None and K % rot[1]:
+        pytest.skip("row length not a multiple of the rotation block")
+    rng = np.random.default_rng(M + K + pad)
+    full = dev(situ_rows(rng, M, K, pad, dt), dt)
+    x = full[:, :2 * K]
+    q, s = P.ops.quant_act_int8_situ(x, rot)
+    q_ref, s_ref = P.ops.quant_act_int8(P.ops.situ(x), rot)
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref)
+    assert torch.equal(s.view(torch.int32), s_ref.view(torch.int32))
+    assert P.ops.device_error() == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_situ_quant_vs_float64(P, dt):
+    """Against a float64 SiTU rounded once to the dtype, then the oracle's
+    quantisation: scales within one dtype unit of the row maximum / 127,
+    codes within one step."""
+    rng = np.random.default_rng(11)
+    M, K = 48, 1024
+    x = O.rnd(dt, situ_rows(rng, M, K, 0, dt))
+    q, s = P.ops.quant_act_int8_situ(dev(x, dt), None)
+    x64 = x.astype(np.float64)
+    h, g = x64[:, :K], x64[:, K:]
+    y = O.rnd(dt, (4 * np.tanh(g / 4) / (1 + np.exp(-g)) * 25 * np.tanh(h / 25)).astype(np.float32))
+    qo, so = O.quantize_int8_axiswise(y, dim=-1)
+    sg = s.cpu().numpy().reshape(-1)
+    unit = 2.0 ** (-7 if dt == "bf16" else -10)
+    assert np.all(np.abs(sg - so.reshape(-1)) <= unit * so.reshape(-1) + 1e-30)
+    assert np.abs(q.cpu().numpy().astype(np.int32) - qo.astype(np.int32)).max() <= 1
+
+
+def test_situ_quant_errors(P):
+    x = torch.zeros((4, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        P.ops.quant_act_int8_situ(x.float(), None)   # float32 rows: not taken by the prologue
+    with pytest.raises(ValueError):
+        P.ops.quant_act_int8_situ(x[:, :63], None)   # odd row: no [hidden | gate] split
+    st = torch.cuda.current_stream().cuda_stream
+    q = torch.empty((4, 24), dtype=torch.int8, device="cuda")
+    s = torch.empty((4,), dtype=torch.float32, device="cuda")
+    with pytest.raises(P._native.NativeError):      # K = 24: not a multiple of 16
+        P._native.call("qlin_quant_act_int8_situ", x.data_ptr(), 0, 4, 24, 64, 0, 0, 0.0, q.data_ptr(),
+                       s.data_ptr(), st)
+    with pytest.raises(P._native.NativeError):      # ldx < 2K
+        P._native.call("qlin_quant_act_int8_situ", x.data_ptr(), 0, 4, 48, 64, 0, 0, 0.0, q.data_ptr(),
+                       s.data_ptr(), st)
+    q0, s0 = P.ops.quant_act_int8_situ(x[:0], None)
+    assert q0.shape == (0, 32) and s0.shape == (0, 1)
+
+
+@pytest.mark.parametrize("convrot", [False, True])
+def test_kitchen_int8_linear_situ_fused(P, convrot):
+    """kitchen_patch.int8_linear with input_act="situ": the fused quantiser
+    path equals the two-call path (situ, then the linear without it)."""
+    kp = P.kitchen_patch
+    rng = np.random.default_rng(5)
+    B, L, K, N = 2, 40, 1024, 384
+    x = dev(rng.standard_normal((B, L, 2 * K)).astype(np.float32) * 2, "bf16")
+    w = torch.from_numpy(rng.standard_normal((N, K)).astype(np.float32) * 0.02).cuda()
+    rot = P.int8_quant.rot_for_group(256) if convrot else None
+    wq, ws = P.ops.quant_weight_int8(w, rot)
+    b = dev(rng.standard_normal(N).astype(np.float32) * 0.1, "bf16")
+    y = kp.int8_linear(x, wq, ws, b, torch.bfloat16, convrot=convrot, convrot_groupsize=256, input_act="situ")
+    y_ref = kp.int8_linear(P.ops.situ(x), wq, ws, b, torch.bfloat16, convrot=convrot, convrot_groupsize=256)
+    assert y.shape == (B, L, N)
+    assert torch.equal(y, y_ref)
