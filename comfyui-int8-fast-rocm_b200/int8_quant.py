@@ -534,16 +534,31 @@ if _COMFY_OPS_AVAILABLE:
                     x_2d = x_2d.to(compute_dtype)
                 rot = rot_for_group(self._convrot_groupsize) if self._use_convrot else None
 
-                if self._is_per_row:
+                patches = self.lora_patches
+                if (len(patches) == 1 and patches[0][2] is None
+                        and compute_dtype in (torch.bfloat16, torch.float16)):
+                    # one full-width dynamic LoRA: y + lora_y.to(y.dtype) is the
+                    # GEMM epilogue's residual step (dt(y + residual), one
+                    # rounding at the store), so the sum is bit-equal to the
+                    # eager add and y is written once
+                    lora_down, lora_up = patches[0][0], patches[0][1]
+                    x_l = ops.rotate(x_2d, *rot) if rot is not None else x_2d
+                    lD = lora_down.to(x.device, non_blocking=True)
+                    lU = lora_up.to(x.device, non_blocking=True)
+                    lora_y = F.linear(F.linear(x_l.to(lD.dtype), lD), lU).to(compute_dtype)
+                    y = int8_forward_fused(x_2d, weight, w_scale, bias, compute_dtype, rot,
+                                           per_row=self._is_per_row, residual=lora_y)
+                    patches = []
+                elif self._is_per_row:
                     y = int8_forward_dynamic_per_row(x_2d, weight, w_scale, bias, compute_dtype, rot)
                 else:
                     y = int8_forward_dynamic(x_2d, weight, w_scale, bias, compute_dtype, rot)
 
-                if self.lora_patches:
+                if patches:
                     # dynamic LoRA (int8_quant.py:718-729): down-projection of
                     # the (rotated) activation, up-projection, added to y
                     x_l = ops.rotate(x_2d, *rot) if rot is not None else x_2d
-                    for lora_down, lora_up, lora_start, lora_size in self.lora_patches:
+                    for lora_down, lora_up, lora_start, lora_size in patches:
                         lD = lora_down.to(x.device, non_blocking=True)
                         lU = lora_up.to(x.device, non_blocking=True)
                         lora_y = F.linear(F.linear(x_l.to(lD.dtype), lD), lU)

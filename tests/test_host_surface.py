@@ -210,3 +210,45 @@ def test_int4_linear_forward(C, golden):
     y = lin(torch.from_numpy(x).to(torch.bfloat16).cuda())
     got = y.cpu().view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(got, golden["i4fwd_y"])
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")
+@pytest.mark.parametrize("convrot", [False, True])
+def test_int8_linear_dynamic_lora_fused_add(C, convrot):
+    """One full-width dynamic LoRA runs its add in the GEMM epilogue: equal
+    to the eager ``y + lora_y.to(y.dtype)`` (int8_quant.py:718-729); a
+    sliced patch (split qkv) and two patches keep the eager form and agree
+    with it too."""
+    Ops = C.Int8TensorwiseOps
+    Ops.dynamic_quantize, Ops.enable_convrot, Ops.excluded_names = True, convrot, []
+    Ops.compute_dtype = None
+    K, N, r = 512, 384, 16
+    lin = Ops.Linear(K, N)
+    w = gi.weight(41, N, K)
+    b = gi.bias(41, N, "bf16")
+    sd = {"l.weight": torch.from_numpy(w).to(torch.bfloat16), "l.bias": torch.from_numpy(b).to(torch.bfloat16)}
+    lin._load_from_state_dict(sd, "l.", {}, True, [], [], [])
+    x = torch.from_numpy(gi.activation(41, 2 * 40, K, "bf16")).reshape(2, 40, K).to(torch.bfloat16).cuda()
+    g = torch.Generator().manual_seed(3)
+    lD = (torch.randn((r, K), generator=g) * 0.05).to(torch.bfloat16)
+    lU = (torch.randn((N, r), generator=g) * 0.05).to(torch.bfloat16)
+    lU2 = (torch.randn((128, r), generator=g) * 0.05).to(torch.bfloat16)
+    lin.lora_patches = []
+    y0 = lin(x).reshape(-1, N)
+    x2 = x.reshape(-1, K)
+    xl = C.ops.rotate(x2, *C.int8_quant.rot_for_group(256)) if convrot else x2
+
+    def up(d, u):
+        return torch.nn.functional.linear(torch.nn.functional.linear(xl, d.cuda()), u.cuda()).to(torch.bfloat16)
+
+    lin.lora_patches = [(lD, lU, None, None)]
+    assert torch.equal(lin(x).reshape(-1, N), y0 + up(lD, lU))
+    lin.lora_patches = [(lD, lU2, 128, 128)]
+    ref = y0.clone()
+    ref[:, 128:256] = ref[:, 128:256] + up(lD, lU2)
+    assert torch.equal(lin(x).reshape(-1, N), ref)
+    lin.lora_patches = [(lD, lU, None, None), (lD, lU, None, None)]
+    assert torch.equal(lin(x).reshape(-1, N), (y0 + up(lD, lU)) + up(lD, lU))
+    lin.lora_patches = []
+    Ops.dynamic_quantize, Ops.enable_convrot = False, False
