@@ -844,34 +844,22 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
             }
 #pragma unroll
             for (int jj = 0; jj < J / 2; ++jj) xform_regs2<KIND, R>(w[jj]);
+            // the chunk stays in this transposed layout (element 2jj + c of
+            // run r is v[i][jj * R + r].{x,y}); only its int8 codes go back
+            // to the natural order, after the row scale is known
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
+            for (int jj = 0; jj < J / 2; ++jj)
 #pragma unroll
-              for (int q = 0; q < NQ; ++q) {
-                if constexpr (J2 == 4) {
-                  *reinterpret_cast<float4*>(wbuf + s2[r][q]) =
-                      make_float4(w[2 * q][r].x, w[2 * q][r].y, w[2 * q + 1][r].x, w[2 * q + 1][r].y);
-                } else {
-                  *reinterpret_cast<float2*>(wbuf + s2[r][q]) = w[0][r];
-                }
-              }
-            }
+              for (int r = 0; r < R; ++r) v[i][jj * R + r] = w[jj][r];
           } else {
             float w[R];
 #pragma unroll
             for (int r = 0; r < R; ++r) w[r] = wbuf[s2[r][0]];
             xform_regs<KIND, R>(w);
 #pragma unroll
-            for (int r = 0; r < R; ++r) wbuf[s2[r][0]] = w[r];
+            for (int r = 0; r < R; r += 2) v[i][r / 2] = make_float2(w[r], w[r + 1]);
           }
-          __syncwarp();
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 f = *reinterpret_cast<const float4*>(wbuf + nat[q4]);
-            v[i][2 * q4] = make_float2(f.x, f.y);
-            v[i][2 * q4 + 1] = make_float2(f.z, f.w);
-          }
-          __syncwarp();
+          __syncwarp();  // the gathers are done before the next chunk's stores
         }
         // normalise with the dtype-rounded constant, round to the compute dtype
 #pragma unroll
@@ -930,6 +918,49 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
     const float2 inv2 = make_float2(inv, inv);
     const float2 one2 = make_float2(p.one, p.one);
     const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    if constexpr (STAGED) {
+      // Run r of this lane's transposed chunk is the J elements at offset
+      // g0 + 16 r + rp J of the warp's 512-element span (the lane's rotation
+      // group starts at g0).  Their codes are stored there in a byte image
+      // of the span (16-byte segment index XOR-ed with the 128-byte row, so
+      // a store instruction and the 16-byte natural reads hit distinct
+      // banks); each lane then reads its own natural chunk back.
+      uint8_t* cb = reinterpret_cast<uint8_t*>(wbuf);
+      const int base = (lane / R) * (16 * R) + (lane % R) * J;
+      auto cswz = [](int a) { return a ^ (((a >> 7) & 7) << 4); };
+#pragma unroll
+      for (int i = 0; i < CHUNKS; ++i) {
+        int c[16];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float2 y = f2_fma(f2_mul(v[i][j], inv2), one2, magic);
+          c[2 * j] = (int)__float_as_uint(y.x);
+          c[2 * j + 1] = (int)__float_as_uint(y.y);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          uint8_t* d = cb + cswz(base + 16 * r);
+          if constexpr (J == 1) {
+            *d = (uint8_t)c[r];
+          } else if constexpr (J == 2) {
+            *reinterpret_cast<uint16_t*>(d) = (uint16_t)__byte_perm((uint32_t)c[2 * r], (uint32_t)c[2 * r + 1], 0x0040);
+          } else if constexpr (J == 4) {
+            *reinterpret_cast<uint32_t*>(d) = pack4(c[2 * r], c[2 * r + 1], c[2 * (R + r)], c[2 * (R + r) + 1]);
+          } else {
+            static_assert(J == 8, "runs of 1, 2, 4 or 8 elements");
+            *reinterpret_cast<uint2*>(d) =
+                make_uint2(pack4(c[2 * r], c[2 * r + 1], c[2 * (R + r)], c[2 * (R + r) + 1]),
+                           pack4(c[2 * (2 * R + r)], c[2 * (2 * R + r) + 1], c[2 * (3 * R + r)], c[2 * (3 * R + r) + 1]));
+          }
+        }
+        __syncwarp();
+        const uint4 o = *reinterpret_cast<const uint4*>(cb + cswz(16 * lane));
+        __syncwarp();  // read before the next chunk's (or row's) stores
+        const int ci = t + i * tpr;
+        if (ci < nchunks) *reinterpret_cast<uint4*>(qrow + (int64_t)ci * 16) = o;
+      }
+      continue;
+    }
 #pragma unroll
     for (int i = 0; i < CHUNKS; ++i) {
       const int ci = t + i * tpr;
