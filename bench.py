@@ -38,7 +38,7 @@ SEED = 1
 CPU_SAMPLE_ROWS = 4096  # the whole batch: the CPU sample is bounded by time instead
 # dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch at this
 # workload, from the ncu capture summarised in profiles/ (None until taken).
-GEMM_TRAFFIC_BYTES = 146699776  # ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/gemm_i8_pair_w8a8_4096x12288x3072.md)
+GEMM_TRAFFIC_BYTES = 146699776  # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM
 
 
 def load_pkg():

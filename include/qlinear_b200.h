@@ -6,7 +6,7 @@
  * kernels are Triton functions called from PyTorch.  Each entry point below
  * replaces one of them (or one PyTorch expression on the hot path); the
  * comment on each cites the reference interface it replaces.  The Python
- * package binds these with ctypes (INTEGRATION.md shows the binding).
+ * package binds these with ctypes (_native.py).
  *
  * Conventions
  *  - All pointers are device pointers unless stated otherwise; matrices are
@@ -16,8 +16,8 @@
  *  - The device is the calling thread's current CUDA device.
  *  - Every function returns QLIN_OK (0) or a QLIN_ERR_* code and never throws;
  *    qlin_last_error() returns a thread-local message for the last failure.
- *  - Numerics follow the reference's PyTorch CPU path bit for bit (see
- *    DESIGN.md for the exact rounding order of every epilogue).
+ *  - Numerics follow the reference's PyTorch CPU path bit for bit; each
+ *    GEMM entry point below states its epilogue's rounding order.
  */
 #ifndef QLINEAR_B200_H
 #define QLINEAR_B200_H

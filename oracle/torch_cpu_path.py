@@ -1,5 +1,5 @@
 """The reference's PyTorch CPU branch of the W8A8 ConvRot linear, restated
-with the same torch calls -- TEST / BASELINE INFRASTRUCTURE ONLY.
+with the same torch calls -- TEST AND CPU-REFERENCE-ARM INFRASTRUCTURE ONLY.
 
 This is what the reference runs when the activation is on the CPU
 (int8_quant.py:148-164 with rotate_activation, convrot.py:89-118, and

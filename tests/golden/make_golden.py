@@ -100,7 +100,7 @@ def main(ref_dir):
         out[f"q8_{dt}_q"] = q.numpy()
         out[f"q8_{dt}_s"] = s.numpy()
 
-    # 1b. configs[0]-scale activation quant (digests)
+    # 1b. activation quant at 4096 x 3072 (digests)
     x = gi.activation(0, 4096, 3072, "bf16")
     q, s = i8.quantize_int8_axiswise(T(x, torch.bfloat16), dim=-1)
     out["q8_c0_q_sha"] = np.array(sha(q.numpy()))
