@@ -959,25 +959,25 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
         const int ci = t + i * tpr;
         if (ci < nchunks) *reinterpret_cast<uint4*>(qrow + (int64_t)ci * 16) = o;
       }
-      continue;
-    }
+    } else {
 #pragma unroll
-    for (int i = 0; i < CHUNKS; ++i) {
-      const int ci = t + i * tpr;
-      if (ci >= nchunks) continue;
-      uint32_t u[16];
+      for (int i = 0; i < CHUNKS; ++i) {
+        const int ci = t + i * tpr;
+        if (ci >= nchunks) continue;
+        uint32_t u[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float2 y = f2_fma(f2_mul(v[i][j], inv2), one2, magic);
-        u[2 * j] = __float_as_uint(y.x);
-        u[2 * j + 1] = __float_as_uint(y.y);
+        for (int j = 0; j < 8; ++j) {
+          const float2 y = f2_fma(f2_mul(v[i][j], inv2), one2, magic);
+          u[2 * j] = __float_as_uint(y.x);
+          u[2 * j + 1] = __float_as_uint(y.y);
+        }
+        int4 o;
+        o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
+        o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
+        o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
+        o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
+        *reinterpret_cast<int4*>(qrow + (int64_t)ci * 16) = o;
       }
-      int4 o;
-      o.x = (int)pack4((int)u[0], (int)u[1], (int)u[2], (int)u[3]);
-      o.y = (int)pack4((int)u[4], (int)u[5], (int)u[6], (int)u[7]);
-      o.z = (int)pack4((int)u[8], (int)u[9], (int)u[10], (int)u[11]);
-      o.w = (int)pack4((int)u[12], (int)u[13], (int)u[14], (int)u[15]);
-      *reinterpret_cast<int4*>(qrow + (int64_t)ci * 16) = o;
     }
   }
 }
