@@ -33,6 +33,9 @@ SIGNATURES = {
     "qlin_version": [],
     "qlin_set_device": [_I],
     "qlin_device_error": [_P, _P],
+    "qlin_set_wait_limit": [_U64],
+    "qlin_selftest_wait_timeout": [_I, _P],
+    "qlin_selftest_gemm_stall": [_P, _P, _P, _P, _P, _L, _L, _L, _L, _P],
     "qlin_quant_act_int8": [_P, _I, _L, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_quant_act_int8_norm": [_P, _I, _L, _L, _L, _I, _F, _P, _P, _L, _P, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_quant_act_int8_cat": [_P, _L, _L, _P, _L, _L, _I, _L, _I, _I, _F, _P, _P, _P],

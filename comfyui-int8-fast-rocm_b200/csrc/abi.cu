@@ -127,6 +127,34 @@ QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits) {
   return QLIN_OK;
 }
 
+QLIN_API int qlin_set_wait_limit(uint64_t limit_ns) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (limit_ns == 0) limit_ns = 2000000000ull;
+  if (limit_ns < 1000ull || limit_ns > 60000000000ull)
+    return fail(QLIN_ERR_INVALID_ARG, "wait limit must lie between 1 us and 60 s");
+  if ((rc = set_gemm_wait_limit(limit_ns))) return rc;
+  return set_rowquant_wait_limit(limit_ns);
+}
+
+QLIN_API int qlin_selftest_wait_timeout(int which, void* stream) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (which == 0) return launch_wait_selftest(static_cast<cudaStream_t>(stream));
+  if (which == 1) return launch_rowquant_wait_selftest(static_cast<cudaStream_t>(stream));
+  return fail(QLIN_ERR_INVALID_ARG, "which must be 0 (GEMM pipeline wait) or 1 (row-kernel wait)");
+}
+
+QLIN_API int qlin_selftest_gemm_stall(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                      void* out, int64_t M, int64_t N, int64_t K, int64_t stall_kb, void* stream) {
+  if (!a || !a_scale || !w || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (K % 16) return fail(QLIN_ERR_ALIGNMENT, "K must be a multiple of 16");
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out)) return fail(QLIN_ERR_ALIGNMENT, "operands must be 16-byte aligned");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_gemm_stall(a, a_scale, w, w_scale, out, M, N, K, stall_kb, static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                  int rot_group, float rot_c, int8_t* q, float* scale, void* stream) {
   if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");

@@ -196,6 +196,7 @@ GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale, co
   for (int i = 0; i < kMaxOutputs; ++i) p.outs[i] = i < o.nout ? o.outs[i] : nullptr;
   p.gelu_col0 = INT64_MAX;  // EPI_POST fields: no GELU, no residual
   p.rows_per_gate = 1;
+  p.stall_kb = -1;
   return p;
 }
 
@@ -366,6 +367,60 @@ int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, 
   p.ldo = N;
   if (a_int4_groups) return dispatch_g128<G128_W4A4>(out_dt, ta, tb, w_packed, p, sms, stream);
   return dispatch_g128<G128_W4A8>(out_dt, ta, tb, w_packed, p, sms, stream);
+}
+
+namespace {
+
+// One thread waits, bounded, on an mbarrier phase that nothing completes.
+__global__ void wait_selftest_kernel() {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait_bounded(&bar, 0, &abort_flag);
+}
+
+}  // namespace
+
+int launch_wait_selftest(cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>();
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QLIN_OK : cuda_fail(e, "wait self-test launch");
+}
+
+int launch_gemm_stall(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, void* out,
+                      int64_t M, int64_t N, int64_t K, int64_t stall_kb, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
+  if (stall_kb < 0 || stall_kb >= (K + GEMM_BK - 1) / GEMM_BK) return fail(QLIN_ERR_INVALID_ARG, "stall_kb out of range");
+  const int sms = device_sm_count();
+  if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  OutSpec o;
+  o.outs[0] = out;
+  o.nout = 1;
+  o.col_off = 0;
+  o.ldo = N;
+  GemmParams p = make_params(M, N, K, a_scale, w_scale, nullptr, o, sms);
+  p.stall_kb = (int)stall_kb;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (M >= 256 && N >= 256 && sms >= 2) {
+    rc = make_tmap(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    return launch_pair_cfg<EPI_W8A8_ROW, DT_BF16>(ta, tb, p, stream);
+  }
+  rc = make_tmap(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 256, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  return launch_cfg<256, EPI_W8A8_ROW, DT_BF16, false>(ta, tb, p, stream);
+}
+
+int set_gemm_wait_limit(uint64_t ns) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+  return e == cudaSuccess ? QLIN_OK : cuda_fail(e, "set wait limit");
 }
 
 int read_device_error(cudaStream_t stream, uint32_t* bits) {

@@ -24,26 +24,29 @@
 
 namespace qlin {
 
-// Device error word (bit 0: a pipeline wait timed out).  Read and cleared by
-// qlin_device_error().  Defined here: gemm.cu is the only translation unit
-// that includes this header.
+// Device error word (bit 0: a pipeline wait timed out; bit 2: after a
+// timeout, the kernel's in-flight TMA loads or MMAs did not drain within the
+// limit either).  Read and cleared by qlin_device_error().  Defined here:
+// gemm.cu is the only translation unit that includes this header.
 __device__ uint32_t g_error_bits = 0;
 
-// Pipeline waits give up after this long and flag the failure.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Pipeline waits give up after this many nanoseconds and flag the failure
+// (qlin_set_wait_limit; 2 s by default).
+__device__ uint64_t g_wait_limit_ns = 2000000000ull;
 
 // Bounded wait on an mbarrier phase.  Returns false (and sets the device
 // error word and *abort) if the phase did not complete within the limit or
 // another role of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
   const uint64_t t0 = globaltimer_ns();
   uint32_t iter = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++iter & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit) {
         atomicOr(&g_error_bits, 1u);
         *abort = 1;
         return false;
@@ -51,6 +54,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
   }
 }
+
+// Abort path: wait (bounded, whatever the abort flag says) for a phase that
+// completes once asynchronous work this thread issued earlier has finished.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit) {
+      atomicOr(&g_error_bits, 4u);
+      return;
+    }
+  }
+}
+
+// TMA loads a producer thread armed on the `full` barriers of the operand
+// ring: bit s of `armed` once stage s was filled, bit s of `par` the phase
+// parity of its last fill.  Before the producer leaves its role it waits for
+// those last fills, so no load is still writing shared memory when the CTA
+// exits -- after an abort too, when the MMA issuer never consumed them.  (On
+// the normal path the last fills land within microseconds, while the MMA
+// issuer is still consuming them.)
+struct ArmedLoads {
+  uint32_t armed = 0, par = 0;
+  __device__ __forceinline__ void note(int stage, uint32_t phase) {
+    armed |= 1u << stage;
+    par = (par & ~(1u << stage)) | (phase << stage);
+  }
+  __device__ __forceinline__ void drain(uint64_t* full, int stages) const {
+    for (int s = 0; s < stages; ++s)
+      if (armed >> s & 1u) mbar_wait_drain(&full[s], par >> s & 1u);
+  }
+};
 
 enum : int {
   EPI_W8A8_ROW = 0,     // dt(dt(float(acc)*xs[m]*ws[n]) + bias[n])
@@ -83,6 +118,10 @@ struct GemmParams {
   const void* gate;
   int64_t gate_ld;
   int64_t rows_per_gate;
+  // Failure-detection self-test only (qlin_selftest_gemm_stall): the
+  // producer leaves this K-slab of the CTA's first tile unfilled, so the
+  // MMA issuer's wait for it runs out; -1 in every product launch.
+  int stall_kb;
 };
 
 constexpr int GEMM_BM = 128;
@@ -838,7 +877,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
   uint64_t* conv = empty + STAGES;      // B unpacked and ready (B_INT4)
   uint64_t* tfull = conv + STAGES;      // [2]
   uint64_t* tempty = tfull + 2;         // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;         // abort path: the MMA issuer's last commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -854,6 +894,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -878,25 +919,30 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       tma_prefetch_desc(&tmB);
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      ArmedLoads armed;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
-          if constexpr (B_INT4) {
-            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::BP_BYTES);
-            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
-            tma_load_2d(sBP + stage * Cfg::BP_BYTES, &tmB, &full[stage], kb * (GEMM_BK / 2), nb * BN);
-          } else {
-            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
-            tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
-            tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          if (!(kb == p.stall_kb && tile == (int)blockIdx.x)) {
+            if constexpr (B_INT4) {
+              mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::BP_BYTES);
+              tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+              tma_load_2d(sBP + stage * Cfg::BP_BYTES, &tmB, &full[stage], kb * (GEMM_BK / 2), nb * BN);
+            } else {
+              mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+              tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+              tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+            }
+            armed.note(stage, phase);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
+      armed.drain(full, STAGES);  // no load still writing shared memory at exit
     }
-  producer_done:;
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -905,15 +951,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) goto mma_done;
+      bool issued = false, ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if constexpr (B_INT4) {
-            if (!mbar_wait_bounded(&conv[stage], phase, abort_flag)) goto mma_done;
+            if (!mbar_wait_bounded(&conv[stage], phase, abort_flag)) { ok = false; break; }
           } else {
-            if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) goto mma_done;
+            if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
           const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
@@ -923,15 +970,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
             // advance 32 bytes of K inside the 128-byte swizzle atom
             umma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
           }
+          issued = true;
           umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
+        if (!ok) break;
         umma_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
+      if (*abort_flag && issued) {  // MMAs complete before TMEM is released
+        umma_commit(drain);
+        mbar_wait_drain(drain, 0);
+      }
     }
-  mma_done:;
   } else if (warp < 2 + EPI_WARPS) {
     // ---------------- epilogue ----------------
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
@@ -1014,7 +1066,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;     // [2]
   uint64_t* tempty = tfull + 2;         // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;         // abort path: the MMA issuer's last commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -1031,6 +1084,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 2 * EPI_WARPS);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1057,22 +1111,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       tma_prefetch_desc(&tmB);
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      ArmedLoads armed;  // both CTAs' loads complete on the leader's barriers
+      bool ok = true;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int arow = mb * 2 * GEMM_BM + (int)rank * GEMM_BM;
         const int brow = nb * BN + (int)rank * Cfg::BNH;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
-          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
-          tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
-          tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          if (!(kb == p.stall_kb && tile == cluster_id)) {
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
+            armed.note(stage, phase);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
+      // no load still writing shared memory at exit: the peer CTA cannot
+      // pass the final cluster barrier before the leader has seen both CTAs'
+      // loads land on its barriers
+      if (leader) armed.drain(full, STAGES);
     }
-  producer_done:;
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only) ----------------
     if (leader && lane == 0) {
@@ -1081,26 +1143,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
-        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) goto mma_done;
+      bool issued = false, ok = true;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) goto mma_done;
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
           const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 32; ++k) umma_i8_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          issued = true;
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
+        if (!ok) break;
         umma_commit_pair(&tfull[acc], 0x3);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
+      if (*abort_flag && issued) {  // MMAs complete before TMEM is released
+        umma_commit_pair(drain, 0x1);
+        mbar_wait_drain(drain, 0);
+      }
     }
-  mma_done:;
   } else {
     // ---------------- epilogue (both CTAs) ----------------
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));

@@ -104,6 +104,15 @@ int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const
 int launch_situ(int dt, const void* x, int64_t ldx, int64_t M, int64_t K, void* y, cudaStream_t stream);
 
 int read_device_error(cudaStream_t stream, uint32_t* bits);
+// Failure detection: wait limits of the GEMM and row-kernel pipelines, the
+// one-thread wait self-tests, and a W8A8 GEMM whose producer leaves K-slab
+// stall_kb of each CTA's first tile unfilled.
+int set_gemm_wait_limit(uint64_t ns);
+int set_rowquant_wait_limit(uint64_t ns);
+int launch_wait_selftest(cudaStream_t stream);
+int launch_rowquant_wait_selftest(cudaStream_t stream);
+int launch_gemm_stall(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, void* out,
+                      int64_t M, int64_t N, int64_t K, int64_t stall_kb, cudaStream_t stream);
 int read_rowquant_error(cudaStream_t stream, uint32_t* bits);
 
 }  // namespace qlin

@@ -360,6 +360,30 @@ int launch_rowquant_cat(int dt, int rot_kind, int rot_group, float rot_c, const 
   return r;
 }
 
+namespace {
+// One thread waits, bounded, on an mbarrier phase that nothing completes.
+__global__ void rq_wait_selftest_kernel() {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)rq_wait_bounded(&bar, 0);
+}
+}  // namespace
+
+int launch_rowquant_wait_selftest(cudaStream_t stream) {
+  rq_wait_selftest_kernel<<<1, 32, 0, stream>>>();
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QLIN_OK : cuda_fail(e, "row-kernel wait self-test launch");
+}
+
+int set_rowquant_wait_limit(uint64_t ns) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_rq_wait_limit_ns, &ns, sizeof(ns));
+  return e == cudaSuccess ? QLIN_OK : cuda_fail(e, "set row-kernel wait limit");
+}
+
 // Error word of the row kernels: read and clear (bit 1: a bulk-copy wait
 // timed out).
 int read_rowquant_error(cudaStream_t stream, uint32_t* bits) {

@@ -556,15 +556,17 @@ __device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
 // Device error word of the row kernels (bit 1: a bulk-copy wait timed out);
 // one copy per translation unit, read through rowquant.cu.
 static __device__ uint32_t g_rq_error_bits = 0;
-constexpr uint64_t kRqWaitLimitNs = 2000000000ull;  // 2 s
+// Wait limit in nanoseconds (qlin_set_wait_limit; 2 s by default).
+static __device__ uint64_t g_rq_wait_limit_ns = 2000000000ull;
 
 __device__ __forceinline__ bool rq_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_rq_wait_limit_ns);
   const uint64_t t0 = globaltimer_ns();
   uint32_t iter = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++iter & 63u) == 0 && globaltimer_ns() - t0 > kRqWaitLimitNs) {
+    if ((++iter & 63u) == 0 && globaltimer_ns() - t0 > limit) {
       atomicOr(&g_rq_error_bits, 2u);
       return false;
     }

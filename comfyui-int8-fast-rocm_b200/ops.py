@@ -570,10 +570,39 @@ def requant_int8(w: torch.Tensor, scale, rot=None, stochastic=False, seed=0) -> 
 
 
 def device_error(device=None) -> int:
-    """Read and clear the device-side error word (nonzero: a GEMM pipeline
-    wait timed out)."""
+    """Read and clear the device-side error word (bit 0: a GEMM pipeline
+    wait timed out; bit 1: a row-kernel wait timed out; bit 2: a timed-out
+    GEMM's in-flight work did not drain within the limit either)."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
     N.call("qlin_set_device", dev.index)
     bits = ctypes.c_uint32(0)
     N.call("qlin_device_error", torch.cuda.current_stream(dev).cuda_stream, ctypes.addressof(bits))
     return bits.value
+
+
+def set_wait_limit(limit_ns: int = 0, device=None) -> None:
+    """Wait limit of the kernels' bounded pipeline waits on ``device``, in
+    nanoseconds (0: the default of 2 s)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    N.call("qlin_set_device", dev.index)
+    N.call("qlin_set_wait_limit", int(limit_ns))
+
+
+def selftest_wait_timeout(which: int) -> None:
+    """Launch the one-thread bounded-wait self-test on the current stream:
+    which 0 checks the GEMM pipeline wait, 1 the row kernels' wait."""
+    N.call("qlin_selftest_wait_timeout", int(which), torch.cuda.current_stream().cuda_stream)
+
+
+def selftest_gemm_stall(a_q, a_scale, w_q, w_scale, stall_kb: int = 0) -> torch.Tensor:
+    """The W8A8 per-row GEMM (bf16 out, no bias) with K-slab ``stall_kb`` of
+    each CTA's first tile never loaded: its wait runs out and the kernel
+    returns with error bit 0 set.  Returns the (partly written) output."""
+    _check_gemm(a_q, w_q)
+    a_q, w_q = _aligned(a_q), _aligned(w_q)
+    M, K = a_q.shape
+    Nn = w_q.shape[0]
+    out = torch.empty((M, Nn), dtype=torch.bfloat16, device=a_q.device)
+    N.call("qlin_selftest_gemm_stall", _ptr(a_q), _ptr(a_scale.float().contiguous()), _ptr(w_q),
+           _ptr(w_scale.float().contiguous()), _ptr(out), M, Nn, K, int(stall_kb), _stream(a_q))
+    return out

@@ -16,8 +16,13 @@
  *  - The device is the calling thread's current CUDA device.
  *  - Every function returns QLIN_OK (0) or a QLIN_ERR_* code and never throws;
  *    qlin_last_error() returns a thread-local message for the last failure.
- *  - Numerics follow the reference's PyTorch CPU path bit for bit; each
- *    GEMM entry point below states its epilogue's rounding order.
+ *  - Numerics follow the reference's PyTorch CPU path bit for bit (codes,
+ *    scales, int32 accumulators, and outputs of the reference's epilogues);
+ *    each GEMM entry point below states its epilogue's rounding order.  The
+ *    exceptions are stated where they occur: the ConvRot rotation sums in a
+ *    fixed butterfly order (the reference's library matmul has its own), the
+ *    GELU step of qlin_gemm_w8a8_fused is within one unit of out_dtype of the
+ *    exact function, and the group-128 schemes have no reference at all.
  */
 #ifndef QLINEAR_B200_H
 #define QLINEAR_B200_H
@@ -75,8 +80,37 @@ QLIN_API int qlin_set_device(int device);
 QLIN_API const char* qlin_last_error(void);
 /* Reads and clears the device-side error words of the current device (bit 0:
  * a pipeline wait inside a GEMM kernel timed out; bit 1: a row kernel's
- * bulk-copy wait timed out).  Synchronises `stream`. */
+ * bulk-copy wait timed out; bit 2: after a GEMM timeout its in-flight work
+ * did not drain within the limit).  Synchronises `stream`. */
 QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits);
+
+/* ---- failure detection ---------------------------------------------------
+ * Every pipeline wait inside the kernels is bounded.  When a wait makes no
+ * progress for the limit, the kernel sets a bit of the device error word,
+ * every role of the CTA leaves its loop, the GEMM's in-flight TMA loads and
+ * MMAs are drained (bit 2 if that drain also runs out), tensor memory is
+ * released and the kernel returns; the context stays usable.  No
+ * counterpart in the reference, which has no device-side error reporting
+ * (its only error handling is host-side ValueErrors,
+ * rocm_int8_kitchen_patch.py:138-150). */
+
+/* Sets the wait limit of the current device's kernels, in nanoseconds
+ * (1 us .. 60 s; 0 restores the default of 2 s).  Synchronous. */
+QLIN_API int qlin_set_wait_limit(uint64_t limit_ns);
+
+/* Self-test of the bounded wait: one thread waits on an mbarrier phase that
+ * nothing completes, for the current limit, then returns.  which 0: the
+ * GEMM pipeline wait (sets error bit 0); which 1: the row kernels' wait
+ * (sets error bit 1). */
+QLIN_API int qlin_selftest_wait_timeout(int which, void* stream);
+
+/* Self-test of a whole GEMM's abort path: the W8A8 per-row GEMM with bf16
+ * output and no bias (as qlin_gemm_w8a8) whose TMA producer leaves K-slab
+ * `stall_kb` (128 int8 of K) of each CTA's first tile unfilled, so the MMA
+ * issuer's wait for it runs out after the limit: error bit 0 is set and the
+ * kernel returns with `out` partly written. */
+QLIN_API int qlin_selftest_gemm_stall(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                      void* out, int64_t M, int64_t N, int64_t K, int64_t stall_kb, void* stream);
 
 /* ---- (a) activation quantisation, fused with the ConvRot rotation -------- */
 

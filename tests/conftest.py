@@ -41,6 +41,11 @@ def golden():
     return np.load(os.path.join(ROOT, "tests", "golden", "golden.npz"))
 
 
+@pytest.fixture(scope="session")
+def golden_c1():
+    return np.load(os.path.join(ROOT, "tests", "golden", "golden_c1.npz"))
+
+
 def cuda_ok():
     try:
         import torch

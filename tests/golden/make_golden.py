@@ -224,6 +224,65 @@ def main(ref_dir):
     np.savez_compressed(path, **out)
     print("wrote", path, os.path.getsize(path), "bytes,", len(out), "arrays")
 
+    config_scale_codes(cr, i8, scipy_hadamard)
+
+
+def config_scale_codes(cr, i8, scipy_hadamard):
+    """ConvRot activation codes at the W8A8 linear's full size.
+
+    The reference rotates with a bf16 library matmul (convrot.py:114-117)
+    whose float32 accumulation order is its own; the kernels (and the
+    oracle) use a fixed-order butterfly.  For each case this stores the
+    reference's int8 codes as a digest plus the sparse list of positions where
+    they differ from the oracle's codes, and the reference's per-token scales
+    in full.  The GPU test patches the kernel's codes at those positions and
+    checks the digest: that proves the kernel differs from the reference at
+    exactly the listed positions, which gives the mismatch count over the
+    whole tensor."""
+    import torch
+
+    from oracle import qlinear_oracle as O
+
+    out = {}
+    cases = [("syl128_k3072", 3072, 128, "sylvester"), ("reg256_k3072", 3072, 256, "regular"),
+             ("syl128_k12288", 12288, 128, "sylvester")]
+    for name, K, g, kind in cases:
+        x = gi.activation(1, 4096, K, "bf16")
+        if kind == "sylvester":
+            H = torch.tensor(scipy_hadamard(g), dtype=torch.float32) / (g ** 0.5)
+        else:
+            H = cr.build_hadamard(g, device="cpu", dtype=torch.float32)
+        xr = cr.rotate_activation(torch.from_numpy(x).to(torch.bfloat16), H, group_size=g)
+        q, s = i8.quantize_int8_axiswise(xr, dim=-1)
+        q = q.numpy()
+        s = s.numpy().reshape(-1)
+        qo, so = O.quantize_int8_axiswise(O.rotate(x, g, kind, "bf16"), -1)
+        diff = np.flatnonzero(q.reshape(-1) != qo.reshape(-1)).astype(np.int64)
+        rot_ref = xr.contiguous().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
+        rot_orc = O.f32_to_bf16_bits(O.rotate(x, g, kind, "bf16")).astype(np.int32)
+        out[f"{name}_q_sha"] = np.array(sha(q))
+        out[f"{name}_s"] = s
+        out[f"{name}_diff_pos"] = diff
+        out[f"{name}_diff_val"] = q.reshape(-1)[diff]
+        out[f"{name}_scale_rows_differ"] = np.array(int((s != so.reshape(-1)).sum()))
+        out[f"{name}_rot_elems_differ"] = np.array(int((rot_ref != rot_orc).sum()))
+        # largest difference in units of the bf16 spacing at the row's
+        # absmax (values that nearly cancel differ by more ulps of their own)
+        fr = xr.to(torch.float32).numpy()
+        fo = O.rotate(x, g, kind, "bf16")
+        amax = np.abs(fr).max(axis=1, keepdims=True)
+        spacing = np.spacing(amax.astype(np.float32)) * 2.0 ** 16
+        out[f"{name}_rot_max_diff_in_row_ulps"] = np.array(float((np.abs(fr - fo) / spacing).max()))
+        print(name, "codes differing:", diff.size, "of", q.size, "scales differing:",
+              int(out[f"{name}_scale_rows_differ"]), "rotated values differing:",
+              int(out[f"{name}_rot_elems_differ"]), "largest difference in row-absmax ulps:",
+              float(out[f"{name}_rot_max_diff_in_row_ulps"]))
+    path = os.path.join(HERE, "golden_c1.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, os.path.getsize(path), "bytes")
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the reference checkout>")
+    main(sys.argv[1])

@@ -567,3 +567,64 @@ def test_situ(P, dt):
     else:  # one rounding to bf16 of a float32 result: within 1 bf16 ulp
         ulp = np.spacing(np.abs(ref).astype(np.float32)) * 2 ** 16
         assert (np.abs(y - ref) <= ulp + 1e-30).all()
+
+
+# ---------------------------------------------------------------------------
+# the W8A8 linear at the benchmarked shapes (whole problem on the GPU, the
+# oracle on a sample of rows: rows of a linear are independent)
+# ---------------------------------------------------------------------------
+
+BENCH_SHAPES = [
+    # (M, N, K, rotation, seed)
+    (4096, 12288, 3072, ("sylvester", 128), 1),  # the ConvRot W8A8 headline
+    (8192, 9216, 12288, ("sylvester", 128), 1),
+    (4096, 3072, 12288, ("regular", 256), 1),
+    (4096, 3072, 3072, None, 0),  # the plain dynamic W8A8 linear, no rotation
+]
+
+
+@pytest.mark.parametrize("M,N,K,rot,seed", BENCH_SHAPES)
+def test_w8a8_linear_bench_shapes_rows(P, M, N, K, rot, seed):
+    """Codes, scales and bf16 outputs of the plain CTA-pair W8A8 kernel (6
+    operand stages, double TMEM accumulator, several tiles per cluster) at
+    the benchmarked shapes, against the oracle on 50 rows."""
+    x = gi.activation(seed, M, K, "bf16")
+    w = gi.weight(seed, N, K)
+    b = gi.bias(seed, N, "bf16")
+    gq, gs = P.ops.quant_weight_int8(dev(w), rot)
+    wrows = _rows_sample(N, n=16, seed=seed + 7)
+    wq_o, ws_o = O.quantize_weight_int8(w[wrows], *((rot[1], rot[0]) if rot else ()))
+    np.testing.assert_array_equal(gq.cpu().numpy()[wrows], wq_o)
+    np.testing.assert_array_equal(gs.cpu().numpy()[wrows], ws_o)
+    xq, xs = P.ops.quant_act_int8(dev(x, "bf16"), rot)
+    y = P.ops.gemm_w8a8(xq, xs, gq, gs, dev(b, "bf16"), torch.bfloat16)
+    assert P.ops.device_error() == 0
+    rows = _rows_sample(M, seed=seed + 11)
+    xr = x[rows] if rot is None else O.rotate(x[rows], rot[1], rot[0], "bf16")
+    qo, so = O.quantize_int8_axiswise(xr, -1)
+    np.testing.assert_array_equal(xq.cpu().numpy()[rows], qo)
+    np.testing.assert_array_equal(xs.cpu().numpy()[rows], so)
+    yo = O.w8a8_epilogue_per_row(O.int_mm(qo, gq.cpu().numpy()), so, gs.cpu().numpy(), b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
+@pytest.mark.parametrize("name,K,g,kind", [("syl128_k3072", 3072, 128, "sylvester"),
+                                           ("reg256_k3072", 3072, 256, "regular"),
+                                           ("syl128_k12288", 12288, 128, "sylvester")])
+def test_rotated_codes_vs_reference_full_size(P, golden_c1, name, K, g, kind):
+    """Activation codes of the fused rotate+quantise kernel against the
+    reference's own rotate_activation + quantize_int8_axiswise on the
+    4096-token activations of the ConvRot linear.  The golden file lists
+    where the reference's codes differ from the fixed-order butterfly's; the
+    kernel's codes patched there must hash to the reference's digest, so the
+    kernel differs from the reference at exactly those positions."""
+    x = gi.activation(1, 4096, K, "bf16")
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"), (kind, g))
+    qf = q.cpu().numpy().reshape(-1).copy()
+    pos = golden_c1[f"{name}_diff_pos"]
+    assert pos.size <= 2e-6 * qf.size  # 13 (K=3072) and 29 (K=12288) positions
+    qf[pos] = golden_c1[f"{name}_diff_val"]
+    import hashlib
+    assert hashlib.sha256(qf.tobytes()).hexdigest() == str(golden_c1[f"{name}_q_sha"])
+    differ = int((s.cpu().numpy().reshape(-1) != golden_c1[f"{name}_s"]).sum())
+    assert differ == int(golden_c1[f"{name}_scale_rows_differ"]) == 0

@@ -187,3 +187,21 @@ def test_lora_bake_roundtrip(golden):
     assert np.abs(d).max() <= 1 and (d != 0).mean() < 1e-3
     # with the reference's re-rotated weight as input the requant is bit-exact
     np.testing.assert_array_equal(O.quantize_int8(golden["lora_rerot"], os_), golden["lora_q"])
+
+
+@pytest.mark.parametrize("name,K,g,kind", [("syl128_k3072", 3072, 128, "sylvester"),
+                                           ("reg256_k3072", 3072, 256, "regular")])
+def test_rotated_codes_vs_reference_full_size(golden_c1, name, K, g, kind):
+    """The oracle's rotate + quantise at the ConvRot linear's full size
+    (4096 tokens) against the reference's codes: they differ exactly at the
+    positions the golden file lists (13 of 12.6 M codes for Sylvester 128,
+    none for regular 256) and the per-token scales are equal."""
+    import hashlib
+    x = gi.activation(1, 4096, K, "bf16")
+    q, s = O.quantize_int8_axiswise(O.rotate(x, g, kind, "bf16"), -1)
+    qf = q.reshape(-1).copy()
+    pos = golden_c1[f"{name}_diff_pos"]
+    assert (qf[pos] != golden_c1[f"{name}_diff_val"]).all()
+    qf[pos] = golden_c1[f"{name}_diff_val"]
+    assert hashlib.sha256(qf.tobytes()).hexdigest() == str(golden_c1[f"{name}_q_sha"])
+    np.testing.assert_array_equal(s.reshape(-1), golden_c1[f"{name}_s"])
