@@ -1,9 +1,11 @@
 // Instantiation and launch of the row-wise rotate/quantise kernel family.
 #include <atomic>
+#include <cstdlib>
 
 #include "../../include/qlinear_b200.h"
 #include "internal.h"
 #include "rowquant.cuh"
+#include "rowstrip.cuh"
 
 namespace qlin {
 namespace {
@@ -197,6 +199,71 @@ int x2_by_chunks(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t 
   return x2_by_rot<DT, 1, FUSED>(rc, p, nchunks, s);
 }
 
+// One 128-element strip per thread (rowstrip.cuh): 16-bit activations, K a
+// multiple of 128 up to 16384, rows 16-byte aligned, codes 32-byte aligned.
+template <int DT, int KIND, int G>
+int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
+  auto kern = rowquant_strip_kernel<DT, KIND, G>;
+  const int T = p.K / STRIP;
+  int rows = 128 / T;  // whole rows per CTA; prefer whole warps
+  for (int r = rows; r >= 1; --r)
+    if ((r * T) % 32 == 0) { rows = r; break; }
+  const int threads = rows * T;
+  const int slot_bytes = (rows * p.K * 2 + 127) / 128 * 128;
+  constexpr int stages = 2;  // measured: 3 or 4 slots were no faster (fewer CTAs per SM)
+  const size_t smem = (size_t)stages * slot_bytes;
+  if (smem > 200 * 1024) return QLIN_ERR_UNSUPPORTED;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<uint64_t> attr_devices{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_devices.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowquant strip)");
+    attr_devices.fetch_or(bit);
+  }
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+  if (per_sm < 1) per_sm = 1;
+  const int64_t nblocks = ((int64_t)p.M + rows - 1) / rows;
+  const int64_t cap = (int64_t)device_sm_count() * per_sm;
+  kern<<<(unsigned)(nblocks < cap ? nblocks : cap), threads, smem, stream>>>(
+      p.x, p.ldx, p.M, p.K, rows, stages, slot_bytes, p.rot_c, p.one, p.q, p.scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rowquant strip launch");
+  return QLIN_OK;
+}
+
+// The strip kernel serves the Sylvester-128 rotation, whose 128-element group
+// is one strip.  Measured at 4096 x 3072 (B200, eight inputs back to back,
+// L2 not holding them): Sylvester 128 14.7 us against 16.8 us on the ring
+// kernel; without rotation 15.8 against 10.6 and regular 256 18.6 against
+// 16.8, so those (and the other sizes) stay on the ring kernel.  (The
+// kernel template also implements the XOR-relabelled reads for the other
+// rotations; the launcher does not instantiate them.)
+template <int DT>
+int strip_by_rot(RotCode rc, const RowQuantParams& p, cudaStream_t s) {
+  if (rc == RC_SYL128) return launch_strip<DT, ROT_SYLVESTER, 128>(p, s);
+  return QLIN_ERR_UNSUPPORTED;
+}
+
+// QLIN_ROWQUANT_NO_STRIP=1 keeps 16-bit activations on the bulk-copy ring
+// kernel (comparison runs).
+bool strip_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_ROWQUANT_NO_STRIP");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
+bool strip_ok(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t K, const int8_t* q) {
+  return L.mode == MODE_INT8 && L.dt_in == L.dt_q && (L.dt_in == DT_BF16 || L.dt_in == DT_F16) && K % STRIP == 0 &&
+         K / STRIP <= 128 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * 2) % 16 == 0 &&
+         (reinterpret_cast<uintptr_t>(q) & 31) == 0 && !strip_disabled();
+}
+
 }  // namespace
 
 int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t M, int64_t K, float rot_c,
@@ -226,6 +293,10 @@ int launch_rowquant(const RowQuantLaunch& L, const void* x, int64_t ldx, int64_t
   // Activation int8 hot path: packed float32x2 kernel fed by a bulk-copy
   // ring (falls through to the register-prefetch kernel when two ring slots
   // do not fit in shared memory).
+  if (strip_ok(L, x, ldx, K, q)) {
+    const int rc2 = L.dt_in == DT_BF16 ? strip_by_rot<DT_BF16>(rc, p, stream) : strip_by_rot<DT_F16>(rc, p, stream);
+    if (rc2 != QLIN_ERR_UNSUPPORTED) return rc2;
+  }
   if (L.mode == MODE_INT8 && L.dt_in == L.dt_q) {
     int rc2 = QLIN_ERR_UNSUPPORTED;
     if (L.dt_in == DT_BF16) rc2 = x2_by_chunks<DT_BF16>(rc, p, (int)nchunks, stream);

@@ -155,13 +155,14 @@ def test_quant_int8_round_half_even_ties(P, K):
     np.testing.assert_array_equal(q.cpu().numpy(), qo)
 
 
-def test_quant_int8_paired_nonfinite_rows(P):
+@pytest.mark.parametrize("rot", [None, ("sylvester", 128)])
+def test_quant_int8_paired_nonfinite_rows(P, rot):
     x = gi.activation(18, 9, 2048, "bf16")
     x[1, 100] = np.inf
     x[4, 2047] = -np.inf
     x[6, 1500] = np.nan
-    q, s = P.ops.quant_act_int8(dev(x, "bf16"))
-    qo, so = O.quantize_int8_axiswise(x, -1)
+    q, s = P.ops.quant_act_int8(dev(x, "bf16"), rot)
+    qo, so = O.quantize_int8_axiswise(x if rot is None else O.rotate(x, 128, "sylvester", "bf16"), -1)
     np.testing.assert_array_equal(q.cpu().numpy(), qo)
     np.testing.assert_array_equal(s.cpu().numpy(), so)  # NaN matches NaN, Inf matches Inf
 
