@@ -13,6 +13,7 @@ import logging
 
 from . import _native  # noqa: F401
 from . import ops  # noqa: F401
+from . import library  # noqa: F401  (the kernels as torch.library operators, namespace qlin_b200)
 from . import convrot  # noqa: F401
 from . import int8_fused_kernel  # noqa: F401
 from . import triton_int4_mm  # noqa: F401
@@ -94,4 +95,4 @@ try:
 except ImportError:
     pass
 
-__all__ = ["NODE_CLASS_MAPPINGS", "NODE_DISPLAY_NAME_MAPPINGS", "Int8TensorwiseOps", "Int4ConvRotOps", "ops"]
+__all__ = ["NODE_CLASS_MAPPINGS", "NODE_DISPLAY_NAME_MAPPINGS", "Int8TensorwiseOps", "Int4ConvRotOps", "ops", "library"]

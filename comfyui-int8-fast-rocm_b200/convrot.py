@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 
 _HADAMARD_CACHE: dict = {}
 _H4 = [[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]]
@@ -74,7 +74,7 @@ def rotate_activation(x: torch.Tensor, H: torch.Tensor, group_size: int) -> torc
     """x_rot = x @ blockdiag(H) (convrot.py:89-118); result in x.dtype."""
     if x.shape[-1] % group_size != 0:
         raise ValueError(f"features {x.shape[-1]} not divisible by group_size {group_size}")
-    return ops.rotate(x, hadamard_kind(H), group_size)
+    return kops.rotate(x, hadamard_kind(H), group_size)
 
 
 def rotate_weight(weight: torch.Tensor, H: torch.Tensor, group_size: int) -> torch.Tensor:
@@ -83,4 +83,4 @@ def rotate_weight(weight: torch.Tensor, H: torch.Tensor, group_size: int) -> tor
         raise ValueError("rotate_weight expects a 2-D weight")
     if weight.shape[1] % group_size != 0:
         raise ValueError(f"in_features {weight.shape[1]} not divisible by group_size {group_size}")
-    return ops.rotate(weight, hadamard_kind(H), group_size)
+    return kops.rotate(weight, hadamard_kind(H), group_size)

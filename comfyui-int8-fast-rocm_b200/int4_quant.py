@@ -14,7 +14,7 @@ import torch
 from torch import Tensor, nn
 import torch.nn.functional as F
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 from .int8_quant import (_normalize_lora_key, _parse_comfy_quant, _pop_metadata, int8_forward_dynamic,
                          int8_forward_dynamic_per_row, rot_for_group)
 
@@ -45,14 +45,14 @@ def unpack_int4_row_major(packed: Tensor) -> Tensor:
 def quantize_signed_int4_rowwise(x: Tensor):
     """Per-row symmetric int4 in x.dtype, int8 storage (int4_quant.py:65-73):
     (q [R,K] int8 in [-7,7], scales float32 [R])."""
-    return ops.quant_act_int4(x.reshape(x.shape[0], -1))
+    return kops.quant_act_int4(x.reshape(x.shape[0], -1))
 
 
 def quantize_signed_int4_rowwise_packed(x: Tensor):
     """Same, packed two per byte (int4_quant.py:76-83)."""
     if x.dtype == torch.float32:
-        return ops.quant_weight_int4(x)
-    q, s = ops.quant_act_int4(x)
+        return kops.quant_weight_int4(x)
+    q, s = kops.quant_act_int4(x)
     return pack_int4_row_major(q), s
 
 
@@ -62,20 +62,20 @@ def quantize_convrot_w4a4_weight(weight: Tensor, convrot_groupsize: int = CONVRO
         raise ValueError(f"ConvRot W4A4 expects a 2D weight, got shape {tuple(weight.shape)}")
     if weight.shape[-1] % convrot_groupsize != 0:
         raise ValueError(f"in_features {weight.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
-    return ops.quant_weight_int4(weight.float(), rot_for_group(convrot_groupsize))
+    return kops.quant_weight_int4(weight.float(), rot_for_group(convrot_groupsize))
 
 
 def quantize_int4_g128(x: Tensor, rot=None):
     """Group-128 int4 (per row and 128-wide K group) in x.dtype:
     (q int8 [R,K], scales float32 [R, K/128])."""
-    return ops.quant_act_int4(x, rot, group=128)
+    return kops.quant_act_int4(x, rot, group=128)
 
 
 def dequantize_convrot_w4a4_weight_full(qweight: Tensor, wscales: Tensor, convrot_groupsize: int,
                                         dtype: torch.dtype = torch.float32) -> Tensor:
     """Unpack, rescale, un-rotate (int4_quant.py:217-231)."""
     w = unpack_int4_row_major(qweight).to(torch.float32) * wscales.reshape(-1, 1).to(torch.float32)
-    return ops.rotate(w, *rot_for_group(convrot_groupsize)).to(dtype)
+    return kops.rotate(w, *rot_for_group(convrot_groupsize)).to(dtype)
 
 
 def prepare_rotated_activation(x: Tensor, convrot_groupsize: int, compute_dtype: torch.dtype,
@@ -87,7 +87,7 @@ def prepare_rotated_activation(x: Tensor, convrot_groupsize: int, compute_dtype:
     x2d = x.reshape(-1, orig_shape[-1]).to(compute_dtype).contiguous()
     if skip_rotation:
         return x2d, orig_shape
-    return ops.rotate(x2d, *rot_for_group(convrot_groupsize)), orig_shape
+    return kops.rotate(x2d, *rot_for_group(convrot_groupsize)), orig_shape
 
 
 def convrot_w4a4_forward(x: Tensor, qweight: Tensor, wscales: Tensor, bias, convrot_groupsize: int,
@@ -102,13 +102,13 @@ def convrot_w4a4_forward(x: Tensor, qweight: Tensor, wscales: Tensor, bias, conv
             raise ValueError(f"Input K={orig_shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
         x2d = x.reshape(-1, orig_shape[-1]).to(compute_dtype)
         rot = None if skip_rotation else rot_for_group(convrot_groupsize)
-        qact, x_scale = ops.quant_act_int4(x2d, rot)
+        qact, x_scale = kops.quant_act_int4(x2d, rot)
     else:
-        qact, x_scale = ops.quant_act_int4(x_rot)
+        qact, x_scale = kops.quant_act_int4(x_rot)
     in_f = orig_shape[-1]
     if in_f != qweight.shape[-1] * 2:
         raise ValueError(f"Input K={in_f} does not match packed qweight K={qweight.shape[-1] * 2}")
-    out = ops.gemm_w4a4(qact, x_scale, qweight, wscales, bias, compute_dtype)
+    out = kops.gemm_w4a4(qact, x_scale, qweight, wscales, bias, compute_dtype)
     return out.reshape(*orig_shape[:-1], wscales.shape[0])
 
 
@@ -139,7 +139,7 @@ def dequantize_simple_int8_rowwise(weight: Tensor, scale: Tensor, out_features: 
     """float32 weight of an ``int8_tensorwise`` layer inside an int4 model,
     un-rotated when the layer is ConvRot (int4_quant.py:137-160)."""
     rot = rot_for_group(convrot_groupsize) if convrot else None
-    return ops.dequant_int8(weight, scale.float().reshape(-1, 1) if scale.numel() == out_features else scale.float(),
+    return kops.dequant_int8(weight, scale.float().reshape(-1, 1) if scale.numel() == out_features else scale.float(),
                             rot)
 
 
@@ -382,7 +382,7 @@ if _COMFY_OPS_AVAILABLE:
                     else:
                         y = int8_forward_dynamic(x2d, weight, w_scale, bias, compute_dtype, rot)
                     y = y.reshape(*x.shape[:-1], weight.shape[0])
-                    x_l = ops.rotate(x2d, *rot) if (self.lora_patches and rot is not None) else x2d
+                    x_l = kops.rotate(x2d, *rot) if (self.lora_patches and rot is not None) else x2d
                 else:
                     y = convrot_w4a4_forward(x, weight, w_scale, bias, self._convrot_groupsize, compute_dtype,
                                              skip_rotation=Int4ConvRotOps.debug_skip_rotation)
@@ -460,10 +460,10 @@ def bake_int4_layer_weight(module, source, delta_fn, stochastic=False, seed=0):
         w = dequantize_simple_int8_rowwise(source, wscale, source.shape[0], convrot=use_rot, convrot_groupsize=group)
         w = delta_fn(w)
         if use_rot:
-            w = ops.rotate(w.float().contiguous(), *rot_for_group(group))
+            w = kops.rotate(w.float().contiguous(), *rot_for_group(group))
         return quantize_int8_with_scale(w, wscale)
     w = dequantize_convrot_w4a4_weight_full(source, wscale, group, dtype=torch.float32)
-    w = ops.rotate(delta_fn(w).float().contiguous(), *rot_for_group(group))
+    w = kops.rotate(delta_fn(w).float().contiguous(), *rot_for_group(group))
     if stochastic:
         return stochastic_round_int4_packed_delta(w, wscale, seed)
     return quantize_signed_int4_packed_with_scale(w, wscale)

@@ -10,25 +10,25 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 
 
 def triton_quantize_rowwise(x: torch.Tensor):
     """[rows, cols] float -> (int8 [rows, cols], float32 [rows, 1])
     (int8_fused_kernel.py:67-85)."""
-    return ops.quant_act_int8(x)
+    return kops.quant_act_int8(x)
 
 
 def _linear(x, weight, weight_scale, bias, compute_dtype, x_q, per_row):
     shape = x.shape
     if x_q is None:
-        x_int8, x_scale = ops.quant_act_int8(x.reshape(-1, shape[-1]))
+        x_int8, x_scale = kops.quant_act_int8(x.reshape(-1, shape[-1]))
     else:
         x_int8, x_scale = x_q
     n = weight.shape[0]
     if not isinstance(weight_scale, torch.Tensor):
         weight_scale = torch.tensor([float(weight_scale)], dtype=torch.float32, device=x_int8.device)
-    out = ops.gemm_w8a8(x_int8, x_scale, weight.to(x_int8.device), weight_scale, bias, compute_dtype,
+    out = kops.gemm_w8a8(x_int8, x_scale, weight.to(x_int8.device), weight_scale, bias, compute_dtype,
                         per_row=per_row)
     return out.reshape(tuple(shape[:-1]) + (n,))
 
@@ -52,4 +52,4 @@ def triton_int8_linear_per_row(x, weight, weight_scale, bias=None, compute_dtype
 def triton_situ(x: torch.Tensor) -> torch.Tensor:
     """[..., 2K] ([hidden | gate]) -> [..., K] SiTU activation
     (int8_fused_kernel.py:389-440)."""
-    return ops.situ(x)
+    return kops.situ(x)

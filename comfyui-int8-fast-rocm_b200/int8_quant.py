@@ -17,7 +17,7 @@ import torch
 from torch import Tensor, nn
 import torch.nn.functional as F
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 
 # Runtime toggle kept for API compatibility (the reference switches between
 # Triton and torch._int_mm with it); this build always runs its own kernels.
@@ -45,7 +45,7 @@ def _rows2d(x: Tensor) -> Tensor:
 def quantize_int8(x: Tensor, scale) -> Tensor:
     """round(x.float() * (1/scale)).clamp(-128, 127) -> int8 with a given
     scalar or per-row [N,1] scale."""
-    return ops.requant_int8(_rows2d(x.float()), scale).reshape(x.shape)
+    return kops.requant_int8(_rows2d(x.float()), scale).reshape(x.shape)
 
 
 def quantize_int8_tensorwise(x: Tensor):
@@ -59,20 +59,20 @@ def quantize_int8_axiswise(x: Tensor, dim: int):
     dim=1 for a 2-D weight)."""
     if dim not in (-1, x.dim() - 1):
         raise ValueError("quantize_int8_axiswise supports the last axis (dim=-1, or dim=1 for 2-D weights)")
-    q, s = ops.quant_act_int8(_rows2d(x))
+    q, s = kops.quant_act_int8(_rows2d(x))
     return q.reshape(x.shape), s.reshape(tuple(x.shape[:-1]) + (1,))
 
 
 def dequantize(q: Tensor, scale) -> Tensor:
     """q.float() * scale (float32)."""
-    return ops.dequant_int8(_rows2d(q), scale).reshape(q.shape)
+    return kops.dequant_int8(_rows2d(q), scale).reshape(q.shape)
 
 
 def stochastic_round_int8_delta(x: Tensor, scale, seed: int = 0) -> Tensor:
     """Stochastic int8 rounding of x/scale (int8_quant.py:80-106): floor +1
     with probability equal to the fraction.  The kernel's counter-based RNG
     draws differ from torch.Generator's stream (same law)."""
-    return ops.requant_int8(_rows2d(x.float()), scale, stochastic=True, seed=seed).reshape(x.shape)
+    return kops.requant_int8(_rows2d(x.float()), scale, stochastic=True, seed=seed).reshape(x.shape)
 
 
 # --- W8A8 forward (int8_quant.py:113-164) ------------------------------------
@@ -81,18 +81,18 @@ def stochastic_round_int8_delta(x: Tensor, scale, seed: int = 0) -> Tensor:
 @torch.no_grad()
 def int8_forward_dynamic(x: Tensor, weight: Tensor, weight_scale, bias, compute_dtype, rot=None) -> Tensor:
     """Per-token activation quant + W8A8 GEMM with a scalar weight scale."""
-    xq, xs = ops.quant_act_int8(x, rot)
+    xq, xs = kops.quant_act_int8(x, rot)
     if not isinstance(weight_scale, torch.Tensor):
         weight_scale = torch.tensor([float(weight_scale)], dtype=torch.float32, device=x.device)
-    return ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=False)
+    return kops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=False)
 
 
 @torch.no_grad()
 def int8_forward_dynamic_per_row(x: Tensor, weight: Tensor, weight_scale: Tensor, bias, compute_dtype,
                                  rot=None) -> Tensor:
     """Per-token activation quant + W8A8 GEMM with per-row weight scales."""
-    xq, xs = ops.quant_act_int8(x, rot)
-    return ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=True)
+    xq, xs = kops.quant_act_int8(x, rot)
+    return kops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=True)
 
 
 @torch.no_grad()
@@ -119,16 +119,16 @@ def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dt
     if x2 is not None:
         if prologue:
             raise ValueError("a concatenated input takes no norm / modulation prologue")
-        xq, xs = ops.quant_act_int8_cat(x, x2, rot)
+        xq, xs = kops.quant_act_int8_cat(x, x2, rot)
     elif prologue:
-        xq, xs = ops.quant_act_int8_norm(x, rot, norm, eps, norm_weight, mod_mul, mod_add, rows_per_sample)
+        xq, xs = kops.quant_act_int8_norm(x, rot, norm, eps, norm_weight, mod_mul, mod_add, rows_per_sample)
     else:
-        xq, xs = ops.quant_act_int8(x, rot)
+        xq, xs = kops.quant_act_int8(x, rot)
     if not per_row and not isinstance(weight_scale, torch.Tensor):
         weight_scale = torch.tensor([float(weight_scale)], dtype=torch.float32, device=x.device)
     if gelu_from is None and residual is None:
-        return ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row)
-    return ops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row,
+        return kops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row)
+    return kops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row,
                                gelu_from=gelu_from, residual=residual, gate=gate, rows_per_gate=rows_per_gate)
 
 
@@ -138,9 +138,9 @@ def lowvram_patch_int8(weight: Tensor, scale, convrot_groupsize, delta_fn, stoch
     float-space patch, e.g. comfy.lora.calculate_weight) -> re-rotate ->
     requantise with the ORIGINAL scale (RNE or stochastic)."""
     rot = rot_for_group(convrot_groupsize) if convrot_groupsize else None
-    w = ops.dequant_int8(weight, scale, rot)
+    w = kops.dequant_int8(weight, scale, rot)
     w = delta_fn(w)
-    return ops.requant_int8(w, scale, rot, stochastic=stochastic, seed=seed)
+    return kops.requant_int8(w, scale, rot, stochastic=stochastic, seed=seed)
 
 
 # =============================================================================
@@ -315,7 +315,7 @@ if _COMFY_OPS_AVAILABLE:
                     rot = rot_for_group(CONVROT_GROUP_SIZE)
                     self._use_convrot = True
                     self._convrot_groupsize = CONVROT_GROUP_SIZE
-                q, s = ops.quant_weight_int8(w, rot)
+                q, s = kops.quant_weight_int8(w, rot)
                 self.weight = nn.Parameter(q.cpu(), requires_grad=False)
                 self.register_buffer("weight_scale", s.cpu())
                 self._weight_scale_scalar = None
@@ -491,7 +491,7 @@ if _COMFY_OPS_AVAILABLE:
                 key = (weight.device, weight.data_ptr())
                 hit = self._w4a8_cache.get(key)
                 if hit is None:
-                    hit = ops.requant_asym_w4a8(weight, self._w4a8_codebook, self._w4a8_s_channel,
+                    hit = kops.requant_asym_w4a8(weight, self._w4a8_codebook, self._w4a8_s_channel,
                                                 self._w4a8_s_rel, self._w4a8_group_size)
                     self._w4a8_cache = {key: hit}
                 return hit
@@ -542,7 +542,7 @@ if _COMFY_OPS_AVAILABLE:
                     # rounding at the store), so the sum is bit-equal to the
                     # eager add and y is written once
                     lora_down, lora_up = patches[0][0], patches[0][1]
-                    x_l = ops.rotate(x_2d, *rot) if rot is not None else x_2d
+                    x_l = kops.rotate(x_2d, *rot) if rot is not None else x_2d
                     lD = lora_down.to(x.device, non_blocking=True)
                     lU = lora_up.to(x.device, non_blocking=True)
                     lora_y = F.linear(F.linear(x_l.to(lD.dtype), lD), lU).to(compute_dtype)
@@ -557,7 +557,7 @@ if _COMFY_OPS_AVAILABLE:
                 if patches:
                     # dynamic LoRA (int8_quant.py:718-729): down-projection of
                     # the (rotated) activation, up-projection, added to y
-                    x_l = ops.rotate(x_2d, *rot) if rot is not None else x_2d
+                    x_l = kops.rotate(x_2d, *rot) if rot is not None else x_2d
                     for lora_down, lora_up, lora_start, lora_size in patches:
                         lD = lora_down.to(x.device, non_blocking=True)
                         lU = lora_up.to(x.device, non_blocking=True)
@@ -641,7 +641,7 @@ def _dynamic_lora_entries(module, patches, rot, group_ok):
         if mid is not None:
             down_scaled = torch.mm(mid.flatten(1), down.flatten(1)) * scale
         if rot is not None and group_ok(down_scaled.shape[1]):
-            down_scaled = ops.rotate(down_scaled.to(torch.float32).cuda(), *rot).to(down_scaled.dtype)
+            down_scaled = kops.rotate(down_scaled.to(torch.float32).cuda(), *rot).to(down_scaled.dtype)
         start = size = None
         if offset is not None:
             _dim, start, size = offset

@@ -21,7 +21,7 @@ import logging
 
 import torch
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 from .int8_quant import rot_for_group
 
 log = logging.getLogger("comfyui-int8-fast-b200")
@@ -69,11 +69,11 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
                 input_act=None, input_act_weight=None, input_act_eps: float = 0.0, residual=None,
                 residual_scale=None) -> torch.Tensor:
     # SiTU of 16-bit rows of 16-element multiples runs inside the activation
-    # quantiser (bit-equal to ops.situ followed by ops.quant_act_int8)
+    # quantiser (bit-equal to kops.situ followed by kops.quant_act_int8)
     fuse_situ = (input_act == "situ" and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16)
                  and x.shape[-1] % 32 == 0)
     if input_act == "situ" and not fuse_situ:
-        x = ops.situ(x)
+        x = kops.situ(x)
     if input_act == "situ":
         input_act = None
     k_in = x.shape[-1] // 2 if fuse_situ else x.shape[-1]
@@ -99,19 +99,19 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     shape = (*x.shape[:-1], k_in)
     x2 = x.reshape(-1, x.shape[-1])
     if fuse_situ:
-        xq, xs = ops.quant_act_int8_situ(x2, rot)
+        xq, xs = kops.quant_act_int8_situ(x2, rot)
     elif fuse_rms:
-        xq, xs = ops.quant_act_int8_norm(x2, rot, "rms", float(input_act_eps), input_act_weight)
+        xq, xs = kops.quant_act_int8_norm(x2, rot, "rms", float(input_act_eps), input_act_weight)
     else:
-        xq, xs = ops.quant_act_int8(x2, rot)
+        xq, xs = kops.quant_act_int8(x2, rot)
     out_shape = (*shape[:-1], weight.shape[0])
     per_row = weight_scale.numel() > 1
     if _fusable_residual(residual, residual_scale, out_shape, out_dtype):
-        out = ops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, out_dtype, per_row=per_row,
+        out = kops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, out_dtype, per_row=per_row,
                                   residual=residual.reshape(-1, weight.shape[0]),
                                   gate=None if residual_scale is None else residual_scale.reshape(1, -1))
         return out.reshape(out_shape)
-    out = ops.gemm_w8a8(xq, xs, weight, weight_scale, bias, out_dtype, per_row=per_row)
+    out = kops.gemm_w8a8(xq, xs, weight, weight_scale, bias, out_dtype, per_row=per_row)
     out = out.reshape(out_shape)
     if ck_quant is not None:
         return ck_quant._apply_residual(out, residual, residual_scale)

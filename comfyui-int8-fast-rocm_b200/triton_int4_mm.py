@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from . import ops
+from . import library as kops  # the kernels as registered torch.library operators
 
 
 def triton_int4_mm(a: torch.Tensor, packed_weight: torch.Tensor, out_dtype: torch.dtype = torch.int32) -> torch.Tensor:
@@ -24,5 +24,5 @@ def triton_int4_mm(a: torch.Tensor, packed_weight: torch.Tensor, out_dtype: torc
     N, K_packed = packed_weight.shape
     assert K == K_packed * 2, f"K mismatch: activation K={K}, packed weight represents {K_packed * 2}"
     assert K % 2 == 0
-    c = ops.int4_mm(a, packed_weight)
+    c = kops.int4_mm(a, packed_weight)
     return c if out_dtype == torch.int32 else c.to(out_dtype)
