@@ -21,6 +21,7 @@ from . import w4a8_int8  # noqa: F401
 from . import int8_quant  # noqa: F401
 from . import int4_quant  # noqa: F401
 from . import tensor_parallel  # noqa: F401
+from . import int8_save  # noqa: F401
 
 log = logging.getLogger("comfyui-int8-fast-b200")
 

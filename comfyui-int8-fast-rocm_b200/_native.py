@@ -55,6 +55,7 @@ SIGNATURES = {
     "qlin_quant_weight_int8": [_P, _I, _L, _L, _I, _I, _F, _P, _P, _P],
     "qlin_quant_weight_int4": [_P, _I, _L, _L, _I, _I, _F, _I, _P, _P, _P],
     "qlin_requant_asym_w4a8": [_P, _P, _P, _P, _I, _L, _L, _P, _P, _P],
+    "qlin_dequant_asym_w4a8": [_P, _P, _P, _P, _I, _L, _L, _P, _P],
     "qlin_dequant_int8": [_P, _P, _I, _L, _L, _I, _I, _F, _P, _P],
     "qlin_requant_int8": [_P, _P, _I, _L, _L, _I, _I, _F, _I, _U64, _P, _P],
 }

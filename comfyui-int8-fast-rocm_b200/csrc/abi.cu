@@ -467,7 +467,22 @@ QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook
   if (rc) return rc;
   if (K % 32 || !aligned16(packed) || !aligned16(q))
     return fail(QLIN_ERR_ALIGNMENT, "need K % 32 == 0 and 16-byte alignment");
-  return launch_requant_asym_w4a8(packed, codebook, s_channel, s_rel_fp8, group_size, N, K, q, scale,
+  return launch_requant_asym_w4a8(packed, codebook, s_channel, s_rel_fp8, group_size, N, K, q, scale, nullptr,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+QLIN_API int qlin_dequant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
+                                    const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K, float* out,
+                                    void* stream) {
+  if (N < 0 || K < 0 || group_size <= 0 || K % group_size)
+    return fail(QLIN_ERR_INVALID_ARG, "bad shape / group_size");
+  if (N == 0 || K == 0) return QLIN_OK;
+  if (!packed || !codebook || !s_channel || !s_rel_fp8 || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  if (K % 32 || !aligned16(packed) || !aligned16(out))
+    return fail(QLIN_ERR_ALIGNMENT, "need K % 32 == 0 and 16-byte alignment");
+  return launch_requant_asym_w4a8(packed, codebook, s_channel, s_rel_fp8, group_size, N, K, nullptr, nullptr, out,
                                   static_cast<cudaStream_t>(stream));
 }
 

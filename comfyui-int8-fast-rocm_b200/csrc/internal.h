@@ -97,9 +97,11 @@ int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, 
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
                      int64_t K, cudaStream_t stream);
 
+// Asymmetric W4A8 rows: int8 requantisation (q, scale), or with wout set the
+// float32 dequantised rows only.
 int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
                              const uint8_t* s_rel, int group_size, int64_t N, int64_t K, int8_t* q, float* scale,
-                             cudaStream_t stream);
+                             float* wout, cudaStream_t stream);
 
 int launch_situ(int dt, const void* x, int64_t ldx, int64_t M, int64_t K, void* y, cudaStream_t stream);
 

@@ -12,13 +12,15 @@ namespace {
 
 // One row per CTA; each thread owns 16 consecutive k (8 packed bytes).
 // w[n,k] = (codebook[code] * s_channel[n]) * s_rel[n, k / gs]  (w4a8_int8.py:46-75)
-// then quantize_int8_axiswise(dim=1): absmax/127 clamped at 1e-30, rint(w * (1/s)).
+// then either (wout != null) the float32 row itself, or
+// quantize_int8_axiswise(dim=1): absmax/127 clamped at 1e-30, rint(w * (1/s)).
 __global__ void __launch_bounds__(1024) requant_asym_w4a8_kernel(const uint8_t* __restrict__ packed,
                                                                    const float* __restrict__ codebook,
                                                                    const float* __restrict__ s_channel,
                                                                    const uint8_t* __restrict__ s_rel, int gs,
                                                                    int N, int K, int8_t* __restrict__ q,
-                                                                   float* __restrict__ scale) {
+                                                                   float* __restrict__ scale,
+                                                                   float* __restrict__ wout) {
   __shared__ float cb[16];
   __shared__ float red[32];
   const int n = blockIdx.x;
@@ -45,6 +47,14 @@ __global__ void __launch_bounds__(1024) requant_asym_w4a8_kernel(const uint8_t* 
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+  }
+  if (wout != nullptr) {  // float32 dequantisation only (uniform over the grid)
+    if (active) {
+      float4* d = reinterpret_cast<float4*>(wout + (int64_t)n * K + t * 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    return;
   }
   float a = 0.0f;
 #pragma unroll
@@ -105,11 +115,11 @@ int launch_situ(int dt, const void* x, int64_t ldx, int64_t M, int64_t K, void* 
 
 int launch_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
                              const uint8_t* s_rel, int group_size, int64_t N, int64_t K, int8_t* q, float* scale,
-                             cudaStream_t stream) {
-  if (K > 16384) return fail(QLIN_ERR_UNSUPPORTED, "asym W4A8 requant supports K <= 16384");
+                             float* wout, cudaStream_t stream) {
+  if (K > 16384) return fail(QLIN_ERR_UNSUPPORTED, "asym W4A8 kernels support K <= 16384");
   const int threads = (int)(((K / 16) + 31) / 32 * 32);
   requant_asym_w4a8_kernel<<<(unsigned)N, threads, 0, stream>>>(packed, codebook, s_channel, s_rel, group_size,
-                                                                 (int)N, (int)K, q, scale);
+                                                                 (int)N, (int)K, q, scale, wout);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "requant_asym_w4a8 launch");
   return QLIN_OK;

@@ -15,6 +15,7 @@ from torch import Tensor, nn
 import torch.nn.functional as F
 
 from . import library as kops  # the kernels as registered torch.library operators
+from .linear_common import QuantLowVramPatch, calc_weight_entries, float_forward, init_linear, store_param
 from .int8_quant import (_normalize_lora_key, _parse_comfy_quant, _pop_metadata, int8_forward_dynamic,
                          int8_forward_dynamic_per_row, rot_for_group)
 
@@ -208,17 +209,7 @@ if _COMFY_OPS_AVAILABLE:
 
         class Linear(manual_cast.Linear):
             def __init__(self, in_features, out_features, bias=True, device=None, dtype=None):
-                if getattr(Int4ConvRotOps, "skeleton_meta_init", False):
-                    nn.Module.__init__(self)
-                    self.in_features = in_features
-                    self.out_features = out_features
-                    kw = {"device": "meta"}
-                    if dtype is not None:
-                        kw["dtype"] = dtype
-                    self.weight = nn.Parameter(torch.empty((out_features, in_features), **kw), requires_grad=False)
-                    self.bias = nn.Parameter(torch.empty((out_features,), **kw), requires_grad=False) if bias else None
-                else:
-                    super().__init__(in_features, out_features, bias, device, dtype)
+                init_linear(self, Int4ConvRotOps, super().__init__, in_features, out_features, bias, device, dtype)
                 self.register_buffer("weight_scale", None)
                 self._is_quantized = False
                 self._convrot_groupsize = Int4ConvRotOps.convrot_groupsize
@@ -253,11 +244,10 @@ if _COMFY_OPS_AVAILABLE:
                 Int4ConvRotOps.applied_lora_patches.add(nk)
                 import comfy.lora
                 import comfy.model_management
-                formatted = [(p[3] if len(p) == 4 else Int4ConvRotOps.lora_strength, p[0], 1.0, p[1], p[2])
-                             for p in patches]
                 dev = torch.device("cuda") if torch.cuda.is_available() else tensor.device
                 tmp = tensor.to(dev).to(comfy.model_management.lora_compute_dtype(dev))
-                return comfy.lora.calculate_weight(formatted, tmp, key).to(tensor.dtype)
+                entries = calc_weight_entries(patches, Int4ConvRotOps.lora_strength)
+                return comfy.lora.calculate_weight(entries, tmp, key).to(tensor.dtype)
 
             def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
                                       unexpected_keys, error_msgs):
@@ -326,41 +316,23 @@ if _COMFY_OPS_AVAILABLE:
 
             def set_weight(self, out_weight, inplace_update=False, seed=0, return_weight=False, **kwargs):
                 if not self._is_quantized:
-                    new_weight = out_weight.to(self.weight.dtype)
+                    value = out_weight.to(self.weight.dtype)
                 elif out_weight.dtype == torch.int8:
-                    new_weight = out_weight
-                else:
-                    q, s = quantize_convrot_w4a4_weight(out_weight.float(), self._convrot_groupsize)
-                    new_weight = q
-                    self.register_buffer("weight_scale", s.to(self.weight_scale.device))
-                if return_weight:
-                    return new_weight
-                if inplace_update:
-                    self.weight.data.copy_(new_weight)
-                else:
-                    self.weight = nn.Parameter(new_weight, requires_grad=False)
+                    value = out_weight
+                else:  # a float patch result: requantised, and the scale follows it
+                    value, scale = quantize_convrot_w4a4_weight(out_weight.float(), self._convrot_groupsize)
+                    self.register_buffer("weight_scale", scale.to(self.weight_scale.device))
+                return store_param(self, "weight", value, inplace_update, return_weight)
 
             def set_bias(self, out_bias, inplace_update=False, seed=0, return_weight=False, **kwargs):
                 if out_bias is None:
                     return None
-                if return_weight:
-                    return out_bias
-                if inplace_update and self.bias is not None:
-                    self.bias.data.copy_(out_bias)
-                else:
-                    self.bias = nn.Parameter(out_bias, requires_grad=False)
+                return store_param(self, "bias", out_bias, inplace_update, return_weight, inplace_creates=True)
 
             def forward(self, x: Tensor) -> Tensor:
                 need_cast = self.comfy_cast_weights or len(self.weight_function) > 0 or len(self.bias_function) > 0
                 if not self._is_quantized:
-                    if need_cast:
-                        weight, bias, offload_stream = cast_bias_weight(self, x, offloadable=True)
-                        out = F.linear(x, weight, bias)
-                        uncast_bias_weight(self, weight, bias, offload_stream)
-                        return out
-                    weight = self.weight.to(device=x.device, dtype=x.dtype)
-                    bias = self.bias.to(device=x.device, dtype=x.dtype) if self.bias is not None else None
-                    return F.linear(x, weight, bias)
+                    return float_forward(self, x, need_cast, cast_bias_weight, uncast_bias_weight)
 
                 if need_cast:
                     weight, bias, offload_stream = cast_bias_weight(
@@ -476,27 +448,11 @@ if _COMFY_PATCHER_AVAILABLE:
         return getattr(module, "_is_quantized", False) and \
             getattr(module, "_linear_dtype", None) in ("int4", "int8_tensorwise")
 
-    class Int4LowVramPatch:
+    class Int4LowVramPatch(QuantLowVramPatch):
         """Low-VRAM LoRA on an INT4 model layer as ComfyUI streams it in
         (int4_quant.py:1018-1060)."""
-        is_lowvram_patch = True
 
-        def __init__(self, key, patches, module, lora_mode):
-            self.key, self.patches, self.module, self.lora_mode = key, patches, module, lora_mode
-            self.prepared_patches = None
-
-        def memory_required(self):
-            return 0
-
-        def prepare(self, *args, **kwargs):
-            self.prepared_patches = list(self.patches[self.key])
-            return self.prepared_patches
-
-        def clear_prepared(self):
-            self.prepared_patches = None
-
-        def __call__(self, weight):
-            patches = self.prepared_patches if self.prepared_patches is not None else self.patches[self.key]
+        def apply(self, weight, patches):
             stochastic = self.lora_mode == "Stochastic"
             return bake_int4_layer_weight(
                 self.module, weight,

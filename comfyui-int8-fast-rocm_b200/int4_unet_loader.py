@@ -6,7 +6,6 @@ of a high-precision model while loading; pre-loaded LoRAs are baked before
 quantisation and the model is wrapped in ``Int4ModelPatcher``."""
 from __future__ import annotations
 
-import json
 import logging
 
 import torch
@@ -15,47 +14,18 @@ import comfy.sd
 import comfy.utils
 
 from .int4_quant import CONVROT_W4A4_GROUP_SIZE, MODEL_TYPE_EXCLUSIONS, Int4ConvRotOps, Int4ModelPatcher
-from .loader_common import (COMPUTE_DTYPES, group_pre_loras, normalize_lora_mode, pre_lora_list, report_unmatched,
-                            stash_metadata)
+from .loader_common import (COMPUTE_DTYPES, bridge_header_quant_metadata, group_pre_loras, normalize_lora_mode,
+                            pre_lora_list, report_unmatched, stash_metadata)
 
 INT4_MODEL_TYPES = ["flux2", "z-image", "ideogram4", "chroma", "krea2", "wan", "ltx2", "qwen", "ernie", "anima",
                     "hidream o1", "boogu"]
 
 
 def bridge_convrot_w4a4_metadata(sd, metadata) -> int:
-    """Copy per-layer ``convrot_w4a4`` entries of the safetensors header's
-    ``_quantization_metadata`` into ``<layer>.comfy_quant`` tensors where the
-    state dict lacks them (int4_unet_loader.py:82-130).  Returns the number
-    of layers bridged."""
-    if not metadata or "_quantization_metadata" not in metadata:
-        return 0
-    try:
-        layers = json.loads(metadata["_quantization_metadata"]).get("layers", {})
-    except Exception as e:
-        logging.warning(f"INT4 ConvRot: failed to parse _quantization_metadata: {e}")
-        return 0
-    bridged = 0
-    for layer, conf in layers.items():
-        if conf.get("format") != "convrot_w4a4":
-            continue
-        candidates = (layer + ".weight", "model." + layer + ".weight", "diffusion_model." + layer + ".weight",
-                      "model.diffusion_model." + layer + ".weight")
-        wkey = next((k for k in candidates if k in sd), None)
-        if wkey is None:
-            suffix = layer + ".weight"
-            matches = [k for k in sd if k == suffix or k.endswith("." + suffix)]
-            wkey = matches[0] if len(matches) == 1 else None
-        if wkey is None:
-            logging.warning(f"INT4 ConvRot: metadata bridge found no weight for quantized layer '{layer}'")
-            continue
-        qkey = wkey[:-len(".weight")] + ".comfy_quant"
-        if qkey not in sd:
-            payload = json.dumps(conf, separators=(",", ":")).encode("utf-8")
-            sd[qkey] = torch.tensor(list(payload), dtype=torch.uint8)
-        bridged += 1
-    if bridged:
-        logging.info(f"INT4 ConvRot: bridged safetensors header metadata for {bridged} convrot_w4a4 layers")
-    return bridged
+    """``<layer>.comfy_quant`` markers for the ``convrot_w4a4`` layers listed in
+    the safetensors header (int4_unet_loader.py:82-130); see
+    :func:`loader_common.bridge_header_quant_metadata`."""
+    return bridge_header_quant_metadata(sd, metadata, ("convrot_w4a4",), "INT4 ConvRot")
 
 
 class UNetLoaderINT4ConvRot:

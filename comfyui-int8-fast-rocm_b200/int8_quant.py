@@ -18,6 +18,8 @@ from torch import Tensor, nn
 import torch.nn.functional as F
 
 from . import library as kops  # the kernels as registered torch.library operators
+from .linear_common import (QuantLowVramPatch, calc_weight_entries, float_forward, init_linear, scale_layout,
+                            store_param)
 
 # Runtime toggle kept for API compatibility (the reference switches between
 # Triton and torch._int_mm with it); this build always runs its own kernels.
@@ -218,17 +220,7 @@ if _COMFY_OPS_AVAILABLE:
 
         class Linear(manual_cast.Linear):
             def __init__(self, in_features, out_features, bias=True, device=None, dtype=None):
-                if getattr(Int8TensorwiseOps, "skeleton_meta_init", False):
-                    nn.Module.__init__(self)
-                    self.in_features = in_features
-                    self.out_features = out_features
-                    kw = {"device": "meta"}
-                    if dtype is not None:
-                        kw["dtype"] = dtype
-                    self.weight = nn.Parameter(torch.empty((out_features, in_features), **kw), requires_grad=False)
-                    self.bias = nn.Parameter(torch.empty((out_features,), **kw), requires_grad=False) if bias else None
-                else:
-                    super().__init__(in_features, out_features, bias, device, dtype)
+                init_linear(self, Int8TensorwiseOps, super().__init__, in_features, out_features, bias, device, dtype)
                 self.register_buffer("weight_scale", None)
                 self._is_quantized = False
                 self._is_per_row = False
@@ -251,18 +243,9 @@ if _COMFY_OPS_AVAILABLE:
 
             @staticmethod
             def _format_lora_patches(patches):
-                """Grouped pre-LoRA entries (value, offset, function[, strength])
-                -> the (strength, value, 1.0, offset, function) tuples that
-                comfy.lora.calculate_weight consumes (int8_quant.py:256-265)."""
-                formatted = []
-                for patch in patches or []:
-                    if len(patch) == 4:
-                        v, offset, function, strength = patch
-                    else:
-                        v, offset, function = patch
-                        strength = getattr(Int8TensorwiseOps, "lora_strength", 1.0)
-                    formatted.append((strength, v, 1.0, offset, function))
-                return formatted
+                """Grouped pre-LoRA entries as comfy.lora.calculate_weight
+                entries (int8_quant.py:256-265)."""
+                return calc_weight_entries(patches, getattr(Int8TensorwiseOps, "lora_strength", 1.0))
 
             def _apply_int8_lora_patches(self, tensor, key, patches, device):
                 """Bake pre-LoRA patches into a float weight in ComfyUI's LoRA
@@ -322,133 +305,123 @@ if _COMFY_OPS_AVAILABLE:
                 self._is_quantized = True
                 self._is_per_row = True
 
+            # pre-LoRA patches grouped by the loader (int8_quant.py:335-453) are
+            # baked into float weights and biases before any quantisation, or
+            # deferred to model load when a dynamic load device is set
+            @staticmethod
+            def _pre_lora_patches(key):
+                table = Int8TensorwiseOps.lora_patches
+                return table.get(_normalize_lora_key(key)) if table else None
+
+            @staticmethod
+            def _mark_pre_lora_applied(key):
+                if getattr(Int8TensorwiseOps, "applied_lora_patches", None) is None:
+                    Int8TensorwiseOps.applied_lora_patches = set()
+                Int8TensorwiseOps.applied_lora_patches.add(_normalize_lora_key(key))
+
+            def _bake_pre_lora(self, tensor, key):
+                if tensor is None or tensor.dtype == torch.int8:
+                    return tensor
+                patches = self._pre_lora_patches(key)
+                if not patches:
+                    return tensor
+                self._mark_pre_lora_applied(key)
+                device = getattr(Int8TensorwiseOps, "dynamic_load_device", None) or tensor.device
+                return self._apply_int8_lora_patches(tensor, key, patches, device).to(tensor.dtype)
+
+            def _keep_float(self, weight):
+                self._is_quantized = False
+                self.weight = nn.Parameter(weight, requires_grad=False)
+
+            def _set_quantized_weight(self, weight, per_row):
+                self.weight = nn.Parameter(weight, requires_grad=False)
+                self._is_quantized = True
+                self._is_per_row = per_row
+                Int8TensorwiseOps._is_prequantized = True
+
+            def _take_asym_w4a8(self, state_dict, prefix, weight, conf, wkey):
+                """asym_w4a8_int8 layer (w4a8_int8.py layout): packed codes
+                plus codebook, channel and group scales; False (and the layer
+                falls through to the generic path) when a part is missing."""
+                if weight is None or weight.dtype != torch.int8:
+                    logging.warning(f"asym W4A8: no packed int8 codes under {wkey}; loading the layer as stored")
+                    return False
+                parts = [_pop_metadata(state_dict, prefix, f"weight_{n}") for n in ("codebook", "s_channel", "s_rel")]
+                if any(t is None for t in parts):
+                    logging.warning(f"asym W4A8: {wkey} comes without codebook or scales; loading the layer as stored")
+                    return False
+                self._w4a8_codebook, self._w4a8_s_channel, self._w4a8_s_rel = parts
+                self._w4a8_group_size = int(conf.get("group_size", 16))
+                self._is_w4a8 = True
+                self._set_quantized_weight(weight, per_row=True)
+                return True
+
+            def _take_float(self, weight, prefix, wkey, pending_lora):
+                """A float weight: quantised now (on the fly), at model load
+                (dynamic load device), or kept in its precision (excluded
+                layers, vectors, quantisation off)."""
+                ops = Int8TensorwiseOps
+                quantize = (ops.dynamic_quantize and not any(ex in prefix for ex in ops.excluded_names)
+                            and 1 not in (self.in_features, self.out_features) and weight.ndim != 1)
+                load_dev = getattr(ops, "dynamic_load_device", None)
+                if load_dev is not None and (quantize or pending_lora):
+                    self._keep_float(weight)
+                    self._pending_int8_finalize = {"weight_key": wkey, "quantize": quantize, "lora_patches": pending_lora,
+                                                   "device": load_dev,
+                                                   "enable_convrot": getattr(ops, "enable_convrot", False)}
+                    if pending_lora:
+                        self._mark_pre_lora_applied(wkey)
+                elif quantize:
+                    if not getattr(ops, "_logged_otf", False):
+                        logging.info(f"INT8 Fast B200: on-the-fly W8A8 quantisation while loading "
+                                     f"(ConvRot {'on' if ops.enable_convrot else 'off'})")
+                        ops._logged_otf = True
+                    self._otf_quantize(weight)
+                else:
+                    self._keep_float(weight)
+
             def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
                                       unexpected_keys, error_msgs):
-                weight_key = prefix + "weight"
-                bias_key = prefix + "bias"
-                weight_scale = _pop_metadata(state_dict, prefix, "weight_scale")
+                """The layer's tensors in any of the formats of
+                int8_quant.py:328-577: asym_w4a8_int8, int8 with a
+                weight_scale (per row or tensor-wide, optional ConvRot), or a
+                float weight."""
+                wkey, bkey = prefix + "weight", prefix + "bias"
+                scale = _pop_metadata(state_dict, prefix, "weight_scale")
                 conf = _parse_comfy_quant(_pop_metadata(state_dict, prefix, "comfy_quant"))
-                weight_tensor = state_dict.pop(weight_key, None)
-                bias_tensor = state_dict.pop(bias_key, None)
+                conf = conf if isinstance(conf, dict) else {}
+                weight, bias = state_dict.pop(wkey, None), state_dict.pop(bkey, None)
                 state_dict.pop(prefix + "input_scale", None)
 
-                # pre-LoRA patches grouped by the loader (int8_quant.py:335-453):
-                # baked into float weights/biases before any quantisation;
-                # deferred to model load when a dynamic load device is set
-                lora_table = Int8TensorwiseOps.lora_patches or {}
-
-                def _note_applied(key):
-                    if not hasattr(Int8TensorwiseOps, "applied_lora_patches"):
-                        Int8TensorwiseOps.applied_lora_patches = set()
-                    Int8TensorwiseOps.applied_lora_patches.add(key)
-
-                def _bake(tensor, key):
-                    if tensor is None or tensor.dtype == torch.int8 or not lora_table:
-                        return tensor
-                    patches = lora_table.get(_normalize_lora_key(key))
-                    if not patches:
-                        return tensor
-                    _note_applied(_normalize_lora_key(key))
-                    device = getattr(Int8TensorwiseOps, "dynamic_load_device", None) or tensor.device
-                    return self._apply_int8_lora_patches(tensor, key, patches, device).to(tensor.dtype)
-
-                pending_weight_lora = None
-                if weight_tensor is not None and weight_tensor.dtype != torch.int8 and lora_table:
-                    pending_weight_lora = lora_table.get(_normalize_lora_key(weight_key))
-                defer_weight_lora = (getattr(Int8TensorwiseOps, "dynamic_load_device", None) is not None
-                                     and bool(pending_weight_lora))
-                if not defer_weight_lora:
-                    weight_tensor = _bake(weight_tensor, weight_key)
-                bias_tensor = _bake(bias_tensor, bias_key)
-
-                if isinstance(conf, dict) and conf.get("convrot", False):
+                pending_lora = (self._pre_lora_patches(wkey)
+                                if weight is not None and weight.dtype != torch.int8 else None)
+                if not (pending_lora and getattr(Int8TensorwiseOps, "dynamic_load_device", None) is not None):
+                    weight = self._bake_pre_lora(weight, wkey)
+                bias = self._bake_pre_lora(bias, bkey)
+                if conf.get("convrot", False):
                     self._use_convrot = True
                     Int8TensorwiseOps.enable_convrot = True
-                    if "convrot_groupsize" in conf:
-                        self._convrot_groupsize = int(conf["convrot_groupsize"])
+                    self._convrot_groupsize = int(conf.get("convrot_groupsize", self._convrot_groupsize))
 
-                w4a8_handled = False
-                if isinstance(conf, dict) and conf.get("format") == "asym_w4a8_int8":
-                    if weight_tensor is None or weight_tensor.dtype != torch.int8:
-                        logging.warning(f"W4A8: {weight_key} missing packed int8 weight, skipping")
-                    else:
-                        codebook = _pop_metadata(state_dict, prefix, "weight_codebook")
-                        s_channel = _pop_metadata(state_dict, prefix, "weight_s_channel")
-                        s_rel = _pop_metadata(state_dict, prefix, "weight_s_rel")
-                        if codebook is None or s_channel is None or s_rel is None:
-                            logging.warning(f"W4A8: {weight_key} missing codebook/s_channel/s_rel, skipping")
-                        else:
-                            self._is_w4a8 = True
-                            self._w4a8_group_size = int(conf.get("group_size", 16))
-                            self._w4a8_codebook = codebook
-                            self._w4a8_s_channel = s_channel
-                            self._w4a8_s_rel = s_rel
-                            self.weight = nn.Parameter(weight_tensor, requires_grad=False)
-                            self._is_quantized = True
-                            self._is_per_row = True
-                            Int8TensorwiseOps._is_prequantized = True
-                            w4a8_handled = True
-                            weight_tensor = None
+                if conf.get("format") == "asym_w4a8_int8" and self._take_asym_w4a8(state_dict, prefix, weight, conf,
+                                                                                   wkey):
+                    pass
+                elif weight is None:
+                    missing_keys.append(wkey)
+                elif weight.dtype == torch.int8 and scale is not None:
+                    buf, per_row = scale_layout(scale, conf.get("per_row"))
+                    self._set_quantized_weight(weight, per_row)
+                    self.register_buffer("weight_scale", buf)
+                elif weight.dtype in (torch.float16, torch.bfloat16, torch.float32):
+                    self._take_float(weight, prefix, wkey, pending_lora)
+                else:
+                    self._keep_float(weight)
 
-                if weight_tensor is not None:
-                    if weight_tensor.dtype == torch.int8 and weight_scale is not None:
-                        self._is_quantized = True
-                        self.weight = nn.Parameter(weight_tensor, requires_grad=False)
-                        Int8TensorwiseOps._is_prequantized = True
-                        per_row_hint = bool(conf["per_row"]) if isinstance(conf, dict) and "per_row" in conf else None
-                        if isinstance(weight_scale, torch.Tensor):
-                            if weight_scale.numel() == 1:
-                                self.register_buffer("weight_scale", weight_scale.float().reshape(1))
-                                self._is_per_row = False if per_row_hint is None else per_row_hint
-                            elif weight_scale.dim() == 2 and weight_scale.shape[1] == 1:
-                                self.register_buffer("weight_scale", weight_scale.float())
-                                self._is_per_row = True if per_row_hint is None else per_row_hint
-                            else:
-                                self.register_buffer("weight_scale", weight_scale.float())
-                                self._is_per_row = False if per_row_hint is None else per_row_hint
-                        else:
-                            self.register_buffer("weight_scale", torch.tensor([float(weight_scale)]))
-                            self._is_per_row = False if per_row_hint is None else per_row_hint
-                    elif weight_tensor.dtype in (torch.float16, torch.bfloat16, torch.float32):
-                        is_excluded = any(ex in prefix for ex in Int8TensorwiseOps.excluded_names)
-                        is_dim1 = self.in_features == 1 or self.out_features == 1 or weight_tensor.ndim == 1
-                        should_quantize = Int8TensorwiseOps.dynamic_quantize and not is_excluded and not is_dim1
-                        load_dev = getattr(Int8TensorwiseOps, "dynamic_load_device", None)
-                        if load_dev is not None and (should_quantize or pending_weight_lora):
-                            # per-layer bake/quant deferred to model load
-                            self._is_quantized = False
-                            self.weight = nn.Parameter(weight_tensor, requires_grad=False)
-                            self._pending_int8_finalize = {
-                                "weight_key": weight_key,
-                                "quantize": should_quantize,
-                                "lora_patches": pending_weight_lora,
-                                "device": load_dev,
-                                "enable_convrot": getattr(Int8TensorwiseOps, "enable_convrot", False),
-                            }
-                            if pending_weight_lora:
-                                _note_applied(_normalize_lora_key(weight_key))
-                        elif should_quantize:
-                            if not hasattr(Int8TensorwiseOps, "_logged_otf"):
-                                logging.info(
-                                    f"INT8 Fast: Quantizing on-the-fly (ConvRot: {Int8TensorwiseOps.enable_convrot})")
-                                Int8TensorwiseOps._logged_otf = True
-                            self._otf_quantize(weight_tensor)
-                        else:
-                            self._is_quantized = False
-                            self.weight = nn.Parameter(weight_tensor, requires_grad=False)
-                    else:
-                        self._is_quantized = False
-                        self.weight = nn.Parameter(weight_tensor, requires_grad=False)
-                elif not w4a8_handled:
-                    missing_keys.append(weight_key)
-
-                self.bias = nn.Parameter(bias_tensor, requires_grad=False) if bias_tensor is not None else None
-                if self.weight is not None:
-                    self.weight_comfy_model_dtype = self.weight.dtype
-                if self.weight_scale is not None:
-                    self.weight_scale_comfy_model_dtype = self.weight_scale.dtype
-                if self.bias is not None:
-                    self.bias_comfy_model_dtype = self.bias.dtype
+                self.bias = nn.Parameter(bias, requires_grad=False) if bias is not None else None
+                for name in ("weight", "weight_scale", "bias"):
+                    t = getattr(self, name)
+                    if t is not None:
+                        setattr(self, f"{name}_comfy_model_dtype", t.dtype)
 
             def _get_weight_scale(self):
                 return self.weight_scale
@@ -460,28 +433,17 @@ if _COMFY_OPS_AVAILABLE:
 
             def set_weight(self, out_weight, inplace_update=False, seed=0, return_weight=False, **kwargs):
                 if not self._is_quantized:
-                    new_weight = out_weight.to(self.weight.dtype)
+                    value = out_weight.to(self.weight.dtype)
                 elif out_weight.dtype == torch.int8:
-                    new_weight = out_weight
-                else:  # a float patch result: requantise with the layer's scale
-                    new_weight = quantize_int8(out_weight, self._get_weight_scale().to(out_weight.device))
-                if return_weight:
-                    return new_weight
-                if inplace_update:
-                    self.weight.data.copy_(new_weight)
-                else:
-                    self.weight = nn.Parameter(new_weight, requires_grad=False)
+                    value = out_weight
+                else:  # a float patch result: requantised with the layer's own scale
+                    value = quantize_int8(out_weight, self._get_weight_scale().to(out_weight.device))
+                return store_param(self, "weight", value, inplace_update, return_weight)
 
             def set_bias(self, out_bias, inplace_update=False, seed=0, return_weight=False, **kwargs):
                 if out_bias is None:
                     return None
-                if return_weight:
-                    return out_bias
-                if inplace_update:
-                    if self.bias is not None:
-                        self.bias.data.copy_(out_bias)
-                else:
-                    self.bias = nn.Parameter(out_bias, requires_grad=False)
+                return store_param(self, "bias", out_bias, inplace_update, return_weight)
 
             # -- forward ----------------------------------------------------
             def _w4a8_int8_weight(self, weight):
@@ -499,16 +461,7 @@ if _COMFY_OPS_AVAILABLE:
             def forward(self, x: Tensor) -> Tensor:
                 need_cast = self.comfy_cast_weights or len(self.weight_function) > 0 or len(self.bias_function) > 0
                 if not self._is_quantized:
-                    if need_cast:
-                        weight, bias, offload_stream = cast_bias_weight(self, x, offloadable=True)
-                        out = F.linear(x, weight, bias)
-                        uncast_bias_weight(self, weight, bias, offload_stream)
-                        return out
-                    if x.device != self.weight.device or x.dtype != self.weight.dtype:
-                        weight = self.weight.to(device=x.device, dtype=x.dtype)
-                        bias = self.bias.to(device=x.device, dtype=x.dtype) if self.bias is not None else None
-                        return F.linear(x, weight, bias)
-                    return F.linear(x, self.weight, self.bias)
+                    return float_forward(self, x, need_cast, cast_bias_weight, uncast_bias_weight)
 
                 if need_cast:
                     weight, bias, offload_stream = cast_bias_weight(
@@ -651,41 +604,21 @@ def _dynamic_lora_entries(module, patches, rot, group_ok):
 
 if _COMFY_PATCHER_AVAILABLE:
 
-    class INT8LowVramPatch:
+    class INT8LowVramPatch(QuantLowVramPatch):
         """Low-VRAM LoRA on an INT8 layer as ComfyUI streams the weight in
         (int8_quant.py:761-843): dequant (+ un-rotate) -> patch in float ->
         re-rotate -> requantise with the layer's original scale."""
-        is_lowvram_patch = True
 
-        def __init__(self, key, patches, module, lora_mode):
-            self.key = key
-            self.patches = patches
-            self.module = module
-            self.lora_mode = lora_mode
-            self.prepared_patches = None
-
-        def memory_required(self):
-            return 0
-
-        def prepare(self, *args, **kwargs):
-            self.prepared_patches = list(self.patches[self.key])
-            return self.prepared_patches
-
-        def clear_prepared(self):
-            self.prepared_patches = None
-
-        def __call__(self, weight):
-            patches = self.prepared_patches if self.prepared_patches is not None else self.patches[self.key]
+        def apply(self, weight, patches):
             scale = self.module._get_weight_scale()
             if isinstance(scale, torch.Tensor):
                 scale = scale.to(weight.device)
-            group = getattr(self.module, "_convrot_groupsize", CONVROT_GROUP_SIZE) \
-                if getattr(self.module, "_use_convrot", False) else 0
+            rot = _int8_module_rot(self.module)
+            stochastic = self.lora_mode == "Stochastic"
             return lowvram_patch_int8(
-                weight, scale, group,
+                weight, scale, rot[1] if rot else 0,
                 lambda w: _comfy_lora.calculate_weight(patches, w, self.key, intermediate_dtype=w.dtype),
-                stochastic=self.lora_mode == "Stochastic",
-                seed=_comfy_utils.string_to_seed(self.key) if self.lora_mode == "Stochastic" else 0)
+                stochastic=stochastic, seed=_comfy_utils.string_to_seed(self.key) if stochastic else 0)
 
     class INT8ModelPatcher(_comfy_model_patcher.ModelPatcher):
         """ModelPatcher that routes LoRA patches on INT8 layers through the

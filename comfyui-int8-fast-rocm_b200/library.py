@@ -257,6 +257,17 @@ def _(packed, codebook, s_channel, s_rel, group_size):
             packed.new_empty((Nn, 1), dtype=torch.float32))
 
 
+@_op("dequant_asym_w4a8")
+def _dequant_asym_w4a8(packed: Tensor, codebook: Tensor, s_channel: Tensor, s_rel: Tensor,
+                       group_size: int) -> Tensor:
+    return ops.dequant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size)
+
+
+@_dequant_asym_w4a8.register_fake
+def _(packed, codebook, s_channel, s_rel, group_size):
+    return packed.new_empty((_rows_of(packed), 2 * packed.shape[1]), dtype=torch.float32)
+
+
 @_op("dequant_int8")
 def _dequant_int8(q: Tensor, scale: Tensor, rot_kind: str, rot_group: int) -> Tensor:
     return ops.dequant_int8(q, scale, _rot(rot_kind, rot_group))
@@ -366,6 +377,10 @@ def quant_weight_int4(w: Tensor, rot=None, group: int = 0):
 
 def requant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size: int):
     return _L.requant_asym_w4a8(packed, codebook, s_channel, s_rel, int(group_size))
+
+
+def dequant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size: int) -> Tensor:
+    return _L.dequant_asym_w4a8(packed, codebook, s_channel, s_rel, int(group_size))
 
 
 def dequant_int8(q: Tensor, scale, rot=None) -> Tensor:

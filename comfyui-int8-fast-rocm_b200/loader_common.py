@@ -5,6 +5,7 @@ layer so the custom operations can bake them while the checkpoint loads.
 ComfyUI modules are imported when a loader runs."""
 from __future__ import annotations
 
+import json
 import logging
 
 import torch
@@ -106,3 +107,54 @@ def stash_metadata(model, metadata, attr):
             setattr(model.model, attr, metadata)
     except Exception:
         pass
+
+
+# Where a checkpoint's header names a layer "blocks.0.attn" its weight may be
+# stored under one of the prefixes ComfyUI checkpoints use (the key-matching
+# rule of int4_unet_loader.py:82-130 and w4a8_int8.py:78-121, which existing
+# checkpoints rely on): the bare name first, then these prefixes in order,
+# then any unique key that ends in the layer's name.
+HEADER_KEY_PREFIXES = ("", "model.", "diffusion_model.", "model.diffusion_model.")
+
+
+def _find_layer_weight(layer: str, keys) -> str | None:
+    for prefix in HEADER_KEY_PREFIXES:
+        if f"{prefix}{layer}.weight" in keys:
+            return f"{prefix}{layer}.weight"
+    tail = f".{layer}.weight"
+    hits = [k for k in keys if k.endswith(tail)]
+    return hits[0] if len(hits) == 1 else None
+
+
+def bridge_header_quant_metadata(state_dict: dict, metadata, formats, tag: str) -> int:
+    """Give every layer that the safetensors header's ``_quantization_metadata``
+    lists with a format in ``formats`` a ``<layer>.comfy_quant`` tensor (the
+    layer's JSON entry as uint8 bytes) when the state dict has none, so the
+    custom operations see the per-layer format while loading.  Returns the
+    number of layers with a marker; unparsable headers and layers whose
+    weight is not found are logged and skipped."""
+    raw = (metadata or {}).get("_quantization_metadata")
+    if raw is None:
+        return 0
+    try:
+        layers = json.loads(raw).get("layers", {})
+    except (ValueError, AttributeError) as e:
+        logging.warning(f"{tag}: ignoring an unreadable _quantization_metadata header ({e})")
+        return 0
+    wanted = {name: entry for name, entry in layers.items()
+              if isinstance(entry, dict) and entry.get("format") in formats}
+    keys = set(state_dict)
+    marked = 0
+    for name, entry in wanted.items():
+        wkey = _find_layer_weight(name, keys)
+        if wkey is None:
+            logging.warning(f"{tag}: header lists layer {name!r} but the checkpoint has no weight for it")
+            continue
+        marker = wkey[: -len("weight")] + "comfy_quant"
+        if marker not in state_dict:
+            state_dict[marker] = torch.frombuffer(bytearray(json.dumps(entry, separators=(",", ":")).encode()),
+                                                  dtype=torch.uint8)
+        marked += 1
+    if marked:
+        logging.info(f"{tag}: {marked} layer formats taken from the safetensors header")
+    return marked

@@ -531,6 +531,26 @@ def requant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size: int):
     return q, s
 
 
+def dequant_asym_w4a8(packed, codebook, s_channel, s_rel, group_size: int) -> torch.Tensor:
+    """asym_w4a8_int8 -> float32 [N, K]: codebook[code] * s_channel[n] *
+    s_rel[n, k // group_size] (no requantisation)."""
+    packed = _aligned(packed)
+    Nn, Kp = packed.shape
+    K = 2 * Kp
+    dev = packed.device
+    groups = s_rel.shape[1] if s_rel.dim() == 2 else -1
+    if groups * group_size != K:
+        raise ValueError(f"asym W4A8: {groups} scale groups of {group_size} do not cover K = {K}")
+    codebook = codebook.to(device=dev, dtype=torch.float32).contiguous()
+    s_channel = s_channel.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    s_rel = (s_rel if s_rel.dtype == torch.uint8 else s_rel.view(torch.uint8)).to(dev).contiguous()
+    out = torch.empty((Nn, K), dtype=torch.float32, device=dev)
+    if Nn and K:
+        N.call("qlin_dequant_asym_w4a8", packed.data_ptr(), codebook.data_ptr(), s_channel.data_ptr(),
+               s_rel.data_ptr(), int(group_size), Nn, K, out.data_ptr(), _stream(packed))
+    return out
+
+
 def _scale_arg(scale, n, device):
     s = scale.reshape(-1).to(device=device, dtype=torch.float32).contiguous() if torch.is_tensor(scale) \
         else torch.tensor([float(scale)], dtype=torch.float32, device=device)

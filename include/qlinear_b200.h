@@ -326,6 +326,14 @@ QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook
                                     const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K,
                                     int8_t* q, float* scale, void* stream);
 
+/* Asymmetric W4A8 -> float32: out[N,K] = codebook[code]*s_channel[n]*s_rel[n,k/gs],
+ * multiplied in that order, the same expression as qlin_requant_asym_w4a8
+ * before its requantisation.  Replaces dequant_asym_w4a8_to_float
+ * (w4a8_int8.py:46-75). */
+QLIN_API int qlin_dequant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
+                                    const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K, float* out,
+                                    void* stream);
+
 /* LoRA bake helpers (int8_quant.py:809-843, 881-941).
  * dequant: out[N,K] float32 = rotate_weight(q * scale)   (rotation optional)
  * requant: q[N,K] = round(rotate_weight(w) * (1/scale)) with the ORIGINAL

@@ -484,6 +484,15 @@ def test_requant_asym_w4a8_golden(P, golden):
     np.testing.assert_array_equal(s.cpu().numpy(), golden["w4a8_s"])
 
 
+def test_dequant_asym_w4a8_golden(P, golden):
+    # the reference's own float dequantisation (w4a8_int8.py:46-75), bit for bit
+    packed, cb, sch, srel = gi.asym_w4a8(10, 96, 256, 16)
+    w = P.w4a8_int8.dequant_asym_w4a8_to_float(dev(packed), dev(cb), dev(sch), dev(srel), 16)
+    np.testing.assert_array_equal(w.cpu().numpy().view(np.uint32), golden["w4a8_deq"].view(np.uint32))
+    with pytest.raises(ValueError):
+        P.ops.dequant_asym_w4a8(dev(packed), dev(cb), dev(sch), dev(srel), 32)
+
+
 @pytest.mark.parametrize("wdt", ["bf16", "f16", "f32"])
 def test_quant_weight_int8_dtypes(P, wdt):
     w = O.rnd(wdt, gi.weight(22, 96, 1024))
