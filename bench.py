@@ -41,6 +41,15 @@ CPU_SAMPLE_ROWS = 4096  # the whole batch: the CPU sample is bounded by time ins
 GEMM_TRAFFIC_BYTES = 146699776  # ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM
 
 
+def headline_config(world):
+    """The workload description both arms print (same dict, so the two lines
+    describe the same configuration)."""
+    return {"workload": f"convrot_w8a8_linear M={M} N={N} K={K} hadamard={KIND}{GROUP} bf16 in/out, "
+                        f"per-token x per-channel int8, bias; one batch per GPU",
+            "M": M, "N": N, "K": K, "l2": "flushed (256 MB write) before every timed step",
+            "parallelism": f"dp{world} (independent batches, no collective)"}
+
+
 def load_pkg():
     import __graft_entry__ as ge
     return ge._load_package()
@@ -708,10 +717,11 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TOPS", "n_gpus": args.gpus,
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
-            "config": {"workload": f"convrot_w8a8_linear M={M} N={N} K={K} hadamard={KIND}{GROUP} bf16 "
-                                   f"(CPU sample: {CPU_SAMPLE_ROWS} rows per step)", "M": M, "N": N, "K": K},
+            "config": headline_config(args.gpus),
             "cpu_baseline": {"value": v, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{CPU_SAMPLE_ROWS} of {M} rows per step"},
+                             "sample": f"{CPU_SAMPLE_ROWS} of {M} rows per step on the host cores (the reference's "
+                                       f"PyTorch CPU path: bf16 rotation matmul, torch._int_mm, two-rounding "
+                                       f"epilogue); the L2 flush does not apply on the CPU"},
             "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -851,15 +861,13 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(total_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
-            "config": {"workload": f"convrot_w8a8_linear M={M} N={N} K={K} hadamard={KIND}{GROUP} bf16 in/out, "
-                                   f"per-token x per-channel int8, bias; one batch per GPU",
-                       "M": M, "N": N, "K": K, "l2": "flushed (256 MB write) before every timed step",
-                       "parallelism": f"dp{world} (independent batches, no collective)"},
+            "config": headline_config(world),
             "roofline": {"bound": "tensor", "kernel": "gemm_i8_pair_kernel (tcgen05 kind::i8, CTA pair)",
                          "achieved": round(gemm_tops, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                          "frac": round(gemm_tops / int8_peak, 4), "traffic": GEMM_TRAFFIC_BYTES,
                          "peak_source": f"2 x {src} dense bf16 ({bf16_tf} TFLOP/s) = dense int8"},
-            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_x2_kernel (fused Hadamard-128 + int8, bulk-copy row ring)",
+            "roofline_quant": {"bound": "hbm", "kernel": "rowquant_strip_kernel (Sylvester-128 rotation + int8 in "
+                                                     "registers, bulk-copy row ring)",
                                "achieved": round(quant_gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
                                "frac": round(quant_gbs / hbm_gbs, 4), "bytes": quant_bytes,
                                "us": round(quant_ms * 1e3, 2)},
@@ -871,14 +879,93 @@ def run_ours(args):
                     "host_output_equals_device_output": e2e_matches},
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
-            "dit": dit,
-            "configs": cfgs,
+            "dit": _compact_dit(dit),
+            "configs": _configs_summary(cfgs),
             "tensor_parallel": tpres,
             "clocks": clk.summary(),
         }
+        # the per-shape tables and descriptions go to stderr, so the one
+        # stdout line stays short enough to be read whole from a log tail
+        print(json.dumps({"bench_details": {"configs": cfgs, "dit": dit}}), file=sys.stderr, flush=True)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def _configs_summary(cfgs):
+    """Roofline fractions of the per-configuration kernel timings (the full
+    per-shape table is printed to stderr)."""
+    if not cfgs:
+        return cfgs
+    out = {"timing": cfgs.get("timing"), "peak_tops": cfgs.get("peak_tops")}
+    sweep = cfgs.get("convrot_w8a8_sylvester128")
+    if sweep:
+        out["convrot_w8a8_min_frac"] = cfgs.get("convrot_w8a8_min_frac")
+        out["convrot_w8a8_shapes_at_0.7"] = f"{sum(r['frac'] >= 0.7 for r in sweep)}/{len(sweep)}"
+        out["convrot_w8a8_fracs"] = [r["frac"] for r in sweep]
+    for key in ("w4a8_g128", "w4a4_g128_sylvester128", "w4a4_row_regular256", "w8a8_plain_c0"):
+        v = cfgs.get(key)
+        if isinstance(v, dict):
+            out[key] = {k: v[k] for k in ("M", "N", "K", "gemm_us", "frac", "quant_us") if k in v}
+        elif isinstance(v, list):
+            out[key] = [{k: r[k] for k in ("N", "gemm_us", "frac") if k in r} for r in v]
+    return out
+
+
+def _compact_dit(dit):
+    if not isinstance(dit, dict):
+        return dit
+    drop = ("config", "fusions")
+    return {k: v for k, v in dit.items() if k not in drop}
+
+
+def cpu_configs():
+    """The reference's PyTorch CPU path per configuration on all host cores
+    (BASELINE table): the plain W8A8 linear, the ConvRot W8A8 linear with its
+    stages timed apart, the group-128 W4A8 and W4A4 restatements and the
+    reference's row-wise W4A4 ConvRot linear; a sample of rows per
+    configuration, median of >= 5 runs after one warm-up."""
+    from oracle import torch_cpu_path as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 1024
+
+    def med(fn, n=5):
+        fn()
+        ts = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    g = torch.Generator().manual_seed(0)
+    res = {"cores": torch.get_num_threads(), "rows_per_sample": rows, "unit": "TOPS (2*M*N*K / time)",
+           "threads_note": "torch.set_num_threads(os.cpu_count())"}
+    for name, (n, k, group, kind) in {"c0_w8a8_4096x3072x3072": (3072, 3072, 0, None),
+                                      "c1_convrot_w8a8_sylvester128_4096x12288x3072": (12288, 3072, 128, "sylvester"),
+                                      "c1_convrot_w8a8_regular256_4096x3072x12288": (3072, 12288, 256, "regular")}.items():
+        x = torch.randn((rows, k), generator=g).to(torch.bfloat16)
+        w = torch.randn((n, k), generator=g) * 0.02
+        b = (torch.randn((n,), generator=g) * 0.01).to(torch.bfloat16)
+        H = R.hadamard(group, kind) if group else None
+        wq, ws = R.quantize_int8_axiswise(R.rotate_activation(w, H, group) if H is not None else w, dim=1)
+        t = med(lambda: R.convrot_w8a8_linear(x, H, group, wq, ws, b, torch.bfloat16))
+        stages = {}
+        xr = R.rotate_activation(x, H, group) if H is not None else x
+        if H is not None:
+            stages["rotate_ms"] = round(med(lambda: R.rotate_activation(x, H, group)) * 1e3, 2)
+        xq, xs = R.quantize_int8_axiswise(xr, dim=-1)
+        stages["quant_ms"] = round(med(lambda: R.quantize_int8_axiswise(xr, dim=-1)) * 1e3, 2)
+        stages["int_mm_ms"] = round(med(lambda: torch._int_mm(xq, wq.T)) * 1e3, 2)
+        res[name] = {"ms": round(t * 1e3, 2), "tops": round(2.0 * rows * n * k / t / 1e12, 3), **stages}
+    for name, fn in {"c2_w4a8_g128_4096x12288x3072": lambda: R.w4a8_g128_case(rows, 12288, 3072, g),
+                     "c3_w4a4_g128_sylvester128_4096x3072x3072": lambda: R.w4a4_g128_case(rows, 3072, 3072, g),
+                     "c3_w4a4_g128_sylvester128_4096x12288x3072": lambda: R.w4a4_g128_case(rows, 12288, 3072, g),
+                     "w4a4_row_regular256_4096x12288x3072": lambda: R.w4a4_row_case(rows, 12288, 3072, g)}.items():
+        run, n, k = fn()
+        t = med(run)
+        res[name] = {"ms": round(t * 1e3, 2), "tops": round(2.0 * rows * n * k / t / 1e12, 3)}
+    print(json.dumps({"cpu_configs": res}), flush=True)
 
 
 def main():
@@ -893,8 +980,12 @@ def main():
     ap.add_argument("--dit-breakdown", action="store_true",
                     help="print a kernel-time breakdown of the fused DiT forward (2 double + 4 single blocks, "
                          "16 samples, torch profiler) and exit")
+    ap.add_argument("--cpu-configs", action="store_true",
+                    help="time the reference's PyTorch CPU path per configuration on the host cores and exit")
     args = ap.parse_args()
-    if args.dit_breakdown:
+    if args.cpu_configs:
+        cpu_configs()
+    elif args.dit_breakdown:
         dit_breakdown()
     elif args.impl == "reference":
         run_reference(args)

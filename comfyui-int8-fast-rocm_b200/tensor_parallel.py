@@ -12,9 +12,14 @@ all-gather pass.  ``mode="nccl"`` computes the shard into a local tensor and
 gathers it with ``all_gather_into_tensor`` (the baseline the fused path
 replaces).
 
-The output of a fused call is a fresh tensor; the symmetric buffers are
-double-buffered so that one barrier per call keeps every rank's copy-out of
-call k ordered before any rank writes call k+2 into the same buffer.
+Lifetime of a fused call's output: it is a view of one of two symmetric
+buffers that alternate between calls (rows padded to 16 bytes, so a layer
+of any width fits), returned without a copy.  Call k+2 rewrites it, and every
+rank's writes of call k+2 come after the device barrier that ends call k+1,
+which each rank reaches only after the work it enqueued on its stream
+before call k+1.  So the output of call k may be read by any work enqueued
+on the calling stream before the layer's next call; clone it to keep it
+longer.
 """
 from __future__ import annotations
 
@@ -37,6 +42,12 @@ def shard_bounds(n: int, world: int, rank: int, align: int = SHARD_ALIGN):
     per = -(-per // align) * align
     start = min(n, rank * per)
     return start, min(n, start + per)
+
+
+def padded_width(n: int, align: int = SHARD_ALIGN) -> int:
+    """Row stride of the gathered output buffer: ``n`` rounded up to
+    ``align`` columns (the fused kernel stores 16-byte rows)."""
+    return -(-n // align) * align
 
 
 def interleave_shards(gathered: torch.Tensor, n: int) -> torch.Tensor:
@@ -82,7 +93,7 @@ class ColumnParallelInt8Linear:
             import torch.distributed._symmetric_memory as symm_mem
             got = []
             for _ in range(2):
-                t = symm_mem.empty((m, self.n), dtype=self.out_dtype, device=self.device)
+                t = symm_mem.empty((m, padded_width(self.n)), dtype=self.out_dtype, device=self.device)
                 h = symm_mem.rendezvous(t, self.group)
                 base = h.buffer_ptrs[self.rank]
                 ptrs = [p + (t.data_ptr() - base) for p in h.buffer_ptrs]
@@ -111,11 +122,11 @@ class ColumnParallelInt8Linear:
             N.call("qlin_set_device", self.device.index)
             N.call("qlin_gemm_w8a8_allgather", xq.data_ptr(), xs.data_ptr(), self.wq.data_ptr(),
                    self.ws.data_ptr(), N.WSCALE_ROW, 0 if self.bias is None else self.bias.data_ptr(),
-                   ctypes.cast(ptrs, ctypes.c_void_p), self.world, self.start, self.n,
+                   ctypes.cast(ptrs, ctypes.c_void_p), self.world, self.start, t.shape[1],
                    ops.dtype_code(self.out_dtype), m, self.stop - self.start, self.k,
                    torch.cuda.current_stream(self.device).cuda_stream)
         h.barrier(channel=0)
-        return t.clone()
+        return t[:, :self.n]  # valid until the layer's next call is enqueued (module docstring)
 
     def _forward_nccl(self, xq, xs, m):
         local = torch.zeros((m, self.per), dtype=self.out_dtype, device=self.device)

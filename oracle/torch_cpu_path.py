@@ -63,3 +63,87 @@ def convrot_w8a8_linear(x, H, group, weight, weight_scale, bias, compute_dtype):
     if H is not None:
         x_2d = rotate_activation(x_2d, H, group)
     return int8_forward_dynamic_per_row(x_2d, weight, weight_scale, bias, compute_dtype)
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines of the int4 configurations (timing only; bench.py
+# --cpu-configs).  The row-wise W4A4 ConvRot linear is the reference's CPU
+# restatement of convrot_w4a4_forward (int4_quant.py:292-353 with
+# triton_int4_mm replaced by unpack + torch._int_mm, triton_int4_mm.py:4-9);
+# the group-128 schemes have no reference and follow the oracle's
+# restatement (group scales folded per 128-deep slab).
+# ---------------------------------------------------------------------------
+
+
+def _unpack_nibbles(packed: torch.Tensor) -> torch.Tensor:
+    """[N, K/2] int8 (low nibble = even k, signed) -> [N, K] int8."""
+    p = packed.to(torch.int16) & 0xFF
+    lo = ((p & 0xF) ^ 8) - 8
+    hi = ((p >> 4) ^ 8) - 8
+    return torch.stack((lo, hi), -1).reshape(packed.shape[0], -1).to(torch.int8)
+
+
+def _pack_nibbles(q: torch.Tensor) -> torch.Tensor:
+    u = q.to(torch.int16) & 0xF
+    return (u[:, 0::2] | (u[:, 1::2] << 4)).to(torch.uint8).view(torch.int8)
+
+
+def _int4_groups(w: torch.Tensor, group: int = 128):
+    """Symmetric int4 per row and 128-wide group: codes [N, K], scales [N, K/g]."""
+    n, k = w.shape
+    wg = w.reshape(n, k // group, group)
+    s = (wg.abs().amax(-1).clamp(min=1e-10) / 7.0)
+    q = (wg / s.unsqueeze(-1)).round().clamp(-7, 7).to(torch.int8).reshape(n, k)
+    return q, s
+
+
+def w4a8_g128_case(rows, n, k, gen):
+    x = torch.randn((rows, k), generator=gen).to(torch.bfloat16)
+    q, s = _int4_groups(torch.randn((n, k), generator=gen) * 0.02)
+    packed, ws = _pack_nibbles(q), s.to(torch.bfloat16).float()
+    bias = (torch.randn((n,), generator=gen) * 0.01).to(torch.bfloat16)
+
+    def run():
+        xq, xs = quantize_int8_axiswise(x, dim=-1)
+        wq = _unpack_nibbles(packed)
+        acc = torch.zeros((rows, n), dtype=torch.float32)
+        for g in range(k // 128):
+            part = torch._int_mm(xq[:, g * 128:(g + 1) * 128].contiguous(), wq[:, g * 128:(g + 1) * 128].T.contiguous())
+            acc += part.float() * ws[:, g]
+        return (acc * xs + bias.float()).to(torch.bfloat16)
+    return run, n, k
+
+
+def w4a4_g128_case(rows, n, k, gen):
+    H = hadamard(128, "sylvester")
+    x = torch.randn((rows, k), generator=gen).to(torch.bfloat16)
+    q, s = _int4_groups(rotate_activation(torch.randn((n, k), generator=gen) * 0.02, H, 128))
+    packed, ws = _pack_nibbles(q), s.to(torch.bfloat16).float()
+    bias = (torch.randn((n,), generator=gen) * 0.01).to(torch.bfloat16)
+
+    def run():
+        xa, xsc = _int4_groups(rotate_activation(x, H, 128).float())
+        wq = _unpack_nibbles(packed)
+        acc = torch.zeros((rows, n), dtype=torch.float32)
+        for g in range(k // 128):
+            part = torch._int_mm(xa[:, g * 128:(g + 1) * 128].contiguous(), wq[:, g * 128:(g + 1) * 128].T.contiguous())
+            acc += part.float() * (xsc[:, g:g + 1] * ws[:, g])
+        return (acc + bias.float()).to(torch.bfloat16)
+    return run, n, k
+
+
+def w4a4_row_case(rows, n, k, gen):
+    H = hadamard(256, "regular")
+    x = torch.randn((rows, k), generator=gen).to(torch.bfloat16)
+    wr = rotate_activation(torch.randn((n, k), generator=gen) * 0.02, H, 256)
+    sw = wr.abs().amax(-1, keepdim=True).clamp(min=1e-10) / 7.0
+    packed = _pack_nibbles((wr / sw).round().clamp(-7, 7).to(torch.int8))
+    bias = (torch.randn((n,), generator=gen) * 0.01).to(torch.bfloat16)
+
+    def run():
+        xr = rotate_activation(x, H, 256)
+        sa = xr.abs().amax(-1, keepdim=True).clamp(min=1e-10) / 7.0
+        qa = (xr / sa).round().clamp(-7, 7).to(torch.int8)
+        acc = torch._int_mm(qa, _unpack_nibbles(packed).T.contiguous())
+        return (acc.float() * sa.float() * sw.reshape(1, -1) + bias.float()).to(torch.bfloat16)
+    return run, n, k

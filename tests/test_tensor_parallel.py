@@ -48,6 +48,11 @@ def test_shard_bounds():
             assert all(b >= a for a, b in bounds)
 
 
+def test_padded_width():
+    tp = load_package().tensor_parallel
+    assert [tp.padded_width(n) for n in (1, 8, 1001, 3072, 3080)] == [8, 8, 1008, 3072, 3080]
+
+
 def test_gather_layout_two_ranks_gloo():
     assert _run_ranks("gather", 2, timeout=120) == [0, 0]
 

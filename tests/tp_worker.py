@@ -46,28 +46,31 @@ def linear_check():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     g = torch.Generator(device="cpu")
     g.manual_seed(7)
-    n, k = 3080, 1024  # n not a multiple of 8 * world: uneven last shard
-    w = torch.randn((n, k), generator=g) * 0.02
-    bias = (torch.randn((n,), generator=g) * 0.01).to(torch.bfloat16)
-    rot = ("regular", 256)
-    wq, ws = P.ops.quant_weight_int8(w.to(dev), rot)
     ok = True
-    layers = {mode: P.tensor_parallel.ColumnParallelInt8Linear(wq, ws, bias, rot=rot, mode=mode)
-              for mode in ("fused", "nccl")}
-    for step, m in enumerate((300, 300, 300, 64)):
-        x = (torch.randn((m, k), generator=g) * (1 + step)).to(torch.bfloat16).to(dev)
-        xq, xs = P.ops.quant_act_int8(x, rot)
-        want = P.ops.gemm_w8a8(xq, xs, wq, ws, bias.to(dev), torch.bfloat16)
-        for mode, layer in layers.items():
-            got = layer(x)
-            torch.cuda.synchronize()
-            if not torch.equal(got.view(torch.int16), want.view(torch.int16)):
-                print(f"rank {rank} mode {mode} step {step}: mismatch "
-                      f"{(got.float() - want.float()).abs().max().item()}", flush=True)
-                ok = False
+    # n = 3080: not a multiple of 8 * world (uneven last shard); n = 1001: rows
+    # of the gathered output not 16-byte multiples (padded buffer stride)
+    for n in (3080, 1001):
+        k = 1024
+        w = torch.randn((n, k), generator=g) * 0.02
+        bias = (torch.randn((n,), generator=g) * 0.01).to(torch.bfloat16)
+        rot = ("regular", 256)
+        wq, ws = P.ops.quant_weight_int8(w.to(dev), rot)
+        layers = {mode: P.tensor_parallel.ColumnParallelInt8Linear(wq, ws, bias, rot=rot, mode=mode)
+                  for mode in ("fused", "nccl")}
+        for step, m in enumerate((300, 300, 300, 64)):
+            x = (torch.randn((m, k), generator=g) * (1 + step)).to(torch.bfloat16).to(dev)
+            xq, xs = P.ops.quant_act_int8(x, rot)
+            want = P.ops.gemm_w8a8(xq, xs, wq, ws, bias.to(dev), torch.bfloat16)
+            for mode, layer in layers.items():
+                got = layer(x)  # read before the layer's next call (the fused output's lifetime)
+                if got.shape != want.shape or not torch.equal(got.view(torch.int16), want.view(torch.int16)):
+                    print(f"rank {rank} n {n} mode {mode} step {step}: mismatch "
+                          f"{(got.float() - want.float()).abs().max().item()}", flush=True)
+                    ok = False
+        torch.cuda.synchronize()
+        layers.clear()
     ok_t = torch.tensor([int(ok)], device=dev)
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
-    layers.clear()
     dist.destroy_process_group()
     return bool(ok_t.item())
 
