@@ -22,6 +22,7 @@ from . import int8_quant  # noqa: F401
 from . import int4_quant  # noqa: F401
 from . import tensor_parallel  # noqa: F401
 from . import int8_save  # noqa: F401
+from . import data_parallel  # noqa: F401
 
 log = logging.getLogger("comfyui-int8-fast-b200")
 

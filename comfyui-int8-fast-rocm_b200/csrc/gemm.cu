@@ -321,14 +321,15 @@ int launch_g128_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const CUt
 template <int MODE>
 int dispatch_g128(int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* w_packed,
                   const G128Params& p, int sms, cudaStream_t s) {
-  // 16-bit outputs with 16-byte aligned rows: the CTA-pair kernel (TMA-store epilogue)
+  // 16-bit outputs with 16-byte aligned rows and K a multiple of two scale
+  // groups: the CTA-pair kernel (TMA-store epilogue, two groups per step)
   if ((out_dt == DT_BF16 || out_dt == DT_F16) && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
-      (p.ldo * 2) % 16 == 0 && !g128_pair_disabled()) {
-    CUtensorMap tc, tb2;  // the pair loads 64 packed weight rows per CTA
+      (p.ldo * 2) % 16 == 0 && p.K % G128PairCfg::KS == 0 && !g128_pair_disabled()) {
+    CUtensorMap tc, tb2;  // the pair loads 64 packed weight rows of a two-group step per CTA
     int rc = make_tmap(&tc, p.out, (uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.ldo * 2, 32, 32,
                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_UINT16);
     if (rc) return rc;
-    rc = make_tmap(&tb2, w_packed, (uint64_t)(p.K / 2), (uint64_t)p.N, (uint64_t)(p.K / 2), G128PairCfg::BK / 2,
+    rc = make_tmap(&tb2, w_packed, (uint64_t)(p.K / 2), (uint64_t)p.N, (uint64_t)(p.K / 2), G128PairCfg::KS / 2,
                    G128PairCfg::BNH, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     if (out_dt == DT_BF16) return launch_g128_pair_cfg<MODE, DT_BF16>(ta, tb2, tc, p, sms, s);
