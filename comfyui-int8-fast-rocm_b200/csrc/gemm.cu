@@ -71,10 +71,10 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
   return QLIN_OK;
 }
 
-template <int EPI, int OUT_DT>
+template <int EPI, int OUT_DT, bool SPLIT = false>
 int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   using Cfg = PairCfg<EPI, OUT_DT>;
-  auto kern = gemm_i8_pair_kernel<EPI, OUT_DT>;
+  auto kern = gemm_i8_pair_kernel<EPI, OUT_DT, SPLIT>;
   // 16-bit output through TMA stores: one destination, 16-byte aligned rows
   CUtensorMap tc = ta;
   int use_tma_store = 0;
@@ -95,8 +95,8 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
     attr_devices.fetch_or(bit);
   }
-  const int num_tiles = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN);
-  const int clusters = num_tiles < p.num_sms / 2 ? num_tiles : p.num_sms / 2;
+  const int num_units = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN) * p.splits;
+  const int clusters = num_units < p.num_sms / 2 ? num_units : p.num_sms / 2;
   kern<<<2 * clusters, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p, use_tma_store);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
@@ -197,6 +197,8 @@ GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale, co
   p.gelu_col0 = INT64_MAX;  // EPI_POST fields: no GELU, no residual
   p.rows_per_gate = 1;
   p.stall_kb = -1;
+  p.splits = 1;
+  p.kb_split = (int)((K + GEMM_BK - 1) / GEMM_BK);
   return p;
 }
 
@@ -342,6 +344,83 @@ int dispatch_g128(int out_dt, const CUtensorMap& ta, const CUtensorMap& tb, cons
 }
 
 }  // namespace
+
+// Split K for the CTA-pair W8A8 kernel.  A problem whose 256 x 256 tiles
+// leave most CTA pairs idle is cut into `splits` (2 or 3) K ranges per tile,
+// all running in one wave.  The parts meet through int32 partials in global
+// scratch (256 KB per tile and part), so a split costs partial traffic and a
+// serialised fix-up: measured on B200, 13-16 us at 48 tiles (1024 x 3072 x
+// 3072: 30.8 us split against 20.5 us unsplit), which is why only problems
+// with at most one wave of split units and K >= 8192 (64 K-slabs) split.
+bool splitk_plan(int64_t M, int64_t N, int64_t K, int sms, int* splits, int* kb_split) {
+  *splits = 1;
+  *kb_split = (int)((K + GEMM_BK - 1) / GEMM_BK);
+  if (M < 256 || N < 256 || sms < 2 || pair_disabled()) return false;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (tiles > SPLITK_MAX_TILES) return false;
+  const int64_t clusters = sms / 2;
+  const int64_t kb = *kb_split;
+  if (kb < 64) return false;
+  for (int s = SPLITK_MAX; s >= 2; --s) {
+    if (tiles * s > clusters) continue;
+    const int64_t per = (kb + s - 1) / s;
+    *splits = (int)((kb + per - 1) / per);
+    *kb_split = (int)per;
+    return *splits > 1;
+  }
+  return false;
+}
+
+size_t splitk_scratch_bytes(int64_t M, int64_t N, int64_t K) {
+  int splits, kb_split;
+  if (!splitk_plan(M, N, K, device_sm_count(), &splits, &kb_split)) return 0;
+  const int tiles = (int)(((M + 255) / 256) * ((N + 255) / 256));
+  return splitk_layout(tiles, splits).bytes;
+}
+
+int launch_gemm_splitk(int kind, const int8_t* a, const int8_t* b, const float* a_scale, const float* w_scale,
+                       const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K, void* scratch,
+                       size_t scratch_bytes, cudaStream_t stream) {
+  if (M == 0 || N == 0) return QLIN_OK;
+  const int sms = device_sm_count();
+  if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  int splits, kb_split;
+  if (kind == GEMM_I32 || !splitk_plan(M, N, K, sms, &splits, &kb_split))
+    return launch_gemm(kind, false, a, b, a_scale, w_scale, bias, out, out_dt, M, N, K, stream);
+  const int tiles = (int)(((M + 255) / 256) * ((N + 255) / 256));
+  const SplitKLayout l = splitk_layout(tiles, splits);
+  if (scratch == nullptr || scratch_bytes < l.bytes)
+    return fail(QLIN_ERR_INVALID_ARG, "split-K scratch smaller than qlin_gemm_w8a8_splitk_scratch reports");
+  if ((reinterpret_cast<uintptr_t>(scratch) & 255) != 0) return fail(QLIN_ERR_ALIGNMENT, "split-K scratch must be 256-byte aligned");
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  OutSpec o;
+  o.outs[0] = out;
+  o.nout = 1;
+  o.col_off = 0;
+  o.ldo = N;
+  GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  p.splits = splits;
+  p.kb_split = kb_split;
+  p.sk_count = reinterpret_cast<uint32_t*>(base + l.count_off);
+  p.sk_ready = reinterpret_cast<uint32_t*>(base + l.ready_off);
+  p.sk_part = reinterpret_cast<int32_t*>(base + l.part_off);
+  if (kind == GEMM_W8A8_ROW) {
+    if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_ROW, DT_BF16, true>(ta, tb, p, stream);
+    if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_ROW, DT_F16, true>(ta, tb, p, stream);
+    if (out_dt == DT_F32) return launch_pair_cfg<EPI_W8A8_ROW, DT_F32, true>(ta, tb, p, stream);
+  }
+  if (kind == GEMM_W8A8_TENSOR) {
+    if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_BF16, true>(ta, tb, p, stream);
+    if (out_dt == DT_F16) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_F16, true>(ta, tb, p, stream);
+    if (out_dt == DT_F32) return launch_pair_cfg<EPI_W8A8_TENSOR, DT_F32, true>(ta, tb, p, stream);
+  }
+  return fail(QLIN_ERR_UNSUPPORTED, "unsupported split-K epilogue / output dtype");
+}
 
 int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,

@@ -122,7 +122,37 @@ struct GemmParams {
   // producer leaves this K-slab of the CTA's first tile unfilled, so the
   // MMA issuer's wait for it runs out; -1 in every product launch.
   int stall_kb;
+  // Split K (CTA-pair kernel, epilogues without EPI_POST, one destination):
+  // work unit u of splits * tiles covers tile u % tiles over the K-slabs
+  // [s * kb_split, min((s + 1) * kb_split, num_kb)), s = u / tiles; each
+  // tile half's units meet in splitk_fixup.  splits == 1: one unit per
+  // tile over the whole K range (the scratch pointers are unused).
+  int splits;
+  int kb_split;
+  uint32_t* sk_count;  // [tiles][2] arrivals per tile half: zero on entry, left zero
+  uint32_t* sk_ready;  // [splits - 1][tiles][2] partial slot written: zero on entry, left zero
+  int32_t* sk_part;    // [splits - 1][tiles][2][128 rows][256 columns] int32 partials
 };
+
+// Scratch layout of a split-K launch: a fixed header of counters and flags
+// (the same place for every problem size, so one scratch buffer serves
+// problems of any shape: every complete launch leaves the header zero),
+// then the partial slots.
+constexpr int SPLITK_MAX = 3;           // K parts per tile (the reader keeps SPLITK_MAX - 1 slots in flight)
+constexpr int SPLITK_MAX_TILES = 2048;  // 256 x 256 tiles of a split problem
+constexpr size_t SPLITK_HEADER = 65536;
+struct SplitKLayout {
+  size_t count_off, ready_off, part_off, bytes;
+};
+__host__ __device__ inline SplitKLayout splitk_layout(int tiles, int splits) {
+  SplitKLayout l;
+  l.count_off = 0;                                                   // [SPLITK_MAX_TILES][2]
+  l.ready_off = (size_t)SPLITK_MAX_TILES * 2 * sizeof(uint32_t);     // [SPLITK_MAX - 1][tiles][2]
+  l.part_off = SPLITK_HEADER;
+  l.bytes = l.part_off + (size_t)(splits - 1) * tiles * 2 * 128 * 256 * sizeof(int32_t);
+  return l;
+}
+static_assert((size_t)SPLITK_MAX_TILES * 2 * 4 * SPLITK_MAX <= SPLITK_HEADER, "split-K header");
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 128;  // bytes (= int8 elements) of K per stage
@@ -137,6 +167,7 @@ struct EpiSmem {
   float bias[2][BN];
   float gate[2][BN];  // EPI_POST gate row of the tile (when its rows share one)
   int gate_ok[2];
+  int sk_order;       // split K: this unit's arrival order on its tile half
 };
 
 template <int BN, bool B_INT4>
@@ -736,12 +767,172 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, uint32_t 
   }
 }
 
+// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// tcgen05.wait::ld tied to the 16 registers of one tmem_ld_32x32b_x16.
+__device__ __forceinline__ void tmem_ld_wait_regs16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+// 32 lanes x 16 columns of 32-bit TMEM <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// 32 lanes x 32 columns of 32-bit TMEM <- 32 registers per thread.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* a, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+// Split K: the units of one tile half (this CTA's 128 rows of a 256 x 256
+// tile) meet here after their MMAs, all 8 epilogue warps of the CTA taking
+// part.  The arrival order comes from an atomic counter (one per tile half):
+// units 0 .. splits-2 store their int32 accumulator in their own scratch
+// slot and publish it with a release flag; the last unit waits (bounded)
+// for those flags, adds the slots into its accumulator in TMEM (int32
+// additions: exact, so the result does not depend on which unit is last)
+// and returns true -- it runs the tile's normal epilogue -- after putting
+// the counter and flags back to zero for the next launch.  The waits are on
+// units that have already arrived, i.e. are past their MMAs and storing.
+// A slot holds each epilogue warp's 32 x 128 block as [chunk][quad][lane]
+// 16-byte vectors, so every warp-wide access is 512 contiguous bytes.
+template <int BN>
+__device__ __forceinline__ bool splitk_fixup(const GemmParams& p, EpiSmem<BN>* es, volatile int* abort_flag,
+                                             uint32_t tmem_acc, int tile, int num_tiles, int rank, int warp,
+                                             int lane) {
+  static_assert(BN == 256, "CTA-pair tiles");
+  const int e = (warp - 2) * 32 + lane;  // 0..255
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const int slot = tile * 2 + rank;  // this tile half
+  const int last = p.splits - 1;
+  if (e == 0) {
+    const uint32_t o = atomicAdd(&p.sk_count[slot], 1u);
+    if (o > (uint32_t)last) {  // the counters were not zero on entry: refuse, report
+      atomicOr(&g_error_bits, 8u);
+      *abort_flag = 1;
+    }
+    es->sk_order = (int)o;
+  }
+  epi_bar();
+  if (*abort_flag) return false;
+  const int order = es->sk_order;
+  // this warp's 32 x 128 block in slot j: 4 chunks x 8 quads x 32 lanes of int4
+  auto block = [&](int j) {
+    return reinterpret_cast<int4*>(p.sk_part) + (((size_t)j * num_tiles * 2 + slot) * 8 + (half * 4 + quarter)) * 1024;
+  };
+  if (order < last) {
+    int4* dst = block(order);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem_acc + (uint32_t)(half * 128 + c * 32) + lane_off, r);
+      tmem_ld_wait_regs(r);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        __stcg(dst + (c * 8 + q) * 32 + lane,
+               make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]));
+    }
+    epi_bar();  // every warp's stores precede the flag
+    if (e == 0) {
+      __threadfence();
+      st_release_gpu(&p.sk_ready[(size_t)order * num_tiles * 2 + slot], 1u);
+    }
+    return false;
+  }
+  if (e == 0) {
+    const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
+    const uint64_t t0 = globaltimer_ns();
+    for (int j = 0; j < last && !*abort_flag; ++j) {
+      const uint32_t* f = &p.sk_ready[(size_t)j * num_tiles * 2 + slot];
+      uint32_t iter = 0;
+      while (ld_acquire_gpu(f) == 0u) {
+        if ((++iter & 63u) == 0) {
+          if (*abort_flag) break;
+          if (globaltimer_ns() - t0 > limit) {
+            atomicOr(&g_error_bits, 1u);
+            *abort_flag = 1;
+            break;
+          }
+        }
+      }
+    }
+  }
+  epi_bar();
+  if (*abort_flag) return false;
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {  // 16-column sub-chunks: quads 4 * (c & 1) .. of chunk c >> 1
+    const uint32_t ta = tmem_acc + (uint32_t)(half * 128 + c * 16) + lane_off;
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(ta, r);
+    int4 v[SPLITK_MAX - 1][4];  // every slot's quads in flight at once
+#pragma unroll
+    for (int j = 0; j < SPLITK_MAX - 1; ++j)
+      if (j < last) {
+        const int4* src = block(j) + ((c >> 1) * 8 + 4 * (c & 1)) * 32 + lane;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[j][q] = __ldcg(src + q * 32);
+      }
+    tmem_ld_wait_regs16(r);
+#pragma unroll
+    for (int j = 0; j < SPLITK_MAX - 1; ++j)
+      if (j < last) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          r[4 * q] += (uint32_t)v[j][q].x;
+          r[4 * q + 1] += (uint32_t)v[j][q].y;
+          r[4 * q + 2] += (uint32_t)v[j][q].z;
+          r[4 * q + 3] += (uint32_t)v[j][q].w;
+        }
+      }
+    tmem_st_32x32b_x16(ta, r);
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  if (e == 0) {  // every unit of this tile half has arrived: reset for the next launch
+    p.sk_count[slot] = 0u;
+    for (int j = 0; j < last; ++j) p.sk_ready[(size_t)j * num_tiles * 2 + slot] = 0u;
+  }
+  return true;
+}
+
 // The epilogue role of a GEMM kernel: for each tile of this CTA, wait for the
 // accumulator, convert it, release it.  Parameters of tile i+1 are loaded into
 // registers while tile i is converted and staged into shared memory after it.
 // All epilogue threads pass the named barrier every tile and leave together
 // when any wait timed out (the abort flag is read after the barrier).
-template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR, int ISHIFT = 0>
+template <int BN, int EPI, int OUT_DT, int ROWS_PER_TILE, bool PAIR, int ISHIFT = 0, bool SPLIT = false>
 __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* es, uint64_t* tfull, uint64_t* tempty,
                                               volatile int* abort_flag, uint32_t tmem_base, int first_tile,
                                               int tile_stride, int num_tiles, int num_m, int num_n, int row_off,
@@ -792,9 +983,12 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       if (bytes) bulk_prefetch_l2(reinterpret_cast<const uint16_t*>(p.residual) + (int64_t)row * p.ld_res + col0, bytes);
     }
   };
-  if (first_tile < num_tiles) {
+  // split K (pair kernel): work units cycle over the tiles once per split
+  static_assert(!SPLIT || (PAIR && !POST), "split K: CTA-pair kernel, plain epilogues");
+  const int num_units = num_tiles * (SPLIT ? p.splits : 1);
+  if (first_tile < num_units) {
     int mb, nb_;
-    tile_coords(first_tile, num_m, num_n, mb, nb_);
+    tile_coords(first_tile % num_tiles, num_m, num_n, mb, nb_);
     prefetch_res(mb, nb_);
     epi_load_params<BN, EPI, OUT_DT>(p, nb_ * BN, e, nws, nb);
     const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
@@ -806,7 +1000,8 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       if (tmC != nullptr && p.residual != nullptr) load_res32<OUT_DT>(p, row, nb_ * BN + half * CPW * 32, res);
     }
   }
-  for (int tile = first_tile; tile < num_tiles; tile += tile_stride) {
+  for (int u = first_tile; u < num_units; u += tile_stride) {
+    const int tile = u % num_tiles;
     int mb, nbk;
     tile_coords(tile, num_m, num_n, mb, nbk);
     const float xs = nxs;
@@ -814,7 +1009,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
     epi_bar();
     if (*abort_flag) break;
     tc_fence_after();
-    const int next = tile + tile_stride;
+    const int next = u + tile_stride < num_units ? (u + tile_stride) % num_tiles : num_tiles;
     int nrow = -1, ncol0 = 0;
     if (next < num_tiles) {
       int mb2, nb2;
@@ -828,8 +1023,13 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       ncol0 = nb2 * BN + half * CPW * 32;
     }
     bool done = false;
+    if constexpr (SPLIT) {
+      // split K: only the last unit of this tile half converts and stores
+      done = !splitk_fixup<BN>(p, es, abort_flag, tmem_base + acc * BN, tile, num_tiles, row_off / GEMM_BM, warp,
+                                 lane);
+    }
     if constexpr (TMA16) {
-      if (tmC != nullptr) {
+      if (tmC != nullptr && !done) {
         epilogue_tile_tma<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter,
                                            half, lane, es->ws[buf], es->bias[buf],
                                            es->gate_ok[buf] ? es->gate[buf] : nullptr, xs, tmC, stage, stc, res,
@@ -1050,7 +1250,7 @@ struct PairCfg {
 // tmC: the output as a 16-bit 2-D tensor map with 32 x 32 boxes and the
 // 64-byte swizzle; used when `use_tma_store` (one 16-byte-aligned
 // destination), else the epilogue stores directly.
-template <int EPI, int OUT_DT>
+template <int EPI, int OUT_DT, bool SPLIT = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>::NUM_THREADS, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, GemmParams p, int use_tma_store) {
@@ -1101,6 +1301,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
+  const int num_units = SPLIT ? num_tiles * p.splits : num_tiles;  // split K: see GemmParams
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
 
@@ -1113,14 +1314,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       uint32_t phase = 0;
       ArmedLoads armed;  // both CTAs' loads complete on the leader's barriers
       bool ok = true;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int tile = u % num_tiles;
+        const int kb0 = SPLIT ? (u / num_tiles) * p.kb_split : 0;
+        const int kb1 = SPLIT ? min(kb0 + p.kb_split, num_kb) : num_kb;
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int arow = mb * 2 * GEMM_BM + (int)rank * GEMM_BM;
         const int brow = nb * BN + (int)rank * Cfg::BNH;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-          if (!(kb == p.stall_kb && tile == cluster_id)) {
+          if (!(kb == p.stall_kb && u == cluster_id)) {
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
             tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
@@ -1144,17 +1348,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued = false, ok = true;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int kb0 = SPLIT ? (u / num_tiles) * p.kb_split : 0;
+        const int kb1 = SPLIT ? min(kb0 + p.kb_split, num_kb) : num_kb;
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
           const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
 #pragma unroll
-          for (int k = 0; k < GEMM_BK / 32; ++k) umma_i8_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < GEMM_BK / 32; ++k)
+            umma_i8_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           issued = true;
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -1174,7 +1381,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
     const bool tma_st = Cfg::TMA_ST && use_tma_store;
     if (tma_st && lane == 0) tma_prefetch_desc(&tmC);
-    epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
+    epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true, 0, SPLIT>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
                                                       num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
                                                       lane, tma_st ? &tmC : nullptr,
                                                       sC + (warp - 2) * Cfg::EPI_BUFS * EPI_STAGE_BYTES);

@@ -93,6 +93,15 @@ int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, cons
                    const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
                    int64_t K, cudaStream_t stream, const EpiPost* post = nullptr);
 
+// Split-K W8A8 GEMM on CTA pairs (GemmParams::splits): the scratch size a
+// problem needs (0: it runs unsplit), and the launch, which falls back to
+// launch_gemm when no split pays.  The scratch's counters are zero on entry
+// and left zero by every complete launch.
+size_t splitk_scratch_bytes(int64_t M, int64_t N, int64_t K);
+int launch_gemm_splitk(int kind, const int8_t* a, const int8_t* b, const float* a_scale, const float* w_scale,
+                       const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K, void* scratch,
+                       size_t scratch_bytes, cudaStream_t stream);
+
 int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
                      int64_t K, cudaStream_t stream);

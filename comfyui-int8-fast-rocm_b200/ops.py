@@ -329,8 +329,34 @@ def _pad_k(a_q, w, mult, w_factor=1):
     return a_q, w
 
 
+# Split-K scratch of the W8A8 GEMM: bytes per (device, M, N, K), and one
+# zero-initialised buffer per (device, stream) -- calls on one stream run in
+# order, and every complete call leaves the buffer's counters at zero.
+_SPLITK_BYTES = {}
+_SPLITK_SCRATCH = {}
+
+
+def _splitk_scratch(device, M, Nn, K, stream):
+    key = (device.index, M, Nn, K)
+    nbytes = _SPLITK_BYTES.get(key)
+    if nbytes is None:
+        out = ctypes.c_uint64(0)
+        N.call("qlin_gemm_w8a8_splitk_scratch", M, Nn, K, ctypes.addressof(out))
+        nbytes = _SPLITK_BYTES[key] = int(out.value)
+    if nbytes == 0:
+        return None
+    skey = (device.index, stream)
+    buf = _SPLITK_SCRATCH.get(skey)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _SPLITK_SCRATCH[skey] = buf
+    return buf
+
+
 def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, per_row=True):
-    """W8A8 linear on int8 operands (int8_forward_dynamic(_per_row) epilogue)."""
+    """W8A8 linear on int8 operands (int8_forward_dynamic(_per_row) epilogue).
+    Problems too small to fill the GPU with 256 x 256 tiles split K over CTA
+    pairs (``qlin_gemm_w8a8_splitk``, same output bits)."""
     _check_gemm(a_q, w_q)
     a_q, w_q = _pad_k(_aligned(a_q), _aligned(w_q), 16)
     M, K = a_q.shape
@@ -347,6 +373,12 @@ def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, p
     if bias is not None:
         bias = bias.reshape(-1).to(device=a_q.device, dtype=out_dtype).contiguous()
     st = _stream(a_q)
+    scratch = _splitk_scratch(a_q.device, M, Nn, K, st)
+    if scratch is not None:
+        N.call("qlin_gemm_w8a8_splitk", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
+               N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
+               M, Nn, K, scratch.data_ptr(), scratch.numel(), st)
+        return out
     N.call("qlin_gemm_w8a8", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
            N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
            M, Nn, K, st)

@@ -81,7 +81,8 @@ QLIN_API const char* qlin_last_error(void);
 /* Reads and clears the device-side error words of the current device (bit 0:
  * a pipeline wait inside a GEMM kernel timed out; bit 1: a row kernel's
  * bulk-copy wait timed out; bit 2: after a GEMM timeout its in-flight work
- * did not drain within the limit).  Synchronises `stream`. */
+ * did not drain within the limit; bit 3: a split-K GEMM found its scratch
+ * counters non-zero on entry).  Synchronises `stream`. */
 QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits);
 
 /* ---- failure detection ---------------------------------------------------
@@ -229,6 +230,30 @@ QLIN_API int qlin_quant_act_int8_situ(const void* x, int x_dtype, int64_t M, int
 QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                             int wscale_mode, const void* bias, void* out, int out_dtype,
                             int64_t M, int64_t N, int64_t K, void* stream);
+
+/* qlin_gemm_w8a8 with the K dimension split over CTA pairs, for problems
+ * whose 256 x 256 output tiles leave most of the GPU idle (e.g. M = 1024,
+ * N = 3072): each tile's K range is cut into up to 3 parts that run on
+ * different CTA pairs; the parts meet through int32 partials in `scratch`
+ * and the last one to finish adds them (exact integer sums) and runs the
+ * qlin_gemm_w8a8 epilogue, so the output is bit-identical to qlin_gemm_w8a8.
+ * qlin_gemm_w8a8_splitk_scratch gives the scratch size for a problem on the
+ * current device (0: no split pays; qlin_gemm_w8a8_splitk then runs the
+ * unsplit kernel and needs no scratch).  scratch: that many bytes of device
+ * memory, 256-byte aligned, whose first 64 KB (counters and flags, at the
+ * same place for every problem size) are zero before its first use; every
+ * complete call leaves them zero again, so one scratch buffer serves calls
+ * of any shape in turn.  Calls that share one scratch must not overlap on
+ * the GPU.  Counters found non-zero on entry set bit 3 (value 8) of the
+ * device error word (qlin_device_error) and the call writes no output.
+ * Replaces: the reference's one-kernel triton_int8_linear(_per_row)
+ * launch (int8_fused_kernel.py:332-377), whose grid is one program per
+ * 128 x 256 output tile at any size. */
+QLIN_API int qlin_gemm_w8a8_splitk_scratch(int64_t M, int64_t N, int64_t K, uint64_t* bytes);
+QLIN_API int qlin_gemm_w8a8_splitk(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                   int wscale_mode, const void* bias, void* out, int out_dtype,
+                                   int64_t M, int64_t N, int64_t K, void* scratch, uint64_t scratch_bytes,
+                                   void* stream);
 
 /* qlin_gemm_w8a8 followed, inside the epilogue, by the element-wise steps
  * that follow a DiT block's linears (out_dtype BF16 or F16; y = the

@@ -638,3 +638,81 @@ def test_rotated_codes_vs_reference_full_size(P, golden_c1, name, K, g, kind):
     assert hashlib.sha256(qf.tobytes()).hexdigest() == str(golden_c1[f"{name}_q_sha"])
     differ = int((s.cpu().numpy().reshape(-1) != golden_c1[f"{name}_s"]).sum())
     assert differ == int(golden_c1[f"{name}_scale_rows_differ"]) == 0
+
+
+# ---------------------------------------------------------------------------
+# split K (small W8A8 problems): bit-equal to the unsplit kernel
+# ---------------------------------------------------------------------------
+
+
+def _unsplit_w8a8(P, xq, xs, wq, ws, b, out_dtype, per_row=True):
+    """qlin_gemm_w8a8 called directly: the CTA-pair kernel without split K."""
+    from comfyui_int8_fast_rocm_b200 import _native
+    M, K = xq.shape
+    Nn = wq.shape[0]
+    out = torch.empty((M, Nn), dtype=out_dtype, device=xq.device)
+    _native.call("qlin_gemm_w8a8", xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+           _native.WSCALE_ROW if per_row else _native.WSCALE_TENSOR, 0 if b is None else b.data_ptr(),
+           out.data_ptr(),
+           P.ops.dtype_code(out_dtype), M, Nn, K, torch.cuda.current_stream().cuda_stream)
+    return out
+
+
+def _scratch_bytes(M, N, K):
+    import ctypes
+    from comfyui_int8_fast_rocm_b200 import _native
+    out = ctypes.c_uint64(0)
+    _native.call("qlin_gemm_w8a8_splitk_scratch", M, N, K, ctypes.addressof(out))
+    return int(out.value)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 768, 8192), (300, 520, 8192), (256, 1024, 16384), (1024, 2048, 16384)])
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+def test_w8a8_splitk_equals_unsplit(P, M, N, K, dt):
+    x = gi.activation(40, M, K, dt)
+    w = gi.weight(40, N, K)
+    b = dev(gi.bias(40, N, dt), dt)
+    wq, ws = P.ops.quant_weight_int8(dev(w))
+    xq, xs = P.ops.quant_act_int8(dev(x, dt))
+    xs = xs.reshape(-1).contiguous()
+    ws = ws.reshape(-1).contiguous()
+    assert _scratch_bytes(M, N, K) > 0  # these shapes split
+    want = _unsplit_w8a8(P, xq, xs, wq, ws, b, TDT[dt])
+    for _ in range(2):  # the scratch's counters are reset by every call
+        got = P.ops.gemm_w8a8(xq, xs, wq, ws, b, TDT[dt])
+        np.testing.assert_array_equal(tbits(got), tbits(want))
+    assert P.ops.device_error() == 0
+
+
+def test_w8a8_splitk_tensorwise_and_no_bias(P):
+    M, N, K = 512, 1024, 12288
+    x = gi.activation(41, M, K, "bf16")
+    wq = dev(np.random.default_rng(41).integers(-127, 128, (N, K), dtype=np.int8))
+    ws = torch.tensor([0.0123], device="cuda")
+    xq, xs = P.ops.quant_act_int8(dev(x, "bf16"))
+    xs = xs.reshape(-1).contiguous()
+    want = _unsplit_w8a8(P, xq, xs, wq, ws, None, torch.bfloat16, per_row=False)
+    got = P.ops.gemm_w8a8(xq, xs, wq, ws, None, torch.bfloat16, per_row=False)
+    np.testing.assert_array_equal(tbits(got), tbits(want))
+
+
+def test_w8a8_splitk_rows_vs_oracle(P):
+    """A split problem with rotation (three K parts of 64 slabs) against the
+    oracle on sampled rows."""
+    M, N, K = 768, 1536, 24576
+    x = gi.activation(42, M, K, "bf16")
+    w = gi.weight(42, N, K)
+    b = gi.bias(42, N, "bf16")
+    gq, gs = P.ops.quant_weight_int8(dev(w), ("sylvester", 128))
+    xq, xs = P.ops.quant_act_int8(dev(x, "bf16"), ("sylvester", 128))
+    y = P.ops.gemm_w8a8(xq, xs, gq, gs, dev(b, "bf16"), torch.bfloat16)
+    rows = _rows_sample(M, seed=43)
+    yo = O.w8a8_epilogue_per_row(O.int_mm(xq.cpu().numpy()[rows], gq.cpu().numpy()), xs.cpu().numpy()[rows],
+                                 gs.cpu().numpy(), b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
+def test_w8a8_large_problem_does_not_split(P):
+    assert _scratch_bytes(4096, 12288, 3072) == 0
+    assert _scratch_bytes(8192, 9216, 12288) == 0
+    assert _scratch_bytes(1024, 3072, 3072) == 0  # measured slower split (partial traffic)
