@@ -27,7 +27,7 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", 
          # reproduce two-rounding float32 sequences bit for bit (explicit
          # fma / __fmaf_rn / fma.rn.f32x2 still issue fused operations)
          "-fmad=false"]
-SOURCES = ["abi.cu", "rowquant.cu", "gemm.cu", "weights.cu", "dit.cu"]
+SOURCES = ["abi.cu", "rowquant.cu", "gemm.cu", "weights.cu", "dit.cu", "noalloc.cu"]
 
 
 def nvcc():

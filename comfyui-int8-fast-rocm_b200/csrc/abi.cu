@@ -330,6 +330,19 @@ QLIN_API int qlin_gemm_w8a8_splitk(const int8_t* a, const float* a_scale, const 
                             static_cast<cudaStream_t>(stream));
 }
 
+QLIN_API int qlin_gemm_w8a8_splitk_noalloc(const int8_t* a, const float* a_scale, const int8_t* w,
+                                           const float* w_scale, int wscale_mode, const void* bias, void* out,
+                                           int out_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  int rc = gemm_common_checks(a, w, M, N, K, 16);
+  if (rc || M == 0 || N == 0) return rc;
+  if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
+  if (!a_scale || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (wscale_mode != QLIN_WSCALE_ROW && wscale_mode != QLIN_WSCALE_TENSOR)
+    return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
+  return launch_gemm_splitk_noalloc(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, a, w, a_scale,
+                                    w_scale, bias, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
 QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                                   int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
                                   int64_t K, int64_t gelu_col0, const void* residual, int64_t ld_res,

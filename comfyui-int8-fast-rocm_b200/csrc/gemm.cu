@@ -371,6 +371,8 @@ bool splitk_plan(int64_t M, int64_t N, int64_t K, int sms, int* splits, int* kb_
   return false;
 }
 
+size_t splitk_header_bytes() { return SPLITK_HEADER; }
+
 size_t splitk_scratch_bytes(int64_t M, int64_t N, int64_t K) {
   int splits, kb_split;
   if (!splitk_plan(M, N, K, device_sm_count(), &splits, &kb_split)) return 0;

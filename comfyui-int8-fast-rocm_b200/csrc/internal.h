@@ -101,6 +101,13 @@ size_t splitk_scratch_bytes(int64_t M, int64_t N, int64_t K);
 int launch_gemm_splitk(int kind, const int8_t* a, const int8_t* b, const float* a_scale, const float* w_scale,
                        const void* bias, void* out, int out_dt, int64_t M, int64_t N, int64_t K, void* scratch,
                        size_t scratch_bytes, cudaStream_t stream);
+// Bytes at the start of a split-K scratch holding its counters and flags.
+size_t splitk_header_bytes();
+// launch_gemm_splitk on the library's fixed device array instead of caller
+// scratch (noalloc.cu); allocates nothing.
+int launch_gemm_splitk_noalloc(int kind, const int8_t* a, const int8_t* b, const float* a_scale,
+                               const float* w_scale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,
+                               int64_t K, cudaStream_t stream);
 
 int launch_gemm_g128(bool a_int4_groups, const int8_t* a, const float* a_scale, const int8_t* w_packed,
                      const uint16_t* w_gscale, const void* bias, void* out, int out_dt, int64_t M, int64_t N,

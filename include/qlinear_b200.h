@@ -255,6 +255,26 @@ QLIN_API int qlin_gemm_w8a8_splitk(const int8_t* a, const float* a_scale, const 
                                    int64_t M, int64_t N, int64_t K, void* scratch, uint64_t scratch_bytes,
                                    void* stream);
 
+/* qlin_gemm_w8a8_splitk for callers that cannot allocate device memory when
+ * they run the GEMM (an engine that reserves its GPU memory up front and
+ * forbids later allocations, a plugin host that owns the allocator and
+ * passes only input and output buffers): the split-K scratch is a fixed
+ * 16 MiB array inside this library's device image instead of a
+ * caller-provided buffer.  This call allocates nothing.  Every GPU that
+ * loads the library holds that array until the process exits.  A problem
+ * whose split needs more than the array holds is refused with
+ * QLIN_ERR_UNSUPPORTED (on a 148-SM B200 every split plan fits: at most
+ * 12.1 MiB).  The first call on each device looks the array's address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Each split call clears the array's counters first (cudaMemsetAsync on
+ * `stream`).  All calls share the one array: calls that overlap on the GPU
+ * (several streams or host threads) race on it and must be serialised by
+ * the caller.  Same arguments and output bits as qlin_gemm_w8a8.  No
+ * counterpart in the reference. */
+QLIN_API int qlin_gemm_w8a8_splitk_noalloc(const int8_t* a, const float* a_scale, const int8_t* w,
+                                           const float* w_scale, int wscale_mode, const void* bias, void* out,
+                                           int out_dtype, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* qlin_gemm_w8a8 followed, inside the epilogue, by the element-wise steps
  * that follow a DiT block's linears (out_dtype BF16 or F16; y = the
  * qlin_gemm_w8a8 value, already rounded to out_dtype):
