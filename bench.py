@@ -564,7 +564,9 @@ def _cfg_time(fn, flush):
     ts = []
     for i in range(CFG_WARM + CFG_ITERS):
         flush.zero_()
-        torch.cuda._sleep(200_000)
+        # about 1 ms of GPU sleep: the host enqueues the call's kernels before
+        # the first event fires, so the events time the kernels, not Python
+        torch.cuda._sleep(2_000_000)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
@@ -641,6 +643,32 @@ def run_configs(pkg, dev, int8_peak, which="all"):
     tq = _cfg_time(lambda: ops.quant_act_int4(xr, rrot, 0), flush)
     tg = _cfg_time(lambda: ops.gemm_w4a4(aq, asc, pw, psc, b, torch.bfloat16), flush)
     out["w4a4_row_regular256"] = entry(Mv, Nv, Kv, tg, tq)
+    # split K (qlin_gemm_w8a8_splitk) on few-tile, long-K W8A8 problems,
+    # against the unsplit kernel (ops.gemm_w8a8 splits them by itself)
+    sk = []
+    for Mv, Nv, Kv in ((256, 1024, 16384), (768, 1536, 24576), (512, 768, 8192)):
+        xq = torch.randint(-127, 128, (Mv, Kv), dtype=torch.int8, device=dev)
+        wq = torch.randint(-127, 128, (Nv, Kv), dtype=torch.int8, device=dev)
+        xs = rnd((Mv,), 1e-3, seed=5).abs() + 1e-5
+        ws = rnd((Nv,), 1e-3, seed=6).abs() + 1e-5
+        b = rnd((Nv,), 0.01, seed=7).to(torch.bfloat16)
+        yu = torch.empty((Mv, Nv), dtype=torch.bfloat16, device=dev)
+        st = torch.cuda.current_stream(dev).cuda_stream
+
+        def unsplit():
+            pkg._native.call("qlin_gemm_w8a8", xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+                             pkg._native.WSCALE_ROW, b.data_ptr(), yu.data_ptr(), pkg._native.BF16, Mv, Nv, Kv, st)
+        t_split = _cfg_time(lambda: ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16), flush)
+        t_unsplit = _cfg_time(unsplit, flush)
+        same = bool(torch.equal(ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16).view(torch.int16),
+                                yu.view(torch.int16)))
+        e = entry(Mv, Nv, Kv, t_split, 0.0)
+        e.pop("quant_us")
+        e.update({"unsplit_us": round(t_unsplit, 1), "speedup": round(t_unsplit / t_split, 2),
+                  "bit_equal_to_unsplit": same})
+        sk.append(e)
+        del xq, wq, xs, ws, b, yu
+    out["w8a8_splitk"] = sk
     del flush
     torch.cuda.empty_cache()
     return out
@@ -906,6 +934,8 @@ def _configs_summary(cfgs):
             out[key] = {k: v[k] for k in ("M", "N", "K", "gemm_us", "frac", "quant_us") if k in v}
         elif isinstance(v, list):
             out[key] = [{k: r[k] for k in ("N", "gemm_us", "frac") if k in r} for r in v]
+    if cfgs.get("w8a8_splitk"):
+        out["w8a8_splitk_speedup"] = [r["speedup"] for r in cfgs["w8a8_splitk"]]
     return out
 
 
