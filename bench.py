@@ -995,6 +995,62 @@ def cpu_configs():
     print(json.dumps({"cpu_configs": res}), flush=True)
 
 
+PROFILE_CASES = ("g128_w4a8", "g128_w4a4", "w4a4_row", "quant_syl128_8192x12288", "w8a8_splitk")
+
+
+def profile_case(name):
+    """Run one kernel case three times (the ncu captures under profiles/ take
+    the last launch with -s 2 -c 1) and exit: no timing, no other kernels
+    between the launches except their inputs' preparation."""
+    pkg = load_pkg()
+    ops = pkg.ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def rnd(shape, scale=1.0):
+        return torch.randn(shape, generator=g, device=dev) * scale
+
+    if name in ("g128_w4a8", "g128_w4a4"):
+        Mv, Nv, Kv = 4096, 12288, 3072
+        w4 = name == "g128_w4a4"
+        rot = ("sylvester", 128) if w4 else None
+        pw, gs = ops.quant_weight_int4(rnd((Nv, Kv), 0.02).to(torch.bfloat16), rot, 128)
+        x = rnd((Mv, Kv)).to(torch.bfloat16)
+        if w4:
+            aq, asc = ops.quant_act_int4(x, rot, 128)
+        else:
+            aq, asc = ops.quant_act_int8(x)
+        b = rnd((Nv,), 0.01).to(torch.bfloat16)
+        fn = lambda: ops.gemm_w4_g128(aq, asc, pw, gs, b, torch.bfloat16, a_int4_groups=w4)
+    elif name == "w4a4_row":
+        Mv, Nv, Kv = 4096, 12288, 3072
+        rot = ("regular", 256)
+        pw, ps = ops.quant_weight_int4(rnd((Nv, Kv), 0.02), rot)
+        aq, asc = ops.quant_act_int4(rnd((Mv, Kv)).to(torch.bfloat16), rot, 0)
+        b = rnd((Nv,), 0.01).to(torch.bfloat16)
+        fn = lambda: ops.gemm_w4a4(aq, asc, pw, ps, b, torch.bfloat16)
+    elif name == "quant_syl128_8192x12288":
+        x = rnd((8192, 12288)).to(torch.bfloat16)
+        fn = lambda: ops.quant_act_int8(x, ("sylvester", 128))
+    elif name == "w8a8_splitk":
+        Mv, Nv, Kv = 768, 1536, 24576
+        xq = torch.randint(-127, 128, (Mv, Kv), dtype=torch.int8, device=dev)
+        wq = torch.randint(-127, 128, (Nv, Kv), dtype=torch.int8, device=dev)
+        xs = rnd((Mv,), 1e-3).abs() + 1e-5
+        ws = rnd((Nv,), 1e-3).abs() + 1e-5
+        fn = lambda: ops.gemm_w8a8(xq, xs, wq, ws, None, torch.bfloat16)
+    else:
+        raise SystemExit(f"unknown profile case {name}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if ops.device_error() != 0:
+        raise SystemExit("device error word set")
+    print(f"profile case {name}: 3 launches done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1009,8 +1065,12 @@ def main():
                          "16 samples, torch profiler) and exit")
     ap.add_argument("--cpu-configs", action="store_true",
                     help="time the reference's PyTorch CPU path per configuration on the host cores and exit")
+    ap.add_argument("--profile-case", choices=PROFILE_CASES,
+                    help="launch one kernel case three times and exit (for the ncu captures under profiles/)")
     args = ap.parse_args()
-    if args.cpu_configs:
+    if args.profile_case:
+        profile_case(args.profile_case)
+    elif args.cpu_configs:
         cpu_configs()
     elif args.dit_breakdown:
         dit_breakdown()
