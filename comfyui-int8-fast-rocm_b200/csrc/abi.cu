@@ -8,6 +8,21 @@
 #include "internal.h"
 #include "rowquant.cuh"
 
+#include <nvtx3/nvToolsExt.h>
+
+namespace {
+// One NVTX range per C-ABI call, named after the entry point (visible in
+// Nsight Systems / Nsight Compute timelines; a few nanoseconds when no tool
+// is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+}  // namespace
+#define QLIN_RANGE() NvtxRange qlin_nvtx_range_(__func__)
+
 namespace qlin {
 
 static thread_local std::string t_last_error;
@@ -109,6 +124,7 @@ extern "C" {
 QLIN_API int qlin_version(void) { return 10000; }
 
 QLIN_API int qlin_set_device(int device) {
+  QLIN_RANGE();
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   return QLIN_OK;
@@ -117,6 +133,7 @@ QLIN_API int qlin_set_device(int device) {
 QLIN_API const char* qlin_last_error(void) { return t_last_error.c_str(); }
 
 QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits) {
+  QLIN_RANGE();
   if (!error_bits) return fail(QLIN_ERR_INVALID_ARG, "error_bits is null");
   int rc = check_device();
   if (rc) return rc;
@@ -128,6 +145,7 @@ QLIN_API int qlin_device_error(void* stream, uint32_t* error_bits) {
 }
 
 QLIN_API int qlin_set_wait_limit(uint64_t limit_ns) {
+  QLIN_RANGE();
   int rc = check_device();
   if (rc) return rc;
   if (limit_ns == 0) limit_ns = 2000000000ull;
@@ -138,6 +156,7 @@ QLIN_API int qlin_set_wait_limit(uint64_t limit_ns) {
 }
 
 QLIN_API int qlin_selftest_wait_timeout(int which, void* stream) {
+  QLIN_RANGE();
   int rc = check_device();
   if (rc) return rc;
   if (which == 0) return launch_wait_selftest(static_cast<cudaStream_t>(stream));
@@ -147,6 +166,7 @@ QLIN_API int qlin_selftest_wait_timeout(int which, void* stream) {
 
 QLIN_API int qlin_selftest_gemm_stall(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                                       void* out, int64_t M, int64_t N, int64_t K, int64_t stall_kb, void* stream) {
+  QLIN_RANGE();
   if (!a || !a_scale || !w || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
   if (K % 16) return fail(QLIN_ERR_ALIGNMENT, "K must be a multiple of 16");
   if (!aligned16(a) || !aligned16(w) || !aligned16(out)) return fail(QLIN_ERR_ALIGNMENT, "operands must be 16-byte aligned");
@@ -157,6 +177,7 @@ QLIN_API int qlin_selftest_gemm_stall(const int8_t* a, const float* a_scale, con
 
 QLIN_API int qlin_quant_act_int8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                  int rot_group, float rot_c, int8_t* q, float* scale, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
   if (M == 0 || K == 0) return QLIN_OK;
@@ -179,6 +200,7 @@ QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int
                                       float eps, const void* norm_weight, const void* mod_mul, int64_t mul_ld,
                                       const void* mod_add, int64_t add_ld, int64_t rows_per_sample, int rot_kind, int rot_group,
                                       float rot_c, int8_t* q, float* scale, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (x_dtype != QLIN_BF16 && x_dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16 or F16");
   if (norm_kind != QLIN_NORM_NONE && norm_kind != QLIN_NORM_LAYER && norm_kind != QLIN_NORM_RMS)
@@ -204,6 +226,7 @@ QLIN_API int qlin_quant_act_int8_norm(const void* x, int x_dtype, int64_t M, int
 
 QLIN_API int qlin_quant_act_int8_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                       int rot_group, float rot_c, int8_t* q, float* scale, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < 2 * K) return fail(QLIN_ERR_INVALID_ARG, "bad shape (rows are [hidden | gate], ldx >= 2K)");
   if (x_dtype != QLIN_BF16 && x_dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16 or F16");
   if (M == 0 || K == 0) return QLIN_OK;
@@ -220,6 +243,7 @@ QLIN_API int qlin_quant_act_int8_situ(const void* x, int x_dtype, int64_t M, int
 QLIN_API int qlin_quant_act_int8_cat(const void* x1, int64_t ld1, int64_t K1, const void* x2, int64_t ld2,
                                      int64_t K2, int x_dtype, int64_t M, int rot_kind, int rot_group, float rot_c,
                                      int8_t* q, float* scale, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K1 <= 0 || K2 <= 0 || ld1 < K1 || ld2 < K2) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
   if (M == 0) return QLIN_OK;
@@ -236,6 +260,7 @@ QLIN_API int qlin_quant_act_int8_cat(const void* x1, int64_t ld1, int64_t K1, co
 QLIN_API int qlin_qk_norm_rope(void* qkv, int dtype, int64_t rows, int64_t ld, int heads, int head_dim,
                                const void* q_weight, const void* k_weight, float eps, const float* cos_tab,
                                const float* sin_tab, int64_t positions, void* stream) {
+  QLIN_RANGE();
   if (rows < 0 || heads < 0 || positions < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (dtype != QLIN_BF16 && dtype != QLIN_F16) return fail(QLIN_ERR_INVALID_ARG, "dtype must be BF16 or F16");
   if (head_dim != 64 && head_dim != 128) return fail(QLIN_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
@@ -257,6 +282,7 @@ QLIN_API int qlin_qk_norm_rope(void* qkv, int dtype, int64_t rows, int64_t ld, i
 QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                                  int rot_group, float rot_c, int group, float clamp_min, int8_t* q, float* scale,
                                  void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
   if (group != 0 && group != 128) return fail(QLIN_ERR_UNSUPPORTED, "int4 group must be 0 (per row) or 128");
@@ -280,6 +306,7 @@ QLIN_API int qlin_quant_act_int4(const void* x, int x_dtype, int64_t M, int64_t 
 
 QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int rot_kind,
                          int rot_group, float rot_c, void* out, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
   if (rot_kind == QLIN_ROT_NONE) return fail(QLIN_ERR_INVALID_ARG, "qlin_rotate needs a rotation");
@@ -298,6 +325,7 @@ QLIN_API int qlin_rotate(const void* x, int x_dtype, int64_t M, int64_t K, int64
 QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                             int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
                             int64_t K, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w, M, N, K, 16);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -309,6 +337,7 @@ QLIN_API int qlin_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t*
 }
 
 QLIN_API int qlin_gemm_w8a8_splitk_scratch(int64_t M, int64_t N, int64_t K, uint64_t* bytes) {
+  QLIN_RANGE();
   if (!bytes) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
   if (M < 0 || N < 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
     return fail(QLIN_ERR_INVALID_ARG, "bad GEMM shape");
@@ -319,6 +348,7 @@ QLIN_API int qlin_gemm_w8a8_splitk_scratch(int64_t M, int64_t N, int64_t K, uint
 QLIN_API int qlin_gemm_w8a8_splitk(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                                    int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
                                    int64_t K, void* scratch, uint64_t scratch_bytes, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w, M, N, K, 16);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -333,6 +363,7 @@ QLIN_API int qlin_gemm_w8a8_splitk(const int8_t* a, const float* a_scale, const 
 QLIN_API int qlin_gemm_w8a8_splitk_noalloc(const int8_t* a, const float* a_scale, const int8_t* w,
                                            const float* w_scale, int wscale_mode, const void* bias, void* out,
                                            int out_dtype, int64_t M, int64_t N, int64_t K, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w, M, N, K, 16);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -347,6 +378,7 @@ QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const i
                                   int wscale_mode, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
                                   int64_t K, int64_t gelu_col0, const void* residual, int64_t ld_res,
                                   const void* gate, int64_t gate_ld, int64_t rows_per_gate, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w, M, N, K, 16);
   if (rc || M == 0 || N == 0) return rc;
   if (out_dtype != QLIN_BF16 && out_dtype != QLIN_F16)
@@ -376,6 +408,7 @@ QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, con
                                       const float* w_scale_shard, int wscale_mode, const void* bias_shard,
                                       void* const* out_bufs, int n_out, int64_t col_off, int64_t ldo, int out_dtype,
                                       int64_t M, int64_t N_shard, int64_t K, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w_shard, M, N_shard, K, 16);
   if (rc || M == 0 || N_shard == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -403,6 +436,7 @@ QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, con
 
 QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c, int64_t M, int64_t N, int64_t K,
                          void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w, M, N, K, 16);
   if (rc || M == 0 || N == 0) return rc;
   if (!c) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
@@ -412,6 +446,7 @@ QLIN_API int qlin_int_mm(const int8_t* a, const int8_t* w, int32_t* c, int64_t M
 
 QLIN_API int qlin_int4_mm(const int8_t* a, const int8_t* w_packed, int32_t* c, int64_t M, int64_t N, int64_t K,
                           void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w_packed, M, N, K, 32);
   if (rc || M == 0 || N == 0) return rc;
   if (!c) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
@@ -422,6 +457,7 @@ QLIN_API int qlin_int4_mm(const int8_t* a, const int8_t* w_packed, int32_t* c, i
 QLIN_API int qlin_gemm_w4a4(const int8_t* a, const float* a_scale, const int8_t* w_packed, const float* w_scale,
                             const void* bias, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
                             void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w_packed, M, N, K, 32);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -433,6 +469,7 @@ QLIN_API int qlin_gemm_w4a4(const int8_t* a, const float* a_scale, const int8_t*
 QLIN_API int qlin_gemm_w4a8_g128(const int8_t* a, const float* a_scale, const int8_t* w_packed,
                                  const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
                                  int64_t M, int64_t N, int64_t K, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w_packed, M, N, K, 128);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -444,6 +481,7 @@ QLIN_API int qlin_gemm_w4a8_g128(const int8_t* a, const float* a_scale, const in
 QLIN_API int qlin_gemm_w4a4_g128(const int8_t* a, const float* a_gscale, const int8_t* w_packed,
                                  const uint16_t* w_gscale_bf16, const void* bias, void* out, int out_dtype,
                                  int64_t M, int64_t N, int64_t K, void* stream) {
+  QLIN_RANGE();
   int rc = gemm_common_checks(a, w_packed, M, N, K, 128);
   if (rc || M == 0 || N == 0) return rc;
   if (!float_dt(out_dtype)) return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16, F16 or F32");
@@ -454,6 +492,7 @@ QLIN_API int qlin_gemm_w4a4_g128(const int8_t* a, const float* a_gscale, const i
 
 QLIN_API int qlin_quant_weight_int8(const void* w, int w_dtype, int64_t N, int64_t K, int rot_kind, int rot_group,
                                     float rot_c, int8_t* q, float* scale, void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(w_dtype)) return fail(QLIN_ERR_INVALID_ARG, "w_dtype must be BF16, F16 or F32");
   if (N == 0 || K == 0) return QLIN_OK;
@@ -470,6 +509,7 @@ QLIN_API int qlin_quant_weight_int8(const void* w, int w_dtype, int64_t N, int64
 
 QLIN_API int qlin_quant_weight_int4(const void* w, int w_dtype, int64_t N, int64_t K, int rot_kind, int rot_group,
                                     float rot_c, int group, int8_t* packed, float* scale, void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(w_dtype)) return fail(QLIN_ERR_INVALID_ARG, "w_dtype must be BF16, F16 or F32");
   if (group != 0 && group != 128) return fail(QLIN_ERR_UNSUPPORTED, "int4 group must be 0 or 128");
@@ -493,6 +533,7 @@ QLIN_API int qlin_quant_weight_int4(const void* w, int w_dtype, int64_t N, int64
 QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
                                     const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K, int8_t* q,
                                     float* scale, void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0 || group_size <= 0 || K % group_size)
     return fail(QLIN_ERR_INVALID_ARG, "bad shape / group_size");
   if (N == 0 || K == 0) return QLIN_OK;
@@ -509,6 +550,7 @@ QLIN_API int qlin_requant_asym_w4a8(const uint8_t* packed, const float* codebook
 QLIN_API int qlin_dequant_asym_w4a8(const uint8_t* packed, const float* codebook, const float* s_channel,
                                     const uint8_t* s_rel_fp8, int group_size, int64_t N, int64_t K, float* out,
                                     void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0 || group_size <= 0 || K % group_size)
     return fail(QLIN_ERR_INVALID_ARG, "bad shape / group_size");
   if (N == 0 || K == 0) return QLIN_OK;
@@ -523,6 +565,7 @@ QLIN_API int qlin_dequant_asym_w4a8(const uint8_t* packed, const float* codebook
 
 QLIN_API int qlin_dequant_int8(const int8_t* q, const float* scale, int scale_mode, int64_t N, int64_t K,
                                int rot_kind, int rot_group, float rot_c, float* out, void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (N == 0 || K == 0) return QLIN_OK;
   if (!q || !scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
@@ -539,6 +582,7 @@ QLIN_API int qlin_dequant_int8(const int8_t* q, const float* scale, int scale_mo
 QLIN_API int qlin_requant_int8(const float* w, const float* scale, int scale_mode, int64_t N, int64_t K,
                                int rot_kind, int rot_group, float rot_c, int round_mode, uint64_t seed, int8_t* q,
                                void* stream) {
+  QLIN_RANGE();
   if (N < 0 || K < 0) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (round_mode != QLIN_ROUND_NEAREST && round_mode != QLIN_ROUND_STOCHASTIC)
     return fail(QLIN_ERR_INVALID_ARG, "bad round_mode");
@@ -556,6 +600,7 @@ QLIN_API int qlin_requant_int8(const float* w, const float* scale, int scale_mod
 }
 
 QLIN_API int qlin_situ(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, void* out, void* stream) {
+  QLIN_RANGE();
   if (M < 0 || K < 0 || ldx < 2 * K) return fail(QLIN_ERR_INVALID_ARG, "bad shape");
   if (!float_dt(x_dtype)) return fail(QLIN_ERR_INVALID_ARG, "x_dtype must be BF16, F16 or F32");
   if (M == 0 || K == 0) return QLIN_OK;
