@@ -299,6 +299,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Remote mbarrier arrival with the default semantics (release, CTA scope),
+// as CUTLASS's cluster barriers arrive: a cluster-scope release waits for
+// the memory system (about 1200 cycles per arrival, measured on B200).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // TMA load into this CTA's shared memory whose completion is counted on an
 // mbarrier of the CTA pair (here: the leader's), no multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t mbar_cluster_addr, int x, int y) {

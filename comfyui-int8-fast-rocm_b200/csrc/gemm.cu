@@ -71,10 +71,10 @@ int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
   return QLIN_OK;
 }
 
-template <int EPI, int OUT_DT, bool SPLIT = false>
+template <int EPI, int OUT_DT, bool SPLIT = false, bool B_INT4 = false>
 int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
-  using Cfg = PairCfg<EPI, OUT_DT>;
-  auto kern = gemm_i8_pair_kernel<EPI, OUT_DT, SPLIT>;
+  using Cfg = PairCfg<EPI, OUT_DT, B_INT4>;
+  auto kern = gemm_i8_pair_kernel<EPI, OUT_DT, SPLIT, B_INT4>;
   // 16-bit output through TMA stores: one destination, 16-byte aligned rows
   CUtensorMap tc = ta;
   int use_tma_store = 0;
@@ -179,6 +179,16 @@ bool pair_disabled() {
   return off;
 }
 
+// QLIN_INT4_NO_PAIR=1 keeps packed-int4 GEMMs on the single-CTA kernel
+// (comparison runs).
+bool int4_pair_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_INT4_NO_PAIR");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
 GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale, const float* w_scale, const void* bias,
                        const OutSpec& o, int sms) {
   GemmParams p{};
@@ -242,6 +252,21 @@ int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, cons
     GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
     if (post != nullptr) set_post(p, *post);
     return dispatch_pair(kind, out_dt, ta, tb, p, stream, post != nullptr);
+  }
+  // Packed-int4 weights on CTA pairs (each CTA unpacks its own 128 rows).
+  if (b_int4 && (kind == GEMM_W4A4_ROW || kind == GEMM_I32) && post == nullptr && o.nout == 1 && M >= 256 &&
+      N >= 256 && sms >= 2 && !pair_disabled() && !int4_pair_disabled()) {
+    int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap(&tb, b, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), GEMM_BK / 2, 128,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
+    if (kind == GEMM_I32) return launch_pair_cfg<EPI_I32, DT_F32, false, true>(ta, tb, p, stream);
+    if (out_dt == DT_BF16) return launch_pair_cfg<EPI_W4A4_ROW, DT_BF16, false, true>(ta, tb, p, stream);
+    if (out_dt == DT_F16) return launch_pair_cfg<EPI_W4A4_ROW, DT_F16, false, true>(ta, tb, p, stream);
+    if (out_dt == DT_F32) return launch_pair_cfg<EPI_W4A4_ROW, DT_F32, false, true>(ta, tb, p, stream);
+    return fail(QLIN_ERR_UNSUPPORTED, "unsupported W4A4 output dtype");
   }
   // Narrow outputs waste half a 256-wide tile; use 128 columns there.
   const int BN = (N <= 128) ? 128 : 256;

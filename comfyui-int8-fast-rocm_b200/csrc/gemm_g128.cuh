@@ -475,10 +475,6 @@ struct G128PairCfg {
   static constexpr uint32_t TMEM_COLS = NBUF * GPS * BN;
 };
 
-// Remote mbarrier arrival with the default semantics (release, CTA scope).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
 
 // Nibble unpack of a [64 rows][KS/2 packed bytes] slab's 64-byte group
 // column `grp` into the 128-byte swizzled [64][128] int8 layout (16*q per

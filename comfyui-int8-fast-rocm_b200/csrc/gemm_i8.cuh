@@ -1228,7 +1228,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, B_INT4>::NUM_THREADS, 1)
 //   tfull[b]  both CTAs: multicast commit at tile end
 //   tempty[b] leader only: 8 local + 8 remote epilogue-warp arrivals
 // ---------------------------------------------------------------------------
-template <int EPI, int OUT_DT>
+template <int EPI, int OUT_DT, bool B_INT4 = false>
 struct PairCfg {
   static constexpr int BN = 256;           // tile columns (both CTAs)
   static constexpr int BNH = 128;          // B rows loaded per CTA
@@ -1237,37 +1237,74 @@ struct PairCfg {
   // overlaps a store with the next chunk; the operand ring gives up a stage)
   static constexpr bool TMA_ST = (OUT_DT == DT_BF16 || OUT_DT == DT_F16) && EPI != EPI_I32;
   static constexpr int EPI_BUFS = (EPI & EPI_POST) ? 2 : 1;
-  static constexpr int STAGES = (TMA_ST && EPI_BUFS == 2) ? 5 : 6;
+  // packed-int4 B: each CTA also stages its 128 packed weight rows (8 KB)
+  // per K slab and two unpack warps (after the epilogue warps) expand them
+  static constexpr int STAGES = B_INT4 ? 5 : ((TMA_ST && EPI_BUFS == 2) ? 5 : 6);
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK;   // 16 KB
   static constexpr int B_BYTES = BNH * GEMM_BK;       // 16 KB
-  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int BP_BYTES = B_INT4 ? BNH * GEMM_BK / 2 : 0;  // 8 KB packed
+  static constexpr int UNPACK_WARPS = B_INT4 ? 2 : 0;
+  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS + UNPACK_WARPS);
   static constexpr int STAGE_BYTES = TMA_ST ? EPI_WARPS * EPI_BUFS * EPI_STAGE_BYTES : 0;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 + 16 + sizeof(EpiSmem<BN>);
+      1024 + STAGES * (A_BYTES + B_BYTES + BP_BYTES) + STAGE_BYTES + 256 + 16 + sizeof(EpiSmem<BN>);
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(3 * STAGES * 8 + 4 * 8 + 8 + 8 <= 256, "barrier block");
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
+
+// Nibble unpack of 64 rows of packed int4 (64 bytes of K each) into the
+// 128-byte swizzled int8 layout (16*q per byte), rows 64*part.. of a
+// 128-row slab, by one warp.
+__device__ __forceinline__ void unpack_int4_rows64_warp(const uint8_t* src, uint8_t* dst, int part, int lane) {
+  const int c = lane & 7;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint2 pk[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = 64 * part + (lane >> 3) + 4 * (8 * h + k);
+      pk[k] = *reinterpret_cast<const uint2*>(src + row * 64 + c * 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = 64 * part + (lane >> 3) + 4 * (8 * h + k);
+      const uint32_t l0 = (pk[k].x << 4) & 0xF0F0F0F0u, h0 = pk[k].x & 0xF0F0F0F0u;
+      const uint32_t l1 = (pk[k].y << 4) & 0xF0F0F0F0u, h1 = pk[k].y & 0xF0F0F0F0u;
+      *reinterpret_cast<uint4*>(dst + row * 128 + ((c ^ (row & 7)) << 4)) =
+          make_uint4(__byte_perm(l0, h0, 0x5140), __byte_perm(l0, h0, 0x7362), __byte_perm(l1, h1, 0x5140),
+                     __byte_perm(l1, h1, 0x7362));
+    }
+  }
+}
 
 // tmC: the output as a 16-bit 2-D tensor map with 32 x 32 boxes and the
 // 64-byte swizzle; used when `use_tma_store` (one 16-byte-aligned
 // destination), else the epilogue stores directly.
-template <int EPI, int OUT_DT, bool SPLIT = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>::NUM_THREADS, 1)
+// B_INT4: B is packed int4 [N, K/2]; each CTA TMA-loads its 128 packed rows
+// with its activation rows onto its own `full` barrier, its two unpack warps
+// expand them and arrive on the leader's `conv` barrier (remotely, with
+// CTA-scope release, from the peer), and the MMA waits on `conv`.
+template <int EPI, int OUT_DT, bool SPLIT = false, bool B_INT4 = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT, B_INT4>::NUM_THREADS, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, GemmParams p, int use_tma_store) {
-  using Cfg = PairCfg<EPI, OUT_DT>;
+  using Cfg = PairCfg<EPI, OUT_DT, B_INT4>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int BN = Cfg::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * Cfg::A_BYTES;
-  uint8_t* sC = sB + STAGES * Cfg::B_BYTES;  // [EPI_WARPS][EPI_STAGE_BYTES] (1024-aligned)
+  uint8_t* sBP = sB + STAGES * Cfg::B_BYTES;  // [STAGES][128 rows][64 B] packed (B_INT4)
+  uint8_t* sC = sBP + STAGES * Cfg::BP_BYTES;  // [EPI_WARPS][EPI_STAGE_BYTES] (1024-aligned)
   uint64_t* full = reinterpret_cast<uint64_t*>(sC + Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;     // [2]
   uint64_t* tempty = tfull + 2;         // [2]
   uint64_t* drain = tempty + 2;         // abort path: the MMA issuer's last commit
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* conv = drain + 1;           // [STAGES] B_INT4, leader: both CTAs' halves unpacked
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (B_INT4 ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -1279,6 +1316,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      if constexpr (B_INT4) mbar_init(&conv[s], 2 * Cfg::UNPACK_WARPS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -1325,10 +1363,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           if (!(kb == p.stall_kb && u == cluster_id)) {
-            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
-            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
-            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
+            if constexpr (B_INT4) {  // own barrier: this CTA's unpack warps wait on it
+              mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::BP_BYTES);
+              tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, arow);
+              tma_load_2d(sBP + stage * Cfg::BP_BYTES, &tmB, &full[stage], kb * (GEMM_BK / 2), brow);
+            } else {
+              const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+              if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+              tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
+              tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
+            }
             armed.note(stage, phase);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -1336,8 +1380,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
       }
       // no load still writing shared memory at exit: the peer CTA cannot
       // pass the final cluster barrier before the leader has seen both CTAs'
-      // loads land on its barriers
-      if (leader) armed.drain(full, STAGES);
+      // loads land on its barriers (packed B: each CTA's own barriers)
+      if (leader || B_INT4) armed.drain(full, STAGES);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only) ----------------
@@ -1355,7 +1399,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_bounded(B_INT4 ? &conv[stage] : &full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = umma_desc_k_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
           const uint64_t bdesc = umma_desc_k_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
@@ -1376,12 +1420,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT>
         mbar_wait_drain(drain, 0);
       }
     }
+  } else if (B_INT4 && warp >= 2 + EPI_WARPS) {
+    // ---------------- int4 -> 16*int4 unpack of this CTA's 128 weight rows ----------------
+    // (warp 10 + j: rows 64*j..; the MMA waits on the leader's conv barrier)
+    const int part = warp - (2 + EPI_WARPS);
+    const uint32_t conv_leader0 = mapa_shared(smem_u32(&conv[0]), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int u = cluster_id; ok && u < num_units; u += num_clusters) {
+      const int kb0 = SPLIT ? (u / num_tiles) * p.kb_split : 0;
+      const int kb1 = SPLIT ? min(kb0 + p.kb_split, num_kb) : num_kb;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) { ok = false; break; }
+        unpack_int4_rows64_warp(sBP + stage * Cfg::BP_BYTES, sB + stage * Cfg::B_BYTES, part, lane);
+        fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&conv[stage]);
+          else mbar_arrive_remote(conv_leader0 + stage * (uint32_t)sizeof(uint64_t));
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
   } else {
     // ---------------- epilogue (both CTAs) ----------------
     EpiSmem<BN>* es = reinterpret_cast<EpiSmem<BN>*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
     const bool tma_st = Cfg::TMA_ST && use_tma_store;
     if (tma_st && lane == 0) tma_prefetch_desc(&tmC);
-    epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true, 0, SPLIT>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
+    epilogue_role<BN, EPI, OUT_DT, 2 * GEMM_BM, true, B_INT4 ? 4 : 0, SPLIT>(p, es, tfull, tempty, abort_flag, tmem_base, cluster_id,
                                                       num_clusters, num_tiles, num_m, num_n, (int)rank * GEMM_BM, warp,
                                                       lane, tma_st ? &tmC : nullptr,
                                                       sC + (warp - 2) * Cfg::EPI_BUFS * EPI_STAGE_BYTES);
