@@ -236,15 +236,21 @@ int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
 }
 
 // The strip kernel serves the Sylvester-128 rotation, whose 128-element group
-// is one strip.  Measured at 4096 x 3072 (B200, eight inputs back to back,
-// L2 not holding them): Sylvester 128 14.7 us against 16.8 us on the ring
+// is one strip, and regular 256 (a group across a lane pair) on large
+// problems.  Measured at 4096 x 3072 (B200, eight inputs back to back, L2
+// not holding them): Sylvester 128 14.7 us against 16.8 us on the ring
 // kernel; without rotation 15.8 against 10.6 and regular 256 18.6 against
-// 16.8, so those (and the other sizes) stay on the ring kernel.  (The
-// kernel template also implements the XOR-relabelled reads for the other
-// rotations; the launcher does not instantiate them.)
+// 16.8, so unrotated rows and small regular-256 problems stay on the ring
+// kernel.  (The kernel template also implements the XOR-relabelled reads
+// for the other rotations; the launcher does not instantiate them.)
+// Regular 256 on the strip kernel from 2^25 elements up (measured on B200:
+// 16384 x 3072 53.3 vs 55.3 us, 65536 x 12288 626.7 vs 792.6 us against the
+// ring kernel; 4096 x 3072 22.5 vs 20.5 us, so small problems stay on the ring).
+constexpr int64_t kStripReg256MinElems = (int64_t)1 << 25;
 template <int DT>
 int strip_by_rot(RotCode rc, const RowQuantParams& p, cudaStream_t s) {
   if (rc == RC_SYL128) return launch_strip<DT, ROT_SYLVESTER, 128>(p, s);
+  if (rc == RC_REG256 && (int64_t)p.M * p.K >= kStripReg256MinElems) return launch_strip<DT, ROT_REGULAR, 256>(p, s);
   return QLIN_ERR_UNSUPPORTED;
 }
 

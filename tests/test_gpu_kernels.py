@@ -716,3 +716,19 @@ def test_w8a8_large_problem_does_not_split(P):
     assert _scratch_bytes(4096, 12288, 3072) == 0
     assert _scratch_bytes(8192, 9216, 12288) == 0
     assert _scratch_bytes(1024, 3072, 3072) == 0  # measured slower split (partial traffic)
+
+
+# Regular-256 rotation + int8 on problems of 2^25 elements and more, which the
+# launcher sends to the strip kernel (a group across a lane pair), against
+# the oracle on sampled rows, with zero and non-finite rows.
+@pytest.mark.parametrize("M,K,dt", [(16384, 3072, "bf16"), (2816, 12288, "f16")])
+def test_quant_regular256_large_rows(P, M, K, dt):
+    x = gi.activation(50 + K, M, K, dt, zero_row=7)
+    x[11, 5] = np.inf
+    x[13, 100] = np.nan
+    q, s = P.ops.quant_act_int8(dev(x, dt), ("regular", 256))
+    rows = sorted(set(_rows_sample(M, seed=K).tolist()) | {7, 11, 13, M - 1})
+    qo, so = O.quantize_int8_axiswise(O.rotate(x[rows], 256, "regular", dt), -1)
+    np.testing.assert_array_equal(q.cpu().numpy()[rows], qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1)[rows], np.asarray(so, np.float32).reshape(-1))
+    assert P.ops.device_error() == 0
