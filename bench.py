@@ -995,7 +995,8 @@ def cpu_configs():
     print(json.dumps({"cpu_configs": res}), flush=True)
 
 
-PROFILE_CASES = ("g128_w4a8", "g128_w4a4", "w4a4_row", "quant_syl128_8192x12288", "w8a8_splitk")
+PROFILE_CASES = ("g128_w4a8", "g128_w4a4", "w4a4_row", "quant_syl128_8192x12288", "w8a8_splitk",
+                 "qk_norm_rope_dit", "quant_norm_dit")
 
 
 def profile_case(name):
@@ -1041,6 +1042,20 @@ def profile_case(name):
         xs = rnd((Mv,), 1e-3).abs() + 1e-5
         ws = rnd((Nv,), 1e-3).abs() + 1e-5
         fn = lambda: ops.gemm_w8a8(xq, xs, wq, ws, None, torch.bfloat16)
+    elif name == "qk_norm_rope_dit":
+        # the DiT double block's attention prologue over its 16 samples
+        H, hd, L = DIT["heads"], DIT["head_dim"], DIT["img"] + DIT["txt"]
+        qkv = rnd((16, L, 3 * H * hd)).to(torch.bfloat16)
+        qn, kn = rnd((hd,), 0.1).to(torch.bfloat16) + 1, rnd((hd,), 0.1).to(torch.bfloat16) + 1
+        cos, sin = _rope_tables(L, dev)
+        fn = lambda: ops.qk_norm_rope_(qkv, H, hd, qn, kn, 1e-6, cos, sin)
+    elif name == "quant_norm_dit":
+        # LayerNorm + modulation + regular-256 rotation + int8 over 16 samples of 4608 tokens
+        D, L = DIT["hidden"], DIT["img"] + DIT["txt"]
+        x = rnd((16 * L, D)).to(torch.bfloat16)
+        sc, sh = rnd((16, D), 0.1).to(torch.bfloat16), rnd((16, D), 0.1).to(torch.bfloat16)
+        mul = 1 + sc
+        fn = lambda: ops.quant_act_int8_norm(x, ("regular", 256), "layer", 1e-6, None, mul, sh, L)
     else:
         raise SystemExit(f"unknown profile case {name}")
     for _ in range(3):
