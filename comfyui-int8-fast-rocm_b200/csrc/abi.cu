@@ -1,6 +1,7 @@
 // extern "C" entry points of libqlinear_b200.so: argument validation, error
 // reporting and dispatch to the kernel launchers.  Nothing here throws.
 #include <cstdint>
+#include <cstdlib>
 #include <string>
 
 #include "../../include/qlinear_b200.h"
@@ -54,6 +55,13 @@ int device_sm_count() {
   if (d < 0) return 0;
   if (!g_sms[d]) cudaDeviceGetAttribute(&g_sms[d], cudaDevAttrMultiProcessorCount, d);
   return g_sms[d];
+}
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QLIN_NO_PDL");
+    return !(v != nullptr && v[0] == '1');
+  }();
+  return on;
 }
 int device_cc() {
   const int d = current_device();

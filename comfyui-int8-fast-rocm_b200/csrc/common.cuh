@@ -287,6 +287,13 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+// Programmatic dependent launch (launch_pdl on the host): pdl_wait returns
+// once the previous kernel of the stream has completed and its memory
+// operations are visible (immediately for a plain launch); after
+// pdl_launch_dependents in every CTA, the next kernel of the stream, if
+// launched with PDL, may be scheduled and start its own set-up.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

@@ -77,6 +77,8 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 // group are loaded before any is computed.
 template <int DT, int LPV, int U>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
+  pdl_wait();  // launched with PDL: the qkv rows of the previous kernel are visible
+  pdl_launch_dependents();
   constexpr int HD = 8 * LPV;
   const int sub = threadIdx.x % LPV;
   const int64_t groups_total = (int64_t)gridDim.x * (blockDim.x / LPV);
@@ -173,8 +175,7 @@ int launch_qk(const QkParams& p, cudaStream_t stream) {
   const int64_t cap = (int64_t)device_sm_count() * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  qk_norm_rope_kernel<DT, LPV, U><<<(unsigned)blocks, 256, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(qk_norm_rope_kernel<DT, LPV, U>, dim3((unsigned)blocks), dim3(256), 0, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
   return QLIN_OK;
 }

@@ -97,8 +97,8 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
   }
   const int num_units = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN) * p.splits;
   const int clusters = num_units < p.num_sms / 2 ? num_units : p.num_sms / 2;
-  kern<<<2 * clusters, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, p, use_tma_store);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(2 * clusters), dim3(Cfg::NUM_THREADS), Cfg::SMEM_BYTES, stream, ta, tb, tc, p,
+                 use_tma_store);
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return QLIN_OK;
 }

@@ -1343,6 +1343,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
 
+  // Launched with PDL, everything above overlaps the previous kernel's tail;
+  // no global memory is read or written before pdl_wait.  (An L2 prefetch of
+  // the first tile's weight slabs here measured no gain.)
+  pdl_wait();
+  pdl_launch_dependents();
+
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {

@@ -15,6 +15,31 @@ int cuda_fail(cudaError_t e, const char* what);
 
 // Number of SMs of the current device (cached per device); 0 on failure.
 int device_sm_count();
+
+// Programmatic dependent launch: a kernel launched by launch_pdl may be
+// scheduled while the previous kernel of the stream is still running and
+// does its set-up (barriers, TMEM, descriptor prefetch) meanwhile; every such
+// kernel executes griddepcontrol.wait (pdl_wait) in all threads before its
+// first global-memory access, which returns once the previous kernel has
+// completed and its writes are visible.  QLIN_NO_PDL=1 launches in plain
+// stream order.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 // Major*10+minor of the current device (cached); 0 on failure.
 int device_cc();
 

@@ -169,8 +169,8 @@ int launch_x2(const RowQuantParams& p, int nchunks, cudaStream_t stream) {
   }
   const int64_t groups = (p.M + rpc - 1) / rpc;
   const int64_t cap = (int64_t)device_sm_count() * per_sm;
-  kern<<<dim3((unsigned)(groups < cap ? groups : cap)), dim3(tpr, rpc), smem, stream>>>(p, stages, slot_bytes);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)(groups < cap ? groups : cap)), dim3(tpr, rpc), smem, stream, p,
+                             stages, slot_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "rowquant x2 launch");
   return QLIN_OK;
 }
@@ -228,9 +228,8 @@ int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
   if (per_sm < 1) per_sm = 1;
   const int64_t nblocks = ((int64_t)p.M + rows - 1) / rows;
   const int64_t cap = (int64_t)device_sm_count() * per_sm;
-  kern<<<(unsigned)(nblocks < cap ? nblocks : cap), threads, smem, stream>>>(
-      p.x, p.ldx, p.M, p.K, rows, stages, slot_bytes, p.rot_c, p.one, p.q, p.scale);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3((unsigned)(nblocks < cap ? nblocks : cap)), dim3(threads), smem, stream, p.x, p.ldx, p.M,
+                 p.K, rows, stages, slot_bytes, p.rot_c, p.one, p.q, p.scale);
   if (e != cudaSuccess) return cuda_fail(e, "rowquant strip launch");
   return QLIN_OK;
 }

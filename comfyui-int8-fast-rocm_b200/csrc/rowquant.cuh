@@ -674,6 +674,8 @@ __global__ void __launch_bounds__(512) rowquant_x2_kernel(RowQuantParams p, int 
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();  // before the first global access (launched with PDL)
+  pdl_launch_dependents();
 
   // fill slot s with the rows of iteration `it` (thread 0 only)
   const bool two_src = p.x2 != nullptr;

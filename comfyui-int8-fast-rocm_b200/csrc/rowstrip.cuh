@@ -191,6 +191,8 @@ __global__ void __launch_bounds__(128, 3)
   }
   for (int i = tid; i < 3 * 128; i += blockDim.x) (&s_amax[0][0])[i] = 0u;
   __syncthreads();
+  pdl_wait();  // the previous kernel's rows and codes buffers are settled
+  pdl_launch_dependents();
 
   auto issue = [&](int it, int s) {  // thread 0: row block of iteration `it` into slot s
     const int64_t b = (int64_t)blockIdx.x + (int64_t)it * gridDim.x;
