@@ -1012,7 +1012,7 @@ def cpu_configs():
     print(json.dumps({"cpu_configs": res}), flush=True)
 
 
-PROFILE_CASES = ("g128_w4a8", "g128_w4a4", "w4a4_row", "quant_syl128_8192x12288", "w8a8_splitk",
+PROFILE_CASES = ("g128_w4a8", "g128_w4a4", "w4a4_row", "quant_syl128_8192x12288", "quant_syl128_4096x3072", "w8a8_splitk",
                  "qk_norm_rope_dit", "quant_norm_dit")
 
 
@@ -1049,8 +1049,8 @@ def profile_case(name):
         aq, asc = ops.quant_act_int4(rnd((Mv, Kv)).to(torch.bfloat16), rot, 0)
         b = rnd((Nv,), 0.01).to(torch.bfloat16)
         fn = lambda: ops.gemm_w4a4(aq, asc, pw, ps, b, torch.bfloat16)
-    elif name == "quant_syl128_8192x12288":
-        x = rnd((8192, 12288)).to(torch.bfloat16)
+    elif name in ("quant_syl128_8192x12288", "quant_syl128_4096x3072"):
+        x = rnd((8192, 12288) if name.endswith("12288") else (M, K)).to(torch.bfloat16)
         fn = lambda: ops.quant_act_int8(x, ("sylvester", 128))
     elif name == "w8a8_splitk":
         Mv, Nv, Kv = 768, 1536, 24576

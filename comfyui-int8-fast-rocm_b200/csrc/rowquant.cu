@@ -201,10 +201,10 @@ int x2_by_chunks(RotCode rc, const RowQuantParams& p, int nchunks, cudaStream_t 
 
 // One 128-element strip per thread (rowstrip.cuh): 16-bit activations, K a
 // multiple of 128 up to 16384, rows 16-byte aligned, codes 32-byte aligned.
-template <int DT, int KIND, int G>
+template <int DT, int KIND, int G, int SW = STRIP>
 int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
-  auto kern = rowquant_strip_kernel<DT, KIND, G>;
-  const int T = p.K / STRIP;
+  auto kern = rowquant_strip_kernel<DT, KIND, G, SW>;
+  const int T = p.K / SW;
   int rows = 128 / T;  // whole rows per CTA; prefer whole warps
   for (int r = rows; r >= 1; --r)
     if ((r * T) % 32 == 0) { rows = r; break; }
@@ -246,9 +246,21 @@ int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
 // 16384 x 3072 53.3 vs 55.3 us, 65536 x 12288 626.7 vs 792.6 us against the
 // ring kernel; 4096 x 3072 22.5 vs 20.5 us, so small problems stay on the ring).
 constexpr int64_t kStripReg256MinElems = (int64_t)1 << 25;
+// QLIN_ROWQUANT_NO_HALF_STRIP=1 keeps Sylvester 128 on 128-element strips
+// (comparison runs).
+bool half_strip_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_ROWQUANT_NO_HALF_STRIP");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
 template <int DT>
 int strip_by_rot(RotCode rc, const RowQuantParams& p, cudaStream_t s) {
-  if (rc == RC_SYL128) return launch_strip<DT, ROT_SYLVESTER, 128>(p, s);
+  if (rc == RC_SYL128) {
+    if (p.K / 64 <= 128 && !half_strip_disabled()) return launch_strip<DT, ROT_SYLVESTER, 128, 64>(p, s);
+    return launch_strip<DT, ROT_SYLVESTER, 128>(p, s);
+  }
   if (rc == RC_REG256 && (int64_t)p.M * p.K >= kStripReg256MinElems) return launch_strip<DT, ROT_REGULAR, 256>(p, s);
   return QLIN_ERR_UNSUPPORTED;
 }

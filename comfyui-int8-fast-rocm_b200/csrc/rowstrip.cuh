@@ -70,22 +70,24 @@ __device__ __forceinline__ void st256(void* p, const uint32_t (&r)[8]) {
                : "memory");
 }
 
-// Hadamard digits of the strip held as 64 float pairs (elements 2p, 2p + 1),
-// over the strip-local index bits below log2(G) (G <= 128; G = 64 is also
-// the in-register part of a regular 256 group).
-template <int KIND, int G>
-__device__ __forceinline__ void strip_xform(float2 (&v)[64]) {
+// Hadamard digits of the strip held as NP float pairs (elements 2p, 2p + 1),
+// over the strip-local index bits below log2(G) (G <= 2 NP; G = 64 is also
+// the in-register part of a regular 256 group and of a Sylvester 128 group
+// split over a lane pair).
+template <int KIND, int G, int NP>
+__device__ __forceinline__ void strip_xform(float2 (&v)[NP]) {
   if constexpr (KIND == ROT_SYLVESTER) {
-    static_assert(G == 32 || G == 128, "Sylvester sizes 32 and 128");
+    static_assert(G == 32 || G == 64 || G == 128, "Sylvester sizes 32, 64 (half group) and 128");
+    static_assert(G <= 2 * NP, "the digits lie inside the strip");
 #pragma unroll
-    for (int p = 0; p < 64; ++p) {
+    for (int p = 0; p < NP; ++p) {
       const float a = v[p].x, b = v[p].y;
       v[p] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
     }
 #pragma unroll
     for (int ps = 1; ps < G / 2; ps *= 2)
 #pragma unroll
-      for (int base = 0; base < 64; base += 2 * ps)
+      for (int base = 0; base < NP; base += 2 * ps)
 #pragma unroll
         for (int o = 0; o < ps; ++o) {
           const float2 a0 = v[base + o], a1 = v[base + o + ps];
@@ -95,7 +97,7 @@ __device__ __forceinline__ void strip_xform(float2 (&v)[64]) {
   } else if constexpr (KIND == ROT_REGULAR) {
     static_assert(G == 16 || G == 64, "in-register regular digits cover 16 or 64 elements");
 #pragma unroll
-    for (int q = 0; q < 32; ++q) {
+    for (int q = 0; q < NP / 2; ++q) {
       float a0 = v[2 * q].x, a1 = v[2 * q].y, a2 = v[2 * q + 1].x, a3 = v[2 * q + 1].y;
       h4_regular(a0, a1, a2, a3);
       v[2 * q] = make_float2(a0, a1);
@@ -104,7 +106,7 @@ __device__ __forceinline__ void strip_xform(float2 (&v)[64]) {
 #pragma unroll
     for (int ps = 2; ps < G / 2; ps *= 4)
 #pragma unroll
-      for (int base = 0; base < 64; base += 4 * ps)
+      for (int base = 0; base < NP; base += 4 * ps)
 #pragma unroll
         for (int o = 0; o < ps; ++o) {
           const float2 m2 = make_float2(-2.0f, -2.0f);
@@ -138,13 +140,30 @@ __device__ __forceinline__ void strip_regular256_top(float2 (&v)[64], unsigned l
   }
 }
 
-// x [M, K] (row stride ldx elements), K a multiple of 128 with K / 128 <=
+// Top (seventh) Sylvester stage of a 128 group split over a lane pair: the
+// lane with pair bit b holds group elements 64b + u; y_u = RN(a_u + a_{64+u})
+// on the even lane and y_{64+u} = RN(a_u - a_{64+u}) on the odd one, both as
+// RN(sgn * mine + partner) with sgn = +1 / -1 (the product is exact).
+__device__ __forceinline__ void strip_sylvester128_top(float2 (&v)[32], unsigned lanes, bool odd) {
+  const float2 sg = odd ? make_float2(-1.0f, -1.0f) : make_float2(1.0f, 1.0f);
+#pragma unroll
+  for (int p = 0; p < 32; ++p) {
+    const float2 pv = make_float2(__shfl_xor_sync(lanes, v[p].x, 1), __shfl_xor_sync(lanes, v[p].y, 1));
+    v[p] = f2_fma(v[p], sg, pv);
+  }
+}
+
+// x [M, K] (row stride ldx elements), K a multiple of 128 with K / SW <=
 // 128; q [M, K] int8 (32-byte aligned), scale [M].  rot_c: the dtype-rounded
 // +-entry of the normalised Hadamard; one: 1.0f at run time (the
 // quantiser's add is an FMA by it, which the assembler cannot contract with
 // the preceding multiply).
 //
-// Persistent CTAs of `rows` whole rows (blockDim.x = rows * K / 128)
+// SW: elements per thread, 128, or 64 for Sylvester 128 (a group split over
+// a lane pair: six stages in registers, the seventh by one shuffle per
+// element; half the registers, so about twice the warps per SM).
+//
+// Persistent CTAs of `rows` whole rows (blockDim.x = rows * K / SW)
 // stream row blocks through a ring of `stages` shared-memory slots filled
 // by 1-D bulk copies (one thread issues them; completion counted on an
 // mbarrier per slot), so the next blocks' loads are in flight while a block
@@ -152,8 +171,9 @@ __device__ __forceinline__ void strip_regular256_top(float2 (&v)[64], unsigned l
 // frees the block's slot for its next copy.
 //
 // Bank-conflict-free strip reads: lane l reads 16-byte chunk i ^ d of its
-// strip into register chunk i (d = l & 7; for a regular 256 group the pair's
-// shared d = (l >> 1) & 7), so a warp's 16-byte reads cover all eight bank
+// strip into register chunk i (d = l & 7; for a group split over a lane
+// pair the pair's shared d = (l >> 1) & 7, so the relabelling is one XOR of
+// the group index), so a warp's 16-byte reads cover all eight bank
 // columns.  Relabelling the inputs of a Hadamard transform by an XOR of the
 // index is undone exactly on the outputs:
 //  * Sylvester: H P = S H with S diagonal +-1, so output k keeps its place
@@ -165,18 +185,23 @@ __device__ __forceinline__ void strip_regular256_top(float2 (&v)[64], unsigned l
 //    k ^ delta: outputs are permuted by the same XOR.
 //  * no rotation: a plain permutation.
 // Codes of register chunk i are stored at chunk (i ^ d) -- except
-// Sylvester 128, whose strip is one group: natural order, 256-bit stores.
-template <int DT, int KIND, int G>
-__global__ void __launch_bounds__(128, 3)
+// Sylvester 128, whose outputs keep their place: natural order, 256-bit
+// stores.
+template <int DT, int KIND, int G, int SW = 128>
+__global__ void __launch_bounds__(128, SW == 64 ? 5 : 3)
     rowquant_strip_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int rows, int stages, int slot_bytes,
                           float rot_c, float one, int8_t* __restrict__ q, float* __restrict__ scale) {
   static_assert(DT == DT_BF16 || DT == DT_F16, "16-bit activations");
+  static_assert(SW == 128 || (SW == 64 && KIND == ROT_SYLVESTER && G == 128), "half strips: Sylvester 128");
   constexpr bool PAIR = KIND == ROT_REGULAR && G == 256;  // a group spans two strips
+  constexpr bool HALF = SW == 64;                          // a Sylvester 128 group spans two strips
   constexpr bool NATURAL = KIND == ROT_SYLVESTER && G == 128;  // outputs keep their place
+  constexpr int NC = SW / 8;  // 16-byte chunks per strip
+  constexpr int NP = SW / 2;  // float pairs per strip
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ uint32_t s_amax[3][128];
   __shared__ uint64_t full[4];
-  const int T = K >> 7;  // strips per row
+  const int T = K / SW;  // strips per row
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int r = tid / T;
@@ -211,10 +236,10 @@ __global__ void __launch_bounds__(128, 3)
   if (tid == 0)
     for (int s = 0; s < stages; ++s) issue(s, s);
 
-  const int d = PAIR ? (lane >> 1) & 7 : lane & 7;
+  const int d = (PAIR || HALF) ? (lane >> 1) & 7 : lane & 7;
   // strip-local chunk c (8 elements) lives at column col(c) of the row:
   // contiguous, or (PAIR) two 64-element halves of the group, 128 apart
-  const int c_lo = PAIR ? (j >> 1) * 256 + (j & 1) * 64 : j * STRIP;
+  const int c_lo = PAIR ? (j >> 1) * 256 + (j & 1) * 64 : j * SW;
   const int c_hi = PAIR ? c_lo + 128 : c_lo + 64;
   auto chunk_col = [&](int c) { return c < 8 ? c_lo + 8 * c : c_hi + 8 * (c - 8); };
 
@@ -228,10 +253,10 @@ __global__ void __launch_bounds__(128, 3)
     const bool live = row < M && ok;
     const uint8_t* slot = dsm + (size_t)s * slot_bytes + (size_t)r * row_bytes;
 
-    float2 v[64];
-    uint32_t pk[64];
+    float2 v[NP];
+    uint32_t pk[NP];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < NC; ++i) {
       const int c = i ^ d;  // i and c share bit 3 (the 64-element half)
       uint4 w = make_uint4(0u, 0u, 0u, 0u);
       if (live) w = *reinterpret_cast<const uint4*>(slot + 2 * chunk_col(c));
@@ -239,16 +264,18 @@ __global__ void __launch_bounds__(128, 3)
     }
     if constexpr (KIND != ROT_NONE) {
 #pragma unroll
-      for (int p = 0; p < 64; ++p) v[p] = strip_unpack<DT>(pk[p]);
-      if constexpr (PAIR) {
+      for (int p = 0; p < NP; ++p) v[p] = strip_unpack<DT>(pk[p]);
+      if constexpr (PAIR || HALF) {
         strip_xform<KIND, 64>(v);
         const int in_warp = (int)blockDim.x - (tid & ~31);
-        strip_regular256_top(v, in_warp >= 32 ? 0xffffffffu : (1u << in_warp) - 1u);
+        const unsigned lanes = in_warp >= 32 ? 0xffffffffu : (1u << in_warp) - 1u;
+        if constexpr (PAIR) strip_regular256_top(v, lanes);
+        else strip_sylvester128_top(v, lanes, (lane & 1) != 0);
       } else {
         strip_xform<KIND, G>(v);
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < NC; ++i) {
         float ci = rot_c;
         if constexpr (KIND == ROT_SYLVESTER) {
           constexpr int GC = G / 8;  // chunks per group
@@ -263,7 +290,7 @@ __global__ void __launch_bounds__(128, 3)
     // absmax of the strip on packed pairs, then of the row
     uint32_t m = pk[0];
 #pragma unroll
-    for (int p = 1; p < 64; ++p) m = strip_absmax2<DT>(m, pk[p]);
+    for (int p = 1; p < NP; ++p) m = strip_absmax2<DT>(m, pk[p]);
     float a0, a1;
     if constexpr (DT == DT_BF16) {
       a0 = __uint_as_float((m << 16) & 0x7FFFFFFFu);
@@ -291,7 +318,7 @@ __global__ void __launch_bounds__(128, 3)
       // Inf or NaN in the row: scale Inf / NaN and every code 0 (torch's result)
       if (j == 0) scale[row] = amax;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) *reinterpret_cast<uint2*>(qr + chunk_col(i)) = make_uint2(0u, 0u);
+      for (int i = 0; i < NC; ++i) *reinterpret_cast<uint2*>(qr + chunk_col(i)) = make_uint2(0u, 0u);
       continue;
     }
     const float s_row = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);  // (absmax.float() / 127).clamp(1e-30)
@@ -302,9 +329,9 @@ __global__ void __launch_bounds__(128, 3)
     const float2 inv2 = make_float2(inv, inv);
     const float2 one2 = make_float2(one, one);
     const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    uint32_t cw[32];  // codes of register chunk i: cw[2i], cw[2i + 1]
+    uint32_t cw[NP / 2];  // codes of register chunk i: cw[2i], cw[2i + 1]
 #pragma unroll
-    for (int w = 0; w < 32; ++w) {
+    for (int w = 0; w < NP / 2; ++w) {
       const float2 ya = f2_fma(f2_mul(strip_unpack<DT>(pk[2 * w]), inv2), one2, magic);
       const float2 yb = f2_fma(f2_mul(strip_unpack<DT>(pk[2 * w + 1]), inv2), one2, magic);
       const uint32_t lo = __byte_perm(__float_as_uint(ya.x), __float_as_uint(ya.y), 0x0040);
@@ -313,17 +340,17 @@ __global__ void __launch_bounds__(128, 3)
     }
     if constexpr (NATURAL) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
+      for (int h = 0; h < SW / 32; ++h) {
         const uint32_t o[8] = {cw[8 * h], cw[8 * h + 1], cw[8 * h + 2], cw[8 * h + 3],
                                cw[8 * h + 4], cw[8 * h + 5], cw[8 * h + 6], cw[8 * h + 7]};
-        st256(qr + j * STRIP + 32 * h, o);
+        st256(qr + j * SW + 32 * h, o);
       }
     } else {
       // Sylvester: only XOR bits above the group move outputs; regular and
       // no rotation: the whole XOR
       constexpr int MOVE = KIND == ROT_SYLVESTER ? 7 & ~(G / 8 - 1) : 7;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
+      for (int i = 0; i < NC; ++i)
         *reinterpret_cast<uint2*>(qr + chunk_col(i ^ (d & MOVE))) = make_uint2(cw[2 * i], cw[2 * i + 1]);
     }
   }

@@ -167,6 +167,25 @@ def test_quant_int8_paired_nonfinite_rows(P, rot):
     np.testing.assert_array_equal(s.cpu().numpy(), so)  # NaN matches NaN, Inf matches Inf
 
 
+# Sylvester 128 with 64-element strips (a group over a lane pair; K <= 8192):
+# K = 128 (two threads per row, 64 rows per CTA), 384 and 640 (CTAs whose
+# last warp is partial), 1152, 3072 (the headline row) and 8192 (the largest
+# that takes this form); zero, Inf and NaN rows; row count not a multiple of
+# the rows per CTA.
+@pytest.mark.parametrize("K", [128, 384, 640, 1152, 3072, 8192])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_quant_sylvester128_half_strips(P, K, dt):
+    x = gi.activation(20 + K // 128, 75, K, dt)
+    x[3] = 0.0
+    x[10, K // 3] = np.inf
+    x[17, K - 1] = -np.inf
+    x[40, 5] = np.nan
+    q, s = P.ops.quant_act_int8(dev(x, dt), ("sylvester", 128))
+    qo, so = O.quantize_int8_axiswise(O.rotate(x, 128, "sylvester", dt), -1)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
 def test_rotate_vs_reference_golden(P, golden):
     # the reference's own bf16 matmul rotation: within 1 bf16 ulp
     x = gi.activation(4, 32, 1024, "bf16")
