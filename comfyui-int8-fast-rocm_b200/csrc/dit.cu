@@ -3,6 +3,8 @@
 // position embedding.  HBM bound: every q/k element is read once and
 // written once (v is not touched); the norm weights and the cos/sin tables
 // stay in L2.
+#include <atomic>
+
 #include "../../include/qlinear_b200.h"
 #include "common.cuh"
 #include "internal.h"
@@ -70,50 +72,57 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 }
 
 // LPV lanes per head vector (head_dim = 8 * LPV); each lane owns 8
-// consecutive elements (one 16-byte load and store).  Vector v of the
-// grid-stride walk is head vector v % (2 * heads) of row v / (2 * heads):
-// q heads first, then k heads, i.e. the column offset is (v % 2H) * head_dim,
-// so the lanes of a warp cover 512 contiguous bytes.  U vectors per lane
-// group are loaded before any is computed.
+// consecutive elements (one 16-byte load and store).  The q and k head
+// vectors of all rows form one flat sequence (vector f is head vector
+// f % (2 * heads) of row f / (2 * heads): q heads first, then k heads, so
+// consecutive vectors are consecutive 16 * LPV-byte segments of a row).  A
+// CTA covers V = U * (256 / LPV) consecutive vectors per iteration, one per
+// slot (lane group g, k < U: vector g + k * 256 / LPV of the range), all U
+// loads in flight before any is computed, and the grid strides by
+// gridDim.x * V.  Each slot carries its (row, head vector, token position)
+// from iteration to iteration by adding the stride's quotient and remainder
+// (computed once), so the walk divides nothing per vector.
 template <int DT, int LPV, int U>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
   pdl_wait();  // launched with PDL: the qkv rows of the previous kernel are visible
   pdl_launch_dependents();
   constexpr int HD = 8 * LPV;
+  constexpr int G = 256 / LPV;  // lane groups per CTA
+  constexpr int V = U * G;      // vectors per CTA and iteration
   const int sub = threadIdx.x % LPV;
-  const int64_t groups_total = (int64_t)gridDim.x * (blockDim.x / LPV);
-  const int64_t g0 = (int64_t)blockIdx.x * (blockDim.x / LPV) + threadIdx.x / LPV;
+  const int g = threadIdx.x / LPV;
   const int two_h = 2 * p.heads;
   const int64_t nvec = p.rows * two_h;
-  const bool small = nvec + groups_total * U < ((int64_t)1 << 32);
-  // the loop bound is uniform across the warp (shuffles need every lane)
-  const int64_t warp_first = g0 - (threadIdx.x % 32) / LPV;
-  for (int64_t base = warp_first; base < nvec; base += groups_total * U) {
-    const int64_t my0 = base + (g0 - warp_first);
+  const int64_t stride = (int64_t)gridDim.x * V;
+  const int64_t st_rows = stride / two_h;           // the stride in rows ...
+  const int st_hv = (int)(stride - st_rows * two_h);  // ... and head vectors
+  const int64_t st_pos = st_rows % p.positions;
+  int64_t row[U], pos[U];
+  int hv[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int64_t f = (int64_t)blockIdx.x * V + g + k * G;
+    row[k] = f / two_h;
+    hv[k] = (int)(f - row[k] * two_h);
+    pos[k] = row[k] % p.positions;
+  }
+  // the loop bound is uniform across the CTA (shuffles need every lane)
+  for (int64_t f0 = (int64_t)blockIdx.x * V; f0 < nvec; f0 += stride) {
     uint4 raw[U];
-    int64_t off[U], rows_u[U];
-    int hvs[U];
+    int64_t off[U];
     bool ok[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t v = my0 + (int64_t)u * groups_total;
-      ok[u] = v < nvec;
-      // 32-bit division when the vector index fits (a 64-bit one is a long
-      // emulated sequence)
-      const int64_t row = !ok[u] ? 0 : (small ? (int64_t)((uint32_t)v / (uint32_t)two_h) : v / two_h);
-      const int hv = ok[u] ? (int)(v - row * two_h) : 0;
-      rows_u[u] = row;
-      hvs[u] = hv;
-      off[u] = row * p.ld + (int64_t)hv * HD + sub * 8;
-      raw[u] = ok[u] ? __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.qkv) + off[u]))
+    for (int k = 0; k < U; ++k) {
+      ok[k] = row[k] < p.rows;
+      off[k] = row[k] * p.ld + (int64_t)hv[k] * HD + sub * 8;
+      raw[k] = ok[k] ? __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.qkv) + off[k]))
                      : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t row = rows_u[u];
-      const bool is_k = ok[u] && hvs[u] >= p.heads;
+    for (int k = 0; k < U; ++k) {
+      const bool is_k = hv[k] >= p.heads;
       float x[8];
-      unpack8<DT>(raw[u], x);
+      unpack8<DT>(raw[k], x);
       float ss = 0.0f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = __fmaf_rn(x[i], x[i], ss);
@@ -138,10 +147,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
         if (wp != nullptr) t = f2_mul(t, make_float2(w[2 * j], w[2 * j + 1]));
         n2[j] = round2<DT>(t);
       }
-      if (p.cos_t != nullptr) {
-        const int64_t pos = row % p.positions;
-        const float4 c4 = *reinterpret_cast<const float4*>(p.cos_t + pos * (HD / 2) + sub * 4);
-        const float4 s4 = *reinterpret_cast<const float4*>(p.sin_t + pos * (HD / 2) + sub * 4);
+      if (p.cos_t != nullptr && ok[k]) {
+        const float4 c4 = *reinterpret_cast<const float4*>(p.cos_t + pos[k] * (HD / 2) + sub * 4);
+        const float4 s4 = *reinterpret_cast<const float4*>(p.sin_t + pos[k] * (HD / 2) + sub * 4);
         const float c[4] = {c4.x, c4.y, c4.z, c4.w};
         const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -161,21 +169,43 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
         n[2 * j] = n2[j].x;
         n[2 * j + 1] = n2[j].y;
       }
-      if (ok[u]) __stcs(reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.qkv) + off[u]), pack8<DT>(n));
+      if (ok[k]) __stcs(reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.qkv) + off[k]), pack8<DT>(n));
+    }
+    // next vector of each slot: stride = st_rows rows + st_hv head vectors
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      hv[k] += st_hv;
+      int64_t dr = st_rows, dp = st_pos;
+      if (hv[k] >= two_h) {
+        hv[k] -= two_h;
+        dr += 1;
+        dp += 1;
+      }
+      row[k] += dr;
+      pos[k] += dp;
+      while (pos[k] >= p.positions) pos[k] -= p.positions;  // dp <= positions: at most twice
     }
   }
 }
 
 template <int DT, int LPV>
 int launch_qk(const QkParams& p, cudaStream_t stream) {
-  constexpr int U = 2;
-  const int64_t groups = p.rows * 2 * p.heads;
-  const int64_t per_block = 256 / LPV;
-  int64_t blocks = (groups + per_block * U - 1) / (per_block * U);
-  const int64_t cap = (int64_t)device_sm_count() * 8;
+  constexpr int U = 4;
+  const int64_t vecs = p.rows * 2 * p.heads;
+  const int64_t per_block = (256 / LPV) * U;
+  int64_t blocks = (vecs + per_block - 1) / per_block;
+  auto kern = qk_norm_rope_kernel<DT, LPV, U>;
+  static std::atomic<int> per_sm{0};  // resident CTAs per SM (one device model per process)
+  if (per_sm.load() == 0) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+    per_sm.store(nb > 0 ? nb : 1);
+  }
+  const int64_t cap = (int64_t)device_sm_count() * per_sm.load();  // one wave of resident CTAs
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  cudaError_t e = launch_pdl(qk_norm_rope_kernel<DT, LPV, U>, dim3((unsigned)blocks), dim3(256), 0, stream, p);
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)blocks), dim3(256), 0, stream, p);
   if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
   return QLIN_OK;
 }
