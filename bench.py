@@ -298,24 +298,44 @@ def dit_forward_fused(params, img, txt, vec, fl, qk):
     into its kernels: ``fl(x, layer, **fusion)`` runs LayerNorm + modulation
     in the activation quantiser (and reads a concatenated input from its two
     parts) and GELU / gated residual in the GEMM epilogue; ``qk`` is the
-    in-place q/k RMSNorm + rotary kernel.  Same arithmetic as ``dit_forward``
-    up to the float32 order of the norm statistics."""
+    in-place q/k RMSNorm + rotary kernel; a double block's streams meet in
+    the joint sequence through segmented GEMM rows (``fl.segments``) instead
+    of torch.cat and slices.  Same arithmetic as ``dit_forward`` up to the
+    float32 order of the norm statistics."""
     D = DIT["hidden"]
     dbl, sgl = params
     Lt = txt.shape[1]
     cos, sin = _rope_tables(Lt + img.shape[1], img.device)
     svec = torch.nn.functional.silu(vec)
+    seg = fl.segments
 
     def pre(shift, scale):
         return dict(norm="layer", mod_mul=1 + scale, mod_add=shift)
 
+    B, Li = img.shape[0], img.shape[1]
+    L = Lt + Li
+    # segmented rows need 128-row segments and >= 256 rows and columns
+    joint = Lt % 128 == 0 and Li % 128 == 0 and B * Lt >= 256 and D >= 256
     for blk in dbl:
         mi = fl(svec, blk["img_mod"]).chunk(6, dim=-1)
         mt = fl(svec, blk["txt_mod"]).chunk(6, dim=-1)
-        qkv = torch.cat((fl(txt, blk["txt_qkv"], **pre(mt[0], mt[1])), fl(img, blk["img_qkv"], **pre(mi[0], mi[1]))), 1)
-        o = _attention_fused(qkv, blk, cos, sin, qk)
-        txt = fl(o[:, :Lt], blk["txt_proj"], residual=txt, gate=mt[2])
-        img = fl(o[:, Lt:], blk["img_proj"], residual=img, gate=mi[2])
+        if joint:
+            # both streams write their q/k/v rows into the joint [text | image]
+            # sequence of each sample, and read their projections' rows from
+            # the joint attention output (segmented GEMM rows: no cat, no slices)
+            qkv = torch.empty((B, L, blk["txt_qkv"].n), dtype=img.dtype, device=img.device)
+            fl(txt, blk["txt_qkv"], out=qkv, out_rows=(Lt, L, 0), **pre(mt[0], mt[1]))
+            fl(img, blk["img_qkv"], out=qkv, out_rows=(Li, L, Lt), **pre(mi[0], mi[1]))
+            o = _attention_fused(qkv, blk, cos, sin, qk)
+            oq, os_ = seg(o)
+            txt = seg(oq, os_, blk["txt_proj"], (Lt, L, 0), residual=txt, gate=mt[2])
+            img = seg(oq, os_, blk["img_proj"], (Li, L, Lt), residual=img, gate=mi[2])
+        else:
+            qkv = torch.cat((fl(txt, blk["txt_qkv"], **pre(mt[0], mt[1])),
+                             fl(img, blk["img_qkv"], **pre(mi[0], mi[1]))), 1)
+            o = _attention_fused(qkv, blk, cos, sin, qk)
+            txt = fl(o[:, :Lt], blk["txt_proj"], residual=txt, gate=mt[2])
+            img = fl(o[:, Lt:], blk["img_proj"], residual=img, gate=mi[2])
         img = fl(fl(img, blk["img_mlp0"], gelu_from=0, **pre(mi[3], mi[4])), blk["img_mlp1"], residual=img, gate=mi[5])
         txt = fl(fl(txt, blk["txt_mlp0"], gelu_from=0, **pre(mt[3], mt[4])), blk["txt_mlp1"], residual=txt, gate=mt[5])
     x = torch.cat((txt, img), 1)
@@ -359,15 +379,29 @@ def dit_linears(pkg, rot):
                                              rot)
         return y.reshape(*shp[:-1], layer.n)
 
-    def fl(x, layer, residual=None, gate=None, x2=None, **kw):
+    def fl(x, layer, residual=None, gate=None, x2=None, out=None, out_rows=None, **kw):
         shp = x.shape
         rows = x.numel() // shp[-1] // shp[0]  # tokens per sample
         y = pub.int8_forward_fused(x.reshape(-1, shp[-1]), layer.wq, layer.ws, layer.b, torch.bfloat16, rot,
                                    rows_per_sample=rows, rows_per_gate=rows, gate=gate,
                                    residual=None if residual is None else residual.reshape(-1, layer.n),
-                                   x2=None if x2 is None else x2.reshape(-1, x2.shape[-1]), **kw)
-        return y.reshape(*shp[:-1], layer.n)
+                                   x2=None if x2 is None else x2.reshape(-1, x2.shape[-1]),
+                                   out=None if out is None else out.view(-1, layer.n), out_rows=out_rows, **kw)
+        return out if out is not None else y.reshape(*shp[:-1], layer.n)
 
+    def segments(x, xs=None, layer=None, a_rows=None, residual=None, gate=None):
+        """The two projections of a double block on one joint input:
+        ``segments(o)`` quantises the joint [batch, tokens, K] rows once;
+        ``segments(q, s, layer, (n, stride, off), residual, gate)`` runs the
+        linear on the n rows at ``off`` of every ``stride`` rows (the fused
+        gated residual per sample)."""
+        if layer is None:
+            return pkg.ops.quant_act_int8(x.reshape(-1, x.shape[-1]), rot)
+        y = pkg.ops.gemm_w8a8_fused(x, xs, layer.wq, layer.ws, layer.b, torch.bfloat16, a_rows=a_rows,
+                                    residual=residual.reshape(-1, layer.n), gate=gate, rows_per_gate=a_rows[0])
+        return y.reshape(residual.shape)
+
+    fl.segments = segments
     return lin, fl
 
 

@@ -49,6 +49,8 @@ SIGNATURES = {
     "qlin_gemm_w8a8_splitk": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _P, _U64, _P],
     "qlin_gemm_w8a8_splitk_noalloc": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _P],
     "qlin_gemm_w8a8_fused": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _L, _P, _L, _P, _L, _L, _P],
+    "qlin_gemm_w8a8_fused_segments": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _L, _L, _P, _L, _P, _L, _L,
+                                      _L, _L, _L, _L, _L, _L, _P],
     "qlin_gemm_w8a8_allgather": [_P, _P, _P, _P, _I, _P, _P, _I, _L, _L, _I, _L, _L, _L, _P],
     "qlin_int_mm": [_P, _P, _P, _L, _L, _L, _P],
     "qlin_int4_mm": [_P, _P, _P, _L, _L, _L, _P],

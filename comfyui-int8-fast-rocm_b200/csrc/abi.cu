@@ -412,6 +412,42 @@ QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const i
                         w_scale, bias, o, out_dtype, M, N, K, static_cast<cudaStream_t>(stream), &e);
 }
 
+QLIN_API int qlin_gemm_w8a8_fused_segments(const int8_t* a, const float* a_scale, const int8_t* w,
+                                           const float* w_scale, int wscale_mode, const void* bias, void* out,
+                                           int out_dtype, int64_t M, int64_t N, int64_t K, int64_t gelu_col0,
+                                           const void* residual, int64_t ld_res, const void* gate, int64_t gate_ld,
+                                           int64_t rows_per_gate, int64_t a_seg_rows, int64_t a_seg_stride,
+                                           int64_t a_seg_off, int64_t out_seg_rows, int64_t out_seg_stride,
+                                           int64_t out_seg_off, void* stream) {
+  QLIN_RANGE();
+  int rc = gemm_common_checks(a, w, M, N, K, 16);
+  if (rc || M == 0 || N == 0) return rc;
+  if (out_dtype != QLIN_BF16 && out_dtype != QLIN_F16)
+    return fail(QLIN_ERR_INVALID_ARG, "out_dtype must be BF16 or F16 for segmented rows");
+  if (!a_scale || !w_scale || !out) return fail(QLIN_ERR_INVALID_ARG, "null pointer");
+  if (wscale_mode != QLIN_WSCALE_ROW && wscale_mode != QLIN_WSCALE_TENSOR)
+    return fail(QLIN_ERR_INVALID_ARG, "bad wscale_mode");
+  if (gelu_col0 < 0) return fail(QLIN_ERR_INVALID_ARG, "gelu_col0 < 0");
+  if (gate && !residual) return fail(QLIN_ERR_INVALID_ARG, "a gate needs a residual");
+  if (residual && ld_res < N) return fail(QLIN_ERR_INVALID_ARG, "ld_res < N");
+  if (gate && gate_ld < N) return fail(QLIN_ERR_INVALID_ARG, "gate_ld < N");
+  if ((residual && (!aligned16(residual) || (ld_res * 2) % 16)) || (gate && (!aligned16(gate) || (gate_ld * 2) % 16)))
+    return fail(QLIN_ERR_ALIGNMENT, "residual and gate rows must be 16-byte aligned");
+  if (N % 8 || !aligned16(out)) return fail(QLIN_ERR_ALIGNMENT, "segmented output rows need N % 8 == 0, aligned out");
+  OutSpec o;
+  for (int i = 0; i < 8; ++i) o.outs[i] = nullptr;
+  o.outs[0] = out;
+  o.nout = 1;
+  o.col_off = 0;
+  o.ldo = N;
+  GemmSegments sg{a_seg_rows, a_seg_stride, a_seg_off, out_seg_rows, out_seg_stride, out_seg_off};
+  const bool post = gelu_col0 < N || residual != nullptr;
+  EpiPost e{gelu_col0 < N ? gelu_col0 : INT64_MAX, residual, ld_res, gate, gate_ld, rows_per_gate};
+  return launch_gemm_to(wscale_mode == QLIN_WSCALE_ROW ? GEMM_W8A8_ROW : GEMM_W8A8_TENSOR, false, a, w, a_scale,
+                        w_scale, bias, o, out_dtype, M, N, K, static_cast<cudaStream_t>(stream), post ? &e : nullptr,
+                        &sg);
+}
+
 QLIN_API int qlin_gemm_w8a8_allgather(const int8_t* a, const float* a_scale, const int8_t* w_shard,
                                       const float* w_scale_shard, int wscale_mode, const void* bias_shard,
                                       void* const* out_bufs, int n_out, int64_t col_off, int64_t ldo, int out_dtype,

@@ -218,6 +218,12 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// 3-D form of tma_store_2d.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the shared-memory sources of this thread's committed bulk stores may be reused
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -319,6 +325,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, ui
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(mbar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+// 3-D form of tma_load_2d_pair (segmented rows: {column, row in segment,
+// segment}).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, uint32_t mbar_cluster_addr, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(mbar_cluster_addr), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {

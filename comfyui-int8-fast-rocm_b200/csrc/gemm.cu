@@ -49,6 +49,25 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
   return QLIN_OK;
 }
 
+// 3-D tensor map of segmented rows: `nseg` segments of `seg_rows` rows of
+// `inner` elements; rows `pitch` bytes apart within a segment, segments
+// `seg_pitch` bytes apart; boxes of box_inner x box_rows x 1.
+int make_tmap3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t seg_rows, uint64_t nseg, uint64_t pitch,
+               uint64_t seg_pitch, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz,
+               CUtensorMapDataType dtype) {
+  PFN_encodeTiled_t enc = get_encode_fn();
+  if (!enc) return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {inner, seg_rows, nseg};
+  cuuint64_t strides[2] = {pitch, seg_pitch};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(QLIN_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string((int)r) + ")");
+  return QLIN_OK;
+}
+
 template <int BN, int EPI, int OUT_DT, bool B_INT4>
 int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, B_INT4>;
@@ -80,11 +99,21 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
   int use_tma_store = 0;
   if (Cfg::TMA_ST && p.nout == 1 && (p.ldo * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
       (p.col_off * 2) % 16 == 0) {
-    const int rc = make_tmap(&tc, p.out, (uint64_t)(p.col_off + p.N), (uint64_t)p.M, (uint64_t)p.ldo * 2, 32, 32,
-                             CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    int rc;
+    if (p.o_seg == 0) {
+      rc = make_tmap(&tc, p.out, (uint64_t)(p.col_off + p.N), (uint64_t)p.M, (uint64_t)p.ldo * 2, 32, 32,
+                     CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    } else {
+      rc = make_tmap3(&tc, static_cast<const uint16_t*>(p.out) + p.o_seg_off * p.ldo, (uint64_t)(p.col_off + p.N),
+                      (uint64_t)p.o_seg, (uint64_t)(p.M / p.o_seg), (uint64_t)p.ldo * 2,
+                      (uint64_t)p.o_seg_stride * p.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    }
     if (rc) return rc;
     use_tma_store = 1;
   }
+  if (p.o_seg != 0 && !use_tma_store)
+    return fail(QLIN_ERR_UNSUPPORTED, "segmented output rows need a 16-bit, 16-byte aligned single destination");
   static std::atomic<uint64_t> attr_devices{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -236,23 +265,53 @@ int launch_gemm(int kind, bool b_int4, const int8_t* a, const int8_t* b, const f
 
 int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
                    const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
-                   int64_t K, cudaStream_t stream, const EpiPost* post) {
+                   int64_t K, cudaStream_t stream, const EpiPost* post, const GemmSegments* seg) {
   if (M == 0 || N == 0) return QLIN_OK;
   if (o.nout < 1 || o.nout > kMaxOutputs) return fail(QLIN_ERR_INVALID_ARG, "between 1 and 8 outputs");
   if (post != nullptr && o.nout != 1) return fail(QLIN_ERR_UNSUPPORTED, "epilogue steps need one destination");
   const int sms = device_sm_count();
   if (sms <= 0) return fail(QLIN_ERR_NO_DEVICE, "no CUDA device");
+  const bool segmented = seg != nullptr && (seg->a_rows != 0 || seg->o_rows != 0);
+  if (segmented) {
+    if (b_int4 || (kind != GEMM_W8A8_ROW && kind != GEMM_W8A8_TENSOR) || o.nout != 1 ||
+        (out_dt != DT_BF16 && out_dt != DT_F16) || M < 256 || N < 256 || sms < 2 || pair_disabled())
+      return fail(QLIN_ERR_UNSUPPORTED, "segmented rows: W8A8 on CTA pairs with a 16-bit output, M and N >= 256");
+    if (seg->a_rows < 0 || seg->o_rows < 0 || seg->a_rows % 128 != 0 || seg->o_rows % 32 != 0 ||
+        (seg->a_rows && (M % seg->a_rows != 0 || seg->a_stride < seg->a_rows || seg->a_off < 0 ||
+                         seg->a_off + seg->a_rows > seg->a_stride)) ||
+        (seg->o_rows && (M % seg->o_rows != 0 || seg->o_stride < seg->o_rows || seg->o_off < 0 ||
+                         seg->o_off + seg->o_rows > seg->o_stride)) ||
+        seg->a_rows > INT32_MAX || seg->o_rows > INT32_MAX)
+      return fail(QLIN_ERR_INVALID_ARG,
+                  "segments: rows a multiple of 128 (A) / 32 (output) dividing M, inside a stride >= offset + rows");
+  }
   CUtensorMap ta, tb;
   // Large int8 x int8 problems run on CTA pairs (256 x 256 tiles).
   if (!b_int4 && kind != GEMM_W4A4_ROW && M >= 256 && N >= 256 && sms >= 2 && !pair_disabled()) {
-    int rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    int rc;
+    if (segmented && seg->a_rows) {
+      rc = make_tmap3(&ta, a + seg->a_off * K, (uint64_t)K, (uint64_t)seg->a_rows, (uint64_t)(M / seg->a_rows),
+                      (uint64_t)K, (uint64_t)(seg->a_stride * K), GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    } else {
+      rc = make_tmap(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     if (rc) return rc;
     rc = make_tmap(&tb, b, (uint64_t)K, (uint64_t)N, (uint64_t)K, GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     GemmParams p = make_params(M, N, K, a_scale, w_scale, bias, o, sms);
     if (post != nullptr) set_post(p, *post);
+    if (segmented) {
+      p.a_seg = (int)seg->a_rows;
+      p.a_seg_stride = seg->a_stride;
+      p.a_seg_off = seg->a_off;
+      p.o_seg = (int)seg->o_rows;
+      p.o_seg_stride = seg->o_stride;
+      p.o_seg_off = seg->o_off;
+    }
     return dispatch_pair(kind, out_dt, ta, tb, p, stream, post != nullptr);
   }
+  if (segmented) return fail(QLIN_ERR_UNSUPPORTED, "segmented rows need the CTA-pair kernel");
   // Packed-int4 weights on CTA pairs (each CTA unpacks its own 128 rows).
   if (b_int4 && (kind == GEMM_W4A4_ROW || kind == GEMM_I32) && post == nullptr && o.nout == 1 && M >= 256 &&
       N >= 256 && sms >= 2 && !pair_disabled() && !int4_pair_disabled()) {

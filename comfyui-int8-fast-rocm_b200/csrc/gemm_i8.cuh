@@ -132,7 +132,38 @@ struct GemmParams {
   uint32_t* sk_count;  // [tiles][2] arrivals per tile half: zero on entry, left zero
   uint32_t* sk_ready;  // [splits - 1][tiles][2] partial slot written: zero on entry, left zero
   int32_t* sk_part;    // [splits - 1][tiles][2][128 rows][256 columns] int32 partials
+  // Segmented rows (CTA-pair kernel, TMA stores; 0: off).  Logical row r of
+  // A and of a_scale lies at row (r / a_seg) * a_seg_stride + a_seg_off of
+  // the A / a_scale arrays (the A tensor map is then 3-D {K, a_seg,
+  // M / a_seg} and encodes the stride and offset itself); logical output
+  // row r at row r % o_seg of segment r / o_seg of the 3-D output tensor map
+  // (which encodes that segment's place).  a_seg is a multiple of 128 and
+  // o_seg of 32, so no TMA box straddles two segments; M is a multiple of
+  // both.  Residual and gate rows stay logical.
+  int a_seg;
+  int64_t a_seg_stride, a_seg_off;
+  int o_seg;
+  int64_t o_seg_stride, o_seg_off;  // host side: the output tensor map's layout
 };
+
+// Memory row of logical A row r (segmented A, see GemmParams).
+__device__ __forceinline__ int64_t a_mem_row(const GemmParams& p, int r) {
+  if (p.a_seg == 0) return r;
+  const int sg = r / p.a_seg;
+  return (int64_t)sg * p.a_seg_stride + p.a_seg_off + (r - sg * p.a_seg);
+}
+
+// One 32 x 32 staged output box of logical rows row..row+31 to the output
+// tensor map (2-D, or 3-D for segmented output rows).
+__device__ __forceinline__ void store_out_box(const GemmParams& p, const CUtensorMap* tmC, const void* src, int x,
+                                              int row) {
+  if (p.o_seg == 0) {
+    tma_store_2d(tmC, src, x, row);
+  } else {
+    const int sg = row / p.o_seg;
+    tma_store_3d(tmC, src, x, row - sg * p.o_seg, sg);
+  }
+}
 
 // Scratch layout of a split-K launch: a fixed header of counters and flags
 // (the same place for every problem size, so one scratch buffer serves
@@ -474,7 +505,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem
             fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(tmC, stage, (int)(p.col_off + col0), row0 + quarter * 32);
+              store_out_box(p, tmC, stage, (int)(p.col_off + col0), row0 + quarter * 32);
               bulk_commit_group();
             }
             continue;
@@ -684,7 +715,7 @@ __device__ __forceinline__ void epi_chunk_tma(const GemmParams& p, const uint32_
   fence_proxy_async_smem();  // generic-proxy writes -> TMA reads
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(tmC, sb, (int)(p.col_off + col0), row_base);
+    store_out_box(p, tmC, sb, (int)(p.col_off + col0), row_base);
     bulk_commit_group();
   }
 }
@@ -992,7 +1023,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
     prefetch_res(mb, nb_);
     epi_load_params<BN, EPI, OUT_DT>(p, nb_ * BN, e, nws, nb);
     const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
-    if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+    if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + a_mem_row(p, row)) : 0.0f;
     load_gate(mb, nb_, ngate, ngok);
     if (e < BN) { es->ws[0][e] = nws; es->bias[0][e] = nb; es->gate[0][e] = ngate; }
     if (e == 0) es->gate_ok[0] = ngok;
@@ -1016,7 +1047,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       tile_coords(next, num_m, num_n, mb2, nb2);
       epi_load_params<BN, EPI, OUT_DT>(p, nb2 * BN, e, nws, nb);
       const int row = mb2 * ROWS_PER_TILE + row_off + quarter * 32 + lane;
-      if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+      if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + a_mem_row(p, row)) : 0.0f;
       load_gate(mb2, nb2, ngate, ngok);
       prefetch_res(mb2, nb2);
       nrow = row;
@@ -1376,7 +1407,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
             } else {
               const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
               if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
-              tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
+              if (p.a_seg == 0) tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow);
+              else tma_load_3d_pair(sA + stage * Cfg::A_BYTES, &tmA, fb, kb * GEMM_BK, arow % p.a_seg, arow / p.a_seg);
               tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, fb, kb * GEMM_BK, brow);
             }
             armed.note(stage, phase);

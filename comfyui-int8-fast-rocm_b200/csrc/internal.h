@@ -114,9 +114,21 @@ struct EpiPost {
   int64_t gate_ld;
   int64_t rows_per_gate;
 };
+// Segmented rows of a W8A8 GEMM (CTA-pair kernel, 16-bit output through
+// TMA stores, one destination): logical row r of A and a_scale is row
+// (r / a_rows) * a_stride + a_off of those arrays, logical output row r is
+// row (r / o_rows) * o_stride + o_off of the output ([.., ldo]); a_rows /
+// o_rows 0: contiguous.  a_rows a multiple of 128, o_rows of 32, M a
+// multiple of each.  Lets the two streams of a DiT double block write their
+// qkv rows straight into the joint sequence, and read their projections'
+// rows from the joint attention output, instead of copying.
+struct GemmSegments {
+  int64_t a_rows, a_stride, a_off;
+  int64_t o_rows, o_stride, o_off;
+};
 int launch_gemm_to(int kind, bool b_int4, const int8_t* a, const int8_t* b, const float* a_scale,
                    const float* w_scale, const void* bias, const OutSpec& o, int out_dt, int64_t M, int64_t N,
-                   int64_t K, cudaStream_t stream, const EpiPost* post = nullptr);
+                   int64_t K, cudaStream_t stream, const EpiPost* post = nullptr, const GemmSegments* seg = nullptr);
 
 // Split-K W8A8 GEMM on CTA pairs (GemmParams::splits): the scratch size a
 // problem needs (0: it runs unsplit), and the launch, which falls back to

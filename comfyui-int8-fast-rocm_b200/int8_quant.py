@@ -101,7 +101,7 @@ def int8_forward_dynamic_per_row(x: Tensor, weight: Tensor, weight_scale: Tensor
 def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dtype, rot=None, per_row=True, *,
                        norm=None, eps: float = 1e-6, norm_weight=None, mod_mul=None, mod_add=None,
                        rows_per_sample=None, gelu_from=None, residual=None, gate=None,
-                       rows_per_gate=None, x2=None) -> Tensor:
+                       rows_per_gate=None, x2=None, out=None, out_rows=None) -> Tensor:
     """:func:`int8_forward_dynamic_per_row` / :func:`int8_forward_dynamic`
     with the element-wise neighbours of a DiT block's linear fused into its
     two kernels (no counterpart in the reference, which runs them as eager
@@ -115,7 +115,11 @@ def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dt
     * epilogue (GEMM): ``dt(gelu_tanh(y))`` on columns ``>= gelu_from``, then
       ``dt(residual + dt(gate[g] * y))`` with ``g = row // rows_per_gate``;
     * ``x2``: the linear's input is ``torch.cat((x, x2), -1)``, read from the
-      two tensors by the quantiser (no prologue steps then).
+      two tensors by the quantiser (no prologue steps then);
+    * ``out_rows=(n, stride, off)``: output row r lands in row
+      ``(r // n) * stride + off + r % n`` of ``out`` (see
+      ``ops.gemm_w8a8_fused``), e.g. one stream's q/k/v rows written straight
+      into the joint sequence of a double block.
     """
     prologue = norm is not None or mod_mul is not None or mod_add is not None
     if x2 is not None:
@@ -128,10 +132,11 @@ def int8_forward_fused(x: Tensor, weight: Tensor, weight_scale, bias, compute_dt
         xq, xs = kops.quant_act_int8(x, rot)
     if not per_row and not isinstance(weight_scale, torch.Tensor):
         weight_scale = torch.tensor([float(weight_scale)], dtype=torch.float32, device=x.device)
-    if gelu_from is None and residual is None:
+    if gelu_from is None and residual is None and out is None:
         return kops.gemm_w8a8(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row)
     return kops.gemm_w8a8_fused(xq, xs, weight, weight_scale, bias, compute_dtype, per_row=per_row,
-                               gelu_from=gelu_from, residual=residual, gate=gate, rows_per_gate=rows_per_gate)
+                               gelu_from=gelu_from, residual=residual, gate=gate, rows_per_gate=rows_per_gate,
+                               out=out, out_rows=out_rows)
 
 
 def lowvram_patch_int8(weight: Tensor, scale, convrot_groupsize, delta_fn, stochastic=False, seed=0) -> Tensor:

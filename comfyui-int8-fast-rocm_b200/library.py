@@ -173,6 +173,17 @@ def _(a_q, a_scale, w_q, w_scale, bias, out_dtype, per_row, gelu_from, residual,
     return a_q.new_empty((_rows_of(a_q), w_q.shape[0]), dtype=out_dtype)
 
 
+@_op("gemm_w8a8_fused_into", mutates_args=("out",))
+def _gemm_w8a8_fused_into(a_q: Tensor, a_scale: Tensor, w_q: Tensor, w_scale: Tensor, bias: Optional[Tensor],
+                          out: Tensor, per_row: bool, gelu_from: int, residual: Optional[Tensor],
+                          gate: Optional[Tensor], rows_per_gate: int, seg_rows: int, seg_stride: int,
+                          seg_off: int) -> None:
+    ops.gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias, out.dtype, per_row,
+                        None if gelu_from < 0 else gelu_from, residual, gate,
+                        None if rows_per_gate < 0 else rows_per_gate, out=out,
+                        out_rows=None if seg_rows <= 0 else (seg_rows, seg_stride, seg_off))
+
+
 @_op("int_mm")
 def _int_mm(a_q: Tensor, w_q: Tensor) -> Tensor:
     return ops.int_mm(a_q, w_q)
@@ -345,10 +356,20 @@ def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, p
 
 
 def gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, per_row=True, gelu_from=None,
-                    residual=None, gate=None, rows_per_gate=None):
-    return _L.gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias, out_dtype, bool(per_row),
-                              -1 if gelu_from is None else int(gelu_from), residual, gate,
-                              -1 if rows_per_gate is None else int(rows_per_gate))
+                    residual=None, gate=None, rows_per_gate=None, out=None, out_rows=None):
+    if out is None:
+        if out_rows is not None:
+            raise ValueError("out_rows needs out")
+        return _L.gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias, out_dtype, bool(per_row),
+                                  -1 if gelu_from is None else int(gelu_from), residual, gate,
+                                  -1 if rows_per_gate is None else int(rows_per_gate))
+    if out.dtype != out_dtype:
+        raise ValueError(f"out is {out.dtype}, the GEMM writes {out_dtype}")
+    n, stride, off = (0, 0, 0) if out_rows is None else (int(v) for v in out_rows)
+    _L.gemm_w8a8_fused_into(a_q, a_scale, w_q, w_scale, bias, out, bool(per_row),
+                            -1 if gelu_from is None else int(gelu_from), residual, gate,
+                            -1 if rows_per_gate is None else int(rows_per_gate), n, stride, off)
+    return out
 
 
 def int_mm(a_q, w_q):

@@ -385,23 +385,61 @@ def gemm_w8a8(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, p
     return out
 
 
+def _segments(rows, total, what):
+    n, stride, off = (int(v) for v in rows)
+    if n <= 0 or stride < n or off < 0 or off + n > stride:
+        raise ValueError(f"{what}: segments of {n} rows at {off} of every {stride} do not fit")
+    if total % stride:
+        raise ValueError(f"{what}: {total} rows are not whole strides of {stride}")
+    return n, stride, off
+
+
 def gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloat16, per_row=True, gelu_from=None,
-                    residual=None, gate=None, rows_per_gate=None):
+                    residual=None, gate=None, rows_per_gate=None, a_rows=None, out=None, out_rows=None):
     """:func:`gemm_w8a8` with a DiT block's element-wise steps in the
     epilogue: ``y = dt(gelu_tanh(y))`` for output columns ``>= gelu_from``,
     then ``y = dt(residual + dt(gate[g] * y))`` (``dt(residual + y)`` without
     ``gate``), gate row ``g = row // rows_per_gate``.  ``residual`` [M, N],
-    ``gate`` [N] or [G, N], both cast to ``out_dtype`` (bf16 / f16)."""
+    ``gate`` [N] or [G, N], both cast to ``out_dtype`` (bf16 / f16).
+
+    Segmented rows (CTA-pair kernel, M and N >= 256): ``a_rows=(n, stride,
+    off)`` takes the linear's logical rows from ``a_q`` / ``a_scale`` as the
+    n rows at offset ``off`` of every ``stride`` rows (M = a_q rows //
+    stride * n; n a multiple of 128); ``out_rows=(n, stride, off)`` writes
+    them into ``out`` ([R, N] contiguous, R a multiple of stride) the same
+    way (n a multiple of 32), and ``out`` is returned.  A Flux double
+    block's text and image streams use this to write q/k/v into the joint
+    sequence and to read their projections' rows from the joint attention
+    output without torch.cat or slice copies."""
     if out_dtype not in (torch.bfloat16, torch.float16):
         raise TypeError(f"the fused epilogue writes bfloat16 or float16, got {out_dtype}")
     _check_gemm(a_q, w_q)
     a_q, w_q = _pad_k(_aligned(a_q), _aligned(w_q), 16)
-    M, K = a_q.shape
+    R, K = a_q.shape
     Nn = w_q.shape[0]
-    out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
+    aseg = oseg = (0, 0, 0)
+    M = R
+    if a_rows is not None:
+        aseg = _segments(a_rows, R, "a_rows")
+        M = R // aseg[1] * aseg[0]
+    if out_rows is not None:
+        if out is None:
+            raise ValueError("out_rows needs out")
+        if out.dtype != out_dtype or out.dim() != 2 or out.shape[1] != Nn or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [R, {Nn}] {out_dtype} tensor")
+        oseg = _segments(out_rows, out.shape[0], "out_rows")
+        if M % oseg[0] or M // oseg[0] != out.shape[0] // oseg[1]:
+            raise ValueError(f"{M} rows do not fill the {out.shape[0] // oseg[1]} output segments of {oseg[0]}")
+    elif out is not None:
+        if tuple(out.shape) != (M, Nn) or out.dtype != out_dtype or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [{M}, {Nn}] {out_dtype} tensor")
+    else:
+        out = torch.empty((M, Nn), dtype=out_dtype, device=a_q.device)
     if M == 0 or Nn == 0:
         return out
     a_scale = a_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
+    if a_scale.numel() != R:
+        raise ValueError(f"a_scale must have {R} entries, got {a_scale.numel()}")
     w_scale = w_scale.reshape(-1).to(device=a_q.device, dtype=torch.float32).contiguous()
     if per_row and w_scale.numel() != Nn:
         raise ValueError(f"per-row weight scale must have {Nn} entries, got {w_scale.numel()}")
@@ -429,6 +467,12 @@ def gemm_w8a8_fused(a_q, a_scale, w_q, w_scale, bias=None, out_dtype=torch.bfloa
         if rpg <= 0 or -(-M // rpg) > G:  # every row's gate row must exist
             raise ValueError(f"rows_per_gate={rpg} needs {-(-M // max(rpg, 1))} gate rows, got {G}")
     st = _stream(a_q)
+    if aseg[0] or oseg[0]:
+        N.call("qlin_gemm_w8a8_fused_segments", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(),
+               w_scale.data_ptr(), N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(),
+               dtype_code(out_dtype), M, Nn, K, gelu_col0, _ptr(residual), ld_res, _ptr(gate), gate_ld, rpg,
+               *aseg, *oseg, st)
+        return out
     N.call("qlin_gemm_w8a8_fused", a_q.data_ptr(), a_scale.data_ptr(), w_q.data_ptr(), w_scale.data_ptr(),
            N.WSCALE_ROW if per_row else N.WSCALE_TENSOR, _ptr(bias), out.data_ptr(), dtype_code(out_dtype),
            M, Nn, K, gelu_col0, _ptr(residual), ld_res, _ptr(gate), gate_ld, rpg, st)

@@ -296,6 +296,28 @@ QLIN_API int qlin_gemm_w8a8_fused(const int8_t* a, const float* a_scale, const i
                                   const void* residual, int64_t ld_res, const void* gate, int64_t gate_ld,
                                   int64_t rows_per_gate, void* stream);
 
+/* qlin_gemm_w8a8_fused (GELU / gated residual steps optional: gelu_col0 >= N
+ * and residual == NULL give the plain epilogue) with segmented rows: logical
+ * row r of a and a_scale is row (r / a_seg_rows) * a_seg_stride + a_seg_off
+ * of those arrays, and logical output row r is row (r / out_seg_rows) *
+ * out_seg_stride + out_seg_off of out ([.., N] row-major); a zero row count
+ * leaves that side contiguous.  Residual and gate rows stay logical.
+ * a_seg_rows a multiple of 128, out_seg_rows of 32, each dividing M; every
+ * segment inside its stride (offset + rows <= stride); M and N >= 256
+ * (CTA-pair kernel).  No counterpart in the reference, whose linears take
+ * contiguous rows: this lets the two streams of a Flux-style double block
+ * write their q/k/v rows straight into the joint [text | image] sequence of
+ * each sample, and read their output projections' rows from the joint
+ * attention output, where a model otherwise runs torch.cat and slice
+ * copies. */
+QLIN_API int qlin_gemm_w8a8_fused_segments(const int8_t* a, const float* a_scale, const int8_t* w,
+                                           const float* w_scale, int wscale_mode, const void* bias, void* out,
+                                           int out_dtype, int64_t M, int64_t N, int64_t K, int64_t gelu_col0,
+                                           const void* residual, int64_t ld_res, const void* gate, int64_t gate_ld,
+                                           int64_t rows_per_gate, int64_t a_seg_rows, int64_t a_seg_stride,
+                                           int64_t a_seg_off, int64_t out_seg_rows, int64_t out_seg_stride,
+                                           int64_t out_seg_off, void* stream);
+
 /* Tensor-parallel W8A8 linear fused with its all-gather: this rank's column
  * shard, out[:, col_off : col_off + N_shard] = the qlin_gemm_w8a8 result for
  * (a, a_scale, w_shard, w_scale_shard, bias_shard), is stored into each of

@@ -285,18 +285,91 @@ def test_gemm_fused_strided_gate_and_errors(P):
         P.ops.gemm_w8a8_fused(dev(a), dev(xs), dev(w), dev(ws), None, torch.bfloat16, residual=res[:100])
 
 
-def test_dit_blocks_fused_match_unfused(P, monkeypatch):
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("B,Lt,Li,N,K", [(3, 128, 256, 512, 384), (2, 128, 640, 768, 256), (1, 256, 512, 256, 128)])
+def test_gemm_segmented_rows(P, dt, B, Lt, Li, N, K):
+    """Segmented rows (qlin_gemm_w8a8_fused_segments): the text / image
+    streams of a joint [text | image] sequence of B samples.  Reading a
+    stream's rows from the joint A and scales, or writing its output rows
+    into the joint buffer, gives bit for bit the GEMM of the contiguous
+    rows, with and without the gated residual; joint rows outside the
+    written segments are untouched.  Odd sample counts leave a partial last
+    pair tile (rows past M beyond the last segment)."""
+    rng = np.random.default_rng(B * 1000 + Lt + Li)
+    L = Lt + Li
+    a, w, xs, ws, b = _gemm_case(rng, B * L, N, K, dt)
+    A, XS, W, WS, BIAS = dev(a), dev(xs), dev(w), dev(ws), dev(b, dt)
+    tdt = TDT[dt]
+    parts = {"txt": (Lt, 0), "img": (Li, Lt)}
+
+    def rows_of(t, n, off):  # the contiguous rows of one stream
+        return t.view(B, L, *t.shape[1:])[:, off:off + n].reshape(B * n, *t.shape[1:]).contiguous()
+
+    for name, (n, off) in parts.items():
+        want = P.ops.gemm_w8a8(rows_of(A, n, off), rows_of(XS, n, off), W, WS, BIAS, tdt)
+        got = P.ops.gemm_w8a8_fused(A, XS, W, WS, BIAS, tdt, a_rows=(n, L, off))
+        assert torch.equal(got, want), name
+        res = dev(rnd_vec(rng, (B * n, N), dt), dt)
+        gate = dev(rnd_vec(rng, (B, N), dt, 0.5), dt)
+        want_r = P.ops.gemm_w8a8_fused(rows_of(A, n, off), rows_of(XS, n, off), W, WS, BIAS, tdt, residual=res,
+                                       gate=gate, rows_per_gate=n)
+        got_r = P.ops.gemm_w8a8_fused(A, XS, W, WS, BIAS, tdt, a_rows=(n, L, off), residual=res, gate=gate,
+                                      rows_per_gate=n)
+        assert torch.equal(got_r, want_r), name
+    # output segments: each stream's contiguous GEMM written into the joint rows
+    joint = torch.full((B * L, N), 7.0, dtype=tdt, device="cuda")
+    ref = joint.clone().view(B, L, N)
+    for name, (n, off) in parts.items():
+        xa, xsa = rows_of(A, n, off), rows_of(XS, n, off)
+        out = P.ops.gemm_w8a8_fused(xa, xsa, W, WS, BIAS, tdt, out=joint, out_rows=(n, L, off))
+        assert out.data_ptr() == joint.data_ptr()
+        ref[:, off:off + n] = P.ops.gemm_w8a8(xa, xsa, W, WS, BIAS, tdt).view(B, n, N)
+        assert torch.equal(joint, ref.view(B * L, N)), name  # the other stream's rows still hold 7.0 at first
+    # both sides segmented in one call: the joint rows mapped onto themselves
+    joint2 = torch.zeros_like(joint)
+    for n, off in parts.values():
+        P.ops.gemm_w8a8_fused(A, XS, W, WS, BIAS, tdt, a_rows=(n, L, off), out=joint2, out_rows=(n, L, off))
+    assert torch.equal(joint2, P.ops.gemm_w8a8(A, XS, W, WS, BIAS, tdt))
+    assert P.ops.device_error() == 0
+
+
+def test_gemm_segmented_rows_errors(P):
+    rng = np.random.default_rng(5)
+    B, Lt, Li, N, K = 2, 128, 256, 256, 128
+    L = Lt + Li
+    a, w, xs, ws, b = _gemm_case(rng, B * L, N, K, "bf16")
+    A, XS, W, WS = dev(a), dev(xs), dev(w), dev(ws)
+    with pytest.raises(Exception):  # segments of 64 rows: not a multiple of 128
+        P.ops.gemm_w8a8_fused(A, XS, W, WS, None, torch.bfloat16, a_rows=(64, L, 0))
+    with pytest.raises(ValueError):  # the segment does not fit its stride
+        P.ops.gemm_w8a8_fused(A, XS, W, WS, None, torch.bfloat16, a_rows=(256, L, 256))
+    with pytest.raises(ValueError):  # out_rows without out
+        P.ops.gemm_w8a8_fused(A, XS, W, WS, None, torch.bfloat16, out_rows=(Lt, L, 0))
+    with pytest.raises(ValueError):  # M rows do not fill the output segments
+        P.ops.gemm_w8a8_fused(A[:Lt * B], XS[:Lt * B], W, WS, None, torch.bfloat16,
+                              out=torch.empty((3 * L, N), dtype=torch.bfloat16, device="cuda"), out_rows=(Lt, L, 0))
+    with pytest.raises(Exception):  # 16 rows per output segment: not a multiple of 32
+        P.ops.gemm_w8a8_fused(A[:512], XS[:512], W, WS, None, torch.bfloat16,
+                              out=torch.empty((32 * 32, N), dtype=torch.bfloat16, device="cuda"), out_rows=(16, 32, 0))
+    assert P.ops.device_error() == 0
+
+
+# (img, txt) tokens: 96 / 32 take the torch.cat / slice path of the double
+# blocks; 256 / 128 the segmented GEMM rows (128-row segments, 256 text rows)
+@pytest.mark.parametrize("n_img,n_txt", [(96, 32), (256, 128)])
+def test_dit_blocks_fused_match_unfused(P, monkeypatch, n_img, n_txt):
     """The measured DiT step with its neighbours fused (bench.py's
     dit_forward_fused: norm / modulation in the quantiser, GELU / residual in
-    the GEMM epilogue, q/k norm + rotary kernel, concatenated linear2 input)
-    against the same blocks with those steps eager around the plain
-    quantised linear, on a small config: equal up to the norm statistics'
-    order (relative L2 <= 1e-2 after two double and two single blocks)."""
+    the GEMM epilogue, q/k norm + rotary kernel, concatenated linear2 input,
+    segmented rows for the double blocks' joint sequence) against the same
+    blocks with those steps eager around the plain quantised linear, on a
+    small config: equal up to the norm statistics' order (relative L2 <=
+    1e-2 after two double and two single blocks)."""
     import bench
     monkeypatch.setitem(bench.DIT, "hidden", 256)
     monkeypatch.setitem(bench.DIT, "heads", 2)
-    monkeypatch.setitem(bench.DIT, "img", 96)
-    monkeypatch.setitem(bench.DIT, "txt", 32)
+    monkeypatch.setitem(bench.DIT, "img", n_img)
+    monkeypatch.setitem(bench.DIT, "txt", n_txt)
     dev_ = torch.device("cuda", 0)
     rot = (bench.DIT["kind"], bench.DIT["group"])
     params = bench._dit_params(dev_, lambda w: P.ops.quant_weight_int8(w, rot), 2, 2)
