@@ -228,8 +228,8 @@ int launch_strip(const RowQuantParams& p, cudaStream_t stream) {
   if (per_sm < 1) per_sm = 1;
   const int64_t nblocks = ((int64_t)p.M + rows - 1) / rows;
   const int64_t cap = (int64_t)device_sm_count() * per_sm;
-  e = launch_pdl(kern, dim3((unsigned)(nblocks < cap ? nblocks : cap)), dim3(threads), smem, stream, p.x, p.ldx, p.M,
-                 p.K, rows, stages, slot_bytes, p.rot_c, p.one, p.q, p.scale);
+  e = launch_pdl(kern, dim3((unsigned)(nblocks < cap ? nblocks : cap)), dim3(threads), smem, stream, p.x, p.ldx, p.x2,
+                 p.ldx2, p.k1, p.M, p.K, rows, stages, slot_bytes, p.rot_c, p.one, p.q, p.scale);
   if (e != cudaSuccess) return cuda_fail(e, "rowquant strip launch");
   return QLIN_OK;
 }
@@ -440,6 +440,14 @@ int launch_rowquant_cat(int dt, int rot_kind, int rot_group, float rot_c, const 
   if (rc == RC_BAD) return fail(QLIN_ERR_UNSUPPORTED, "unsupported Hadamard kind/size");
   const int64_t nchunks = p.K / 16;
   if (nchunks > 2048) return fail(QLIN_ERR_UNSUPPORTED, "K > 32768 is not supported by the row kernels");
+  // 16-bit rows on the strip kernel (as launch_rowquant routes them), the
+  // two parts landing side by side in its shared-memory row
+  if ((dt == DT_BF16 || dt == DT_F16) && p.K % STRIP == 0 && p.K / STRIP <= 128 && K1 % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(x1) & 15) == 0 && (reinterpret_cast<uintptr_t>(x2) & 15) == 0 &&
+      (ld1 * 2) % 16 == 0 && (ld2 * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(q) & 31) == 0 && !strip_disabled()) {
+    const int rs = dt == DT_BF16 ? strip_by_rot<DT_BF16>(rc, p, stream) : strip_by_rot<DT_F16>(rc, p, stream);
+    if (rs != QLIN_ERR_UNSUPPORTED) return rs;
+  }
   int r = QLIN_ERR_UNSUPPORTED;
   if (dt == DT_BF16) r = x2_by_chunks<DT_BF16>(rc, p, (int)nchunks, stream);
   else if (dt == DT_F16) r = x2_by_chunks<DT_F16>(rc, p, (int)nchunks, stream);

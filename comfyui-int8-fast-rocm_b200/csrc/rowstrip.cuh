@@ -153,8 +153,9 @@ __device__ __forceinline__ void strip_sylvester128_top(float2 (&v)[32], unsigned
   }
 }
 
-// x [M, K] (row stride ldx elements), K a multiple of 128 with K / SW <=
-// 128; q [M, K] int8 (32-byte aligned), scale [M].  rot_c: the dtype-rounded
+// x [M, K] (row stride ldx elements), or with x2 the concatenated rows
+// [x[r, 0:k1] | x2[r, 0:K-k1]] (k1 and K - k1 multiples of 8, row strides ldx
+// and ldx2); K a multiple of 128 with K / SW <= 128; q [M, K] int8 (32-byte aligned), scale [M].  rot_c: the dtype-rounded
 // +-entry of the normalised Hadamard; one: 1.0f at run time (the
 // quantiser's add is an FMA by it, which the assembler cannot contract with
 // the preceding multiply).
@@ -189,8 +190,9 @@ __device__ __forceinline__ void strip_sylvester128_top(float2 (&v)[32], unsigned
 // stores.
 template <int DT, int KIND, int G, int SW = 128>
 __global__ void __launch_bounds__(128, SW == 64 ? 5 : 3)
-    rowquant_strip_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int rows, int stages, int slot_bytes,
-                          float rot_c, float one, int8_t* __restrict__ q, float* __restrict__ scale) {
+    rowquant_strip_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ x2, int64_t ldx2, int k1,
+                          int M, int K, int rows, int stages, int slot_bytes, float rot_c, float one,
+                          int8_t* __restrict__ q, float* __restrict__ scale) {
   static_assert(DT == DT_BF16 || DT == DT_F16, "16-bit activations");
   static_assert(SW == 128 || (SW == 64 && KIND == ROT_SYLVESTER && G == 128), "half strips: Sylvester 128");
   constexpr bool PAIR = KIND == ROT_REGULAR && G == 256;  // a group spans two strips
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(128, SW == 64 ? 5 : 3)
   const int j = tid - r * T;
   const int nblocks = (M + rows - 1) / rows;
   const int row_bytes = K * 2;
-  const bool dense = ldx == (int64_t)K;
+  const bool dense = x2 == nullptr && ldx == (int64_t)K;
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
@@ -229,6 +231,13 @@ __global__ void __launch_bounds__(128, SW == 64 ? 5 : 3)
     uint8_t* dst = dsm + (size_t)s * slot_bytes;
     if (dense) {
       bulk_load(dst, src + f * row_bytes, (uint32_t)(n * row_bytes), &full[s]);
+    } else if (x2 != nullptr) {  // row = [x[r, 0:k1] | x2[r, 0:K-k1]]
+      const uint8_t* src2 = reinterpret_cast<const uint8_t*>(x2);
+      const int b1 = k1 * 2;
+      for (int k = 0; k < n; ++k) {
+        bulk_load(dst + (size_t)k * row_bytes, src + (f + k) * ldx * 2, (uint32_t)b1, &full[s]);
+        bulk_load(dst + (size_t)k * row_bytes + b1, src2 + (f + k) * ldx2 * 2, (uint32_t)(row_bytes - b1), &full[s]);
+      }
     } else {
       for (int k = 0; k < n; ++k) bulk_load(dst + (size_t)k * row_bytes, src + (f + k) * ldx * 2, (uint32_t)row_bytes, &full[s]);
     }

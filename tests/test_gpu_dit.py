@@ -64,6 +64,32 @@ def test_quant_cat_matches_cat(pkg, dt, rot, M, K1, K2, pad1, pad2):
     assert pkg.ops.device_error() == 0
 
 
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_quant_cat_large_regular256(pkg, dt):
+    """A single block's linear2 input at a size that takes the strip kernel
+    (regular 256, >= 2^25 elements): 2200 rows of [attention 3072 | MLP
+    12288] with a padded MLP row pitch; equal to quantising torch.cat of the
+    parts, and to the oracle on 24 sampled rows plus the first and last."""
+    M, K1, K2 = 2200, 3072, 12288
+    g = torch.Generator(device="cuda").manual_seed(9)
+    ta = torch.randn((M, K1), generator=g, device="cuda").to(TDT[dt])
+    tb = (torch.randn((M, K2 + 64), generator=g, device="cuda") * 0.5).to(TDT[dt])
+    tb[:, 77] *= 20
+    ta[5] = 0.0
+    x2 = tb[:, :K2]
+    rot = ("regular", 256)
+    q, s = pkg.ops.quant_act_int8_cat(ta, x2, rot)
+    q_ref, s_ref = pkg.ops.quant_act_int8(torch.cat((ta, x2), -1), rot)
+    assert torch.equal(q, q_ref)
+    np.testing.assert_array_equal(bits(s), bits(s_ref))
+    rows = np.unique(np.concatenate([[0, 5, M - 1], np.random.default_rng(3).integers(0, M, 24)]))
+    xo = torch.cat((ta, x2), -1)[torch.from_numpy(rows).cuda()].float().cpu().numpy()
+    qo, so = O.quantize_int8_axiswise(O.rotate(xo, 256, "regular", dt), dim=-1)
+    np.testing.assert_array_equal(q.cpu().numpy()[rows], qo)
+    np.testing.assert_array_equal(s.cpu().numpy()[rows].view(np.uint32), so.astype(np.float32).view(np.uint32))
+    assert pkg.ops.device_error() == 0
+
+
 def test_quant_cat_rejects_misaligned(pkg):
     a = torch.zeros((4, 40), dtype=torch.bfloat16, device="cuda")
     b = torch.zeros((4, 32), dtype=torch.bfloat16, device="cuda")
