@@ -614,6 +614,26 @@ def _cfg_time(fn, flush):
     return statistics.median(ts)
 
 
+def _cfg_time_b2b(fns, flush, reps=5):
+    """Steady-state time of one call: the calls in ``fns`` (one per distinct
+    operand set, together larger than the L2 cache) back to back between
+    two events, so no single launch carries the event and launch latency;
+    the per-call mean, median over ``reps``."""
+    ts = []
+    for i in range(2 + reps):
+        flush.zero_()
+        torch.cuda._sleep(2_000_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for f in fns:
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            ts.append(e0.elapsed_time(e1) * 1e3 / len(fns))
+    return statistics.median(ts)
+
+
 def run_configs(pkg, dev, int8_peak, which="all"):
     ops = pkg.ops
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -628,7 +648,9 @@ def run_configs(pkg, dev, int8_peak, which="all"):
         return {"M": Mv, "N": Nv, "K": Kv, "gemm_us": round(us_gemm, 1), "gemm_tops": round(tops, 1),
                 "frac": round(tops / int8_peak, 3), "quant_us": round(us_quant, 1)}
 
-    out = {"timing": f"CUDA events per kernel, L2 flushed before each launch, median of {CFG_ITERS}",
+    out = {"timing": f"CUDA events per kernel, L2 flushed before each launch, median of {CFG_ITERS}; "
+                     f"*_b2b: the same GEMM back to back over b2b_sets distinct operand sets (>= 256 MB, "
+                     f"more than twice the L2) between two events, per-launch mean, median of 5",
            "peak_tops": round(int8_peak, 1)}
     rot = ("sylvester", 128)
     sweep = []
@@ -642,7 +664,20 @@ def run_configs(pkg, dev, int8_peak, which="all"):
                 xq, xs = ops.quant_act_int8(xk, rot)
                 tq = _cfg_time(lambda: ops.quant_act_int8(xk, rot), flush)
                 tg = _cfg_time(lambda: ops.gemm_w8a8(xq, xs, wq, ws, b, torch.bfloat16), flush)
-                sweep.append(entry(Mv, Nv, Kv, tg, tq))
+                e = entry(Mv, Nv, Kv, tg, tq)
+                set_bytes = Mv * Kv + Nv * Kv + 2 * Mv * Nv
+                if set_bytes <= 80 << 20:
+                    # small shapes also back to back over enough distinct
+                    # operand sets to exceed the L2 twice (>= 256 MB)
+                    nsets = min(32, -(-(256 << 20) // set_bytes))
+                    sets = [(xq.clone(), wq.clone()) for _ in range(nsets)]
+                    tb = _cfg_time_b2b([lambda a=a, w=w: ops.gemm_w8a8(a, xs, w, ws, b, torch.bfloat16)
+                                        for a, w in sets], flush)
+                    e["gemm_us_b2b"] = round(tb, 1)
+                    e["frac_b2b"] = round(2.0 * Mv * Nv * Kv / (tb * 1e-6) / 1e12 / int8_peak, 3)
+                    e["b2b_sets"] = nsets
+                    del sets
+                sweep.append(e)
                 del wq, ws, b, xq, xs
             del xk
         del x
@@ -979,6 +1014,10 @@ def _configs_summary(cfgs):
     if sweep:
         out["convrot_w8a8_min_frac"] = cfgs.get("convrot_w8a8_min_frac")
         out["convrot_w8a8_shapes_at_0.7"] = f"{sum(r['frac'] >= 0.7 for r in sweep)}/{len(sweep)}"
+        b2b = [r for r in sweep if "frac_b2b" in r]
+        if b2b:
+            out["convrot_w8a8_b2b"] = [{k: r[k] for k in ("M", "N", "K", "gemm_us", "gemm_us_b2b", "frac_b2b")}
+                                       for r in b2b]
     for key in ("w4a8_g128", "w4a4_g128_sylvester128", "w4a4_row_regular256", "w8a8_plain_c0"):
         v = cfgs.get(key)
         if isinstance(v, dict):
