@@ -751,3 +751,55 @@ def test_quant_regular256_large_rows(P, M, K, dt):
     np.testing.assert_array_equal(q.cpu().numpy()[rows], qo)
     np.testing.assert_array_equal(s.cpu().numpy().reshape(-1)[rows], np.asarray(so, np.float32).reshape(-1))
     assert P.ops.device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# programmatic dependent launch: consumers read their producers' fresh data
+# ---------------------------------------------------------------------------
+
+
+def test_pdl_chain_reads_fresh_inputs(P):
+    """The quantiser and the CTA-pair GEMM are launched with programmatic
+    dependent launch.  A chain [copy new rows in] -> quantise -> GEMM, run 24
+    times without synchronising, with four input batches in turn, must give
+    each batch's eager result bit for bit -- a consumer that read its
+    operands before its producer finished would see the previous batch --
+    both enqueued directly and replayed from a CUDA graph."""
+    torch.manual_seed(11)
+    M, N, K = 2048, 3072, 3072
+    rot = ("sylvester", 128)
+    xs = [(torch.randn((M, K), device="cuda") * (1 + i)).to(torch.bfloat16) for i in range(4)]
+    wq, ws = P.ops.quant_weight_int8((torch.randn((N, K), device="cuda") * 0.02).to(torch.bfloat16), rot)
+    b = (torch.randn(N, device="cuda") * 0.01).to(torch.bfloat16)
+
+    def linear(x):
+        q, s = P.ops.quant_act_int8(x, rot)
+        return P.ops.gemm_w8a8(q, s, wq, ws, b, torch.bfloat16)
+
+    want = [linear(x).clone() for x in xs]
+    torch.cuda.synchronize()
+    xbuf = torch.empty_like(xs[0])
+    outs = []
+    for i in range(24):
+        xbuf.copy_(xs[i % 4])
+        outs.append(linear(xbuf))
+    torch.cuda.synchronize()
+    for i, y in enumerate(outs):
+        assert torch.equal(y, want[i % 4]), i
+
+    # the same chain captured once and replayed with new rows each time
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            linear(xbuf)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        yg = linear(xbuf)
+    for i in range(12):
+        xbuf.copy_(xs[i % 4])
+        g.replay()
+        assert torch.equal(yg, want[i % 4]), i
+    del g
+    assert P.ops.device_error() == 0
