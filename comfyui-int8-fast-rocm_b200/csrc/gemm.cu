@@ -68,6 +68,16 @@ int make_tmap3(CUtensorMap* m, const void* base, uint64_t inner, uint64_t seg_ro
   return QLIN_OK;
 }
 
+// QLIN_NO_NARROW_TAIL=1 keeps every tile of the CTA-pair kernel 256 columns
+// wide (comparison runs).
+bool narrow_tail_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("QLIN_NO_NARROW_TAIL");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
 template <int BN, int EPI, int OUT_DT, bool B_INT4>
 int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, B_INT4>;
@@ -124,9 +134,21 @@ int launch_pair_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
     attr_devices.fetch_or(bit);
   }
-  const int num_units = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN) * p.splits;
+  const int num_tiles = ((p.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((p.N + Cfg::BN - 1) / Cfg::BN);
+  // Narrow last wave (plain 16-bit epilogue through TMA stores, one
+  // destination, no split K): when the tiles leave a last wave that fills at
+  // most half of the CTA pairs, that wave's tiles run as two 128-column
+  // units each.  QLIN_NO_NARROW_TAIL=1 keeps every tile full width.
+  GemmParams pn = p;
+  const int all_clusters = p.num_sms / 2;
+  const int rem = all_clusters > 0 ? num_tiles % all_clusters : 0;
+  if (!SPLIT && !B_INT4 && !(EPI & EPI_POST) && EPI != EPI_I32 && use_tma_store && num_tiles > all_clusters &&
+      rem > 0 && 2 * rem <= all_clusters && !narrow_tail_disabled())
+    pn.narrow_first = num_tiles - rem;
+  const int num_units = SPLIT ? num_tiles * p.splits
+                              : (pn.narrow_first > 0 ? pn.narrow_first + 2 * (num_tiles - pn.narrow_first) : num_tiles);
   const int clusters = num_units < p.num_sms / 2 ? num_units : p.num_sms / 2;
-  e = launch_pdl(kern, dim3(2 * clusters), dim3(Cfg::NUM_THREADS), Cfg::SMEM_BYTES, stream, ta, tb, tc, p,
+  e = launch_pdl(kern, dim3(2 * clusters), dim3(Cfg::NUM_THREADS), Cfg::SMEM_BYTES, stream, ta, tb, tc, pn,
                  use_tma_store);
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return QLIN_OK;

@@ -129,6 +129,12 @@ struct GemmParams {
   // tile over the whole K range (the scratch pointers are unused).
   int splits;
   int kb_split;
+  // Narrow last wave (CTA-pair kernel, plain epilogues): tiles [0,
+  // narrow_first) run as one 256-column unit each; every later tile runs as
+  // two 128-column units (M=256, N=128 MMAs), so a last wave that would
+  // occupy at most half of the CTA pairs ends in about half a tile's time.
+  // 0: every tile full width.
+  int narrow_first;
   uint32_t* sk_count;  // [tiles][2] arrivals per tile half: zero on entry, left zero
   uint32_t* sk_ready;  // [splits - 1][tiles][2] partial slot written: zero on entry, left zero
   int32_t* sk_part;    // [splits - 1][tiles][2][128 rows][256 columns] int32 partials
@@ -222,6 +228,27 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   mb = first_m + in_g % gsz;
   nb = in_g / gsz;
 }
+
+// Units of a launch without split K: full tiles, then (narrow_first > 0)
+// the remaining tiles as two 128-column units each.
+__device__ __forceinline__ int full_or_narrow_units(const GemmParams& p, int num_tiles) {
+  return p.narrow_first > 0 ? p.narrow_first + 2 * (num_tiles - p.narrow_first) : num_tiles;
+}
+// Unit u's row block, first column and width (columns) for BN-wide tiles.
+template <int BN>
+__device__ __forceinline__ int unit_geometry(const GemmParams& p, int u, int num_m, int num_n, int& mb, int& n0) {
+  int nb;
+  if (p.narrow_first == 0 || u < p.narrow_first) {
+    tile_coords(u, num_m, num_n, mb, nb);
+    n0 = nb * BN;
+    return BN;
+  }
+  const int j = u - p.narrow_first;
+  tile_coords(p.narrow_first + (j >> 1), num_m, num_n, mb, nb);
+  n0 = nb * BN + (j & 1) * (BN / 2);
+  return BN / 2;
+}
+
 
 template <int DT>
 __device__ __forceinline__ void store_out_chunk(typename Elem<DT>::T* dst, const float (&y)[32], bool vec, int ncols) {
@@ -984,7 +1011,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
   uint4 res[4] = {};
   // EPI_POST gate of a tile: staged when the CTA's rows of the tile share one
   // gate row (warp-uniform), else read per row in the epilogue
-  auto load_gate = [&](int mb, int nbk, float& g, int& ok) {
+  auto load_gate = [&](int mb, int n0, float& g, int& ok) {
     g = 0.0f;
     ok = 0;
     if constexpr (POST) {
@@ -994,7 +1021,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       const int r_last = min(r_first + GEMM_BM - 1, p.M - 1);
       if ((int64_t)r_first / p.rows_per_gate != (int64_t)r_last / p.rows_per_gate) return;
       ok = 1;
-      const int col = nbk * BN + e;
+      const int col = n0 + e;
       if (e < BN && col < p.N) {
         const uint16_t h =
             reinterpret_cast<const uint16_t*>(p.gate)[((int64_t)r_first / p.rows_per_gate) * p.gate_ld + col];
@@ -1004,11 +1031,11 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
   };
   // EPI_POST residual rows of a tile (this lane's row, the warp's columns)
   // into L2 a tile ahead of their use
-  auto prefetch_res = [&](int mb, int nbk) {
+  auto prefetch_res = [&](int mb, int n0) {
     if constexpr (TMA16 && POST) {
       if (tmC == nullptr || p.residual == nullptr) return;
       const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
-      const int col0 = nbk * BN + half * CPW * 32;
+      const int col0 = n0 + half * CPW * 32;
       if (row >= p.M || col0 >= p.N) return;
       const uint32_t bytes = (uint32_t)(min(CPW * 32, p.N - col0) * 2) & ~15u;
       if (bytes) bulk_prefetch_l2(reinterpret_cast<const uint16_t*>(p.residual) + (int64_t)row * p.ld_res + col0, bytes);
@@ -1016,42 +1043,57 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
   };
   // split K (pair kernel): work units cycle over the tiles once per split
   static_assert(!SPLIT || (PAIR && !POST), "split K: CTA-pair kernel, plain epilogues");
-  const int num_units = num_tiles * (SPLIT ? p.splits : 1);
+  // unit u: its tile, row block, first column and width (split K: whole
+  // tiles, u cycling over them once per split; else see unit_geometry)
+  const int num_units = SPLIT ? num_tiles * p.splits : full_or_narrow_units(p, num_tiles);
+  auto geometry = [&](int u, int& mb, int& n0) {
+    if constexpr (SPLIT) {
+      int nbt;
+      tile_coords(u % num_tiles, num_m, num_n, mb, nbt);
+      n0 = nbt * BN;
+      return BN;
+    } else {
+      return unit_geometry<BN>(p, u, num_m, num_n, mb, n0);
+    }
+  };
   if (first_tile < num_units) {
-    int mb, nb_;
-    tile_coords(first_tile % num_tiles, num_m, num_n, mb, nb_);
-    prefetch_res(mb, nb_);
-    epi_load_params<BN, EPI, OUT_DT>(p, nb_ * BN, e, nws, nb);
+    int mb, n0_;
+    geometry(first_tile, mb, n0_);
+    prefetch_res(mb, n0_);
+    epi_load_params<BN, EPI, OUT_DT>(p, n0_, e, nws, nb);
     const int row = mb * ROWS_PER_TILE + row_off + quarter * 32 + lane;
     if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + a_mem_row(p, row)) : 0.0f;
-    load_gate(mb, nb_, ngate, ngok);
+    load_gate(mb, n0_, ngate, ngok);
     if (e < BN) { es->ws[0][e] = nws; es->bias[0][e] = nb; es->gate[0][e] = ngate; }
     if (e == 0) es->gate_ok[0] = ngok;
     if constexpr (TMA16 && POST) {
-      if (tmC != nullptr && p.residual != nullptr) load_res32<OUT_DT>(p, row, nb_ * BN + half * CPW * 32, res);
+      if (tmC != nullptr && p.residual != nullptr) load_res32<OUT_DT>(p, row, n0_ + half * CPW * 32, res);
     }
   }
   for (int u = first_tile; u < num_units; u += tile_stride) {
-    const int tile = u % num_tiles;
-    int mb, nbk;
-    tile_coords(tile, num_m, num_n, mb, nbk);
+    const int tile = u % num_tiles;  // split K only
+    int mb, n0;
+    const int width = geometry(u, mb, n0);
+    // a narrow unit's columns are the first half: the second-half warps
+    // store nothing (they still take part in every barrier and arrival)
+    const bool idle_half = half * (BN / 2) >= width;
     const float xs = nxs;
     mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag);
     epi_bar();
     if (*abort_flag) break;
     tc_fence_after();
-    const int next = u + tile_stride < num_units ? (u + tile_stride) % num_tiles : num_tiles;
+    const bool has_next = u + tile_stride < num_units;
     int nrow = -1, ncol0 = 0;
-    if (next < num_tiles) {
-      int mb2, nb2;
-      tile_coords(next, num_m, num_n, mb2, nb2);
-      epi_load_params<BN, EPI, OUT_DT>(p, nb2 * BN, e, nws, nb);
+    if (has_next) {
+      int mb2, n02;
+      geometry(u + tile_stride, mb2, n02);
+      epi_load_params<BN, EPI, OUT_DT>(p, n02, e, nws, nb);
       const int row = mb2 * ROWS_PER_TILE + row_off + quarter * 32 + lane;
       if constexpr (EPI != EPI_I32) nxs = row < p.M ? __ldg(p.a_scale + a_mem_row(p, row)) : 0.0f;
-      load_gate(mb2, nb2, ngate, ngok);
-      prefetch_res(mb2, nb2);
+      load_gate(mb2, n02, ngate, ngok);
+      prefetch_res(mb2, n02);
       nrow = row;
-      ncol0 = nb2 * BN + half * CPW * 32;
+      ncol0 = n02 + half * CPW * 32;
     }
     bool done = false;
     if constexpr (SPLIT) {
@@ -1059,9 +1101,10 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       done = !splitk_fixup<BN>(p, es, abort_flag, tmem_base + acc * BN, tile, num_tiles, row_off / GEMM_BM, warp,
                                  lane);
     }
+    if (idle_half) done = true;  // narrow unit (plain epilogues only: no residual pipeline to keep)
     if constexpr (TMA16) {
       if (tmC != nullptr && !done) {
-        epilogue_tile_tma<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter,
+        epilogue_tile_tma<BN, EPI, OUT_DT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, n0, quarter,
                                            half, lane, es->ws[buf], es->bias[buf],
                                            es->gate_ok[buf] ? es->gate[buf] : nullptr, xs, tmC, stage, stc, res,
                                            nrow, ncol0);
@@ -1069,7 +1112,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       }
     }
     if (!done)
-      epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, nbk * BN, quarter,
+      epilogue_tile<BN, EPI, OUT_DT, ISHIFT>(p, tmem_base + acc * BN, mb * ROWS_PER_TILE + row_off, n0, quarter,
                                              half, lane, es->ws[buf], es->bias[buf], xs, tmC, stage);
     tc_fence_before();
     __syncwarp();
@@ -1081,8 +1124,8 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, EpiSmem<BN>* 
       }
     }
     buf ^= 1;
-    if (next < num_tiles && e < BN) { es->ws[buf][e] = nws; es->bias[buf][e] = nb; es->gate[buf][e] = ngate; }
-    if (next < num_tiles && e == 0) es->gate_ok[buf] = ngok;
+    if (has_next && e < BN) { es->ws[buf][e] = nws; es->bias[buf][e] = nb; es->gate[buf][e] = ngate; }
+    if (has_next && e == 0) es->gate_ok[buf] = ngok;
     acc ^= 1;
     if (acc == 0) acc_phase ^= 1;
   }
@@ -1370,7 +1413,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + GEMM_BK - 1) / GEMM_BK;
-  const int num_units = SPLIT ? num_tiles * p.splits : num_tiles;  // split K: see GemmParams
+  // split K / narrow last wave: see GemmParams
+  const int num_units = SPLIT ? num_tiles * p.splits : full_or_narrow_units(p, num_tiles);
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
 
@@ -1390,13 +1434,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
       ArmedLoads armed;  // both CTAs' loads complete on the leader's barriers
       bool ok = true;
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        const int tile = u % num_tiles;
         const int kb0 = SPLIT ? (u / num_tiles) * p.kb_split : 0;
         const int kb1 = SPLIT ? min(kb0 + p.kb_split, num_kb) : num_kb;
-        int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        int mb, n0, width = BN;
+        if constexpr (SPLIT) {
+          int nb;
+          tile_coords(u % num_tiles, num_m, num_n, mb, nb);
+          n0 = nb * BN;
+        } else {
+          width = unit_geometry<BN>(p, u, num_m, num_n, mb, n0);
+        }
         const int arow = mb * 2 * GEMM_BM + (int)rank * GEMM_BM;
-        const int brow = nb * BN + (int)rank * Cfg::BNH;
+        // each CTA holds half of the unit's weight rows (a narrow unit's MMA
+        // reads the first 64 of the 128 loaded)
+        const int brow = n0 + (int)rank * (width / 2);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           if (!(kb == p.stall_kb && u == cluster_id)) {
@@ -1424,7 +1475,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_i8(2 * GEMM_BM, BN);
+      constexpr uint32_t idesc_full = umma_idesc_i8(2 * GEMM_BM, BN);
+      constexpr uint32_t idesc_narrow = umma_idesc_i8(2 * GEMM_BM, BN / 2);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -1433,6 +1485,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<EPI, OUT_DT,
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         const int kb0 = SPLIT ? (u / num_tiles) * p.kb_split : 0;
         const int kb1 = SPLIT ? min(kb0 + p.kb_split, num_kb) : num_kb;
+        const uint32_t idesc = (!SPLIT && p.narrow_first > 0 && u >= p.narrow_first) ? idesc_narrow : idesc_full;
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;

@@ -637,6 +637,27 @@ def test_w8a8_linear_bench_shapes_rows(P, M, N, K, rot, seed):
     np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
 
 
+# A last wave of at most half the CTA pairs runs as 128-column units: 768
+# tiles = 10 waves of 74 + 28 (4096 x 12288, the headline grid; and 4000 x
+# 12160, whose last row block and last column tile are partial, so one
+# narrow unit lies wholly past N), full output rows against the oracle,
+# including the last row.
+@pytest.mark.parametrize("M,N,K", [(4096, 12288, 1024), (4000, 12160, 1024)])
+def test_w8a8_narrow_last_wave_rows(P, M, N, K):
+    rng = np.random.default_rng(M + N)
+    a = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    sa = (rng.random(M, dtype=np.float32) * 0.02 + 1e-3).astype(np.float32)
+    sw = (rng.random(N, dtype=np.float32) * 0.002 + 1e-4).astype(np.float32)
+    b = O.rnd("bf16", rng.standard_normal(N).astype(np.float32) * 0.5)
+    y = P.ops.gemm_w8a8(dev(a), torch.from_numpy(sa).cuda(), dev(w), torch.from_numpy(sw).cuda(), dev(b, "bf16"),
+                        torch.bfloat16)
+    assert P.ops.device_error() == 0
+    rows = np.unique(np.concatenate([_rows_sample(M, seed=5), [M - 1, M // 2, 2048, 3071]]))
+    yo = O.w8a8_epilogue_per_row(O.int_mm(a[rows], w), sa[rows], sw, b, "bf16")
+    np.testing.assert_array_equal(tbits(y)[rows], bits("bf16", yo))
+
+
 @pytest.mark.parametrize("name,K,g,kind", [("syl128_k3072", 3072, 128, "sylvester"),
                                            ("reg256_k3072", 3072, 256, "regular"),
                                            ("syl128_k12288", 12288, 128, "sylvester")])
